@@ -1,0 +1,140 @@
+/* spb200.h -- C ABI of the B200-native byte-exact OK_Q4B forward (libspb200.so).
+ *
+ * Plain pointers and sizes only. This is the device-side library the reference's
+ * L1 backend hooks bind to (the binding itself is libspb200_l1.so, declared in
+ * spb200_l1.h). Every entry point returns 0 or a negative status whose values are
+ * the reference's sp_status codes (sp_status.h:19-56) where one exists; detail goes
+ * to the thread-local spb_last_error().
+ *
+ * Exactness: every result is byte-identical to the exact-integer CPU restatement
+ * of the forward (the checker under oracle/), because every reduction is an integer
+ * sum and every rounding is a single IEEE operation; sharding or reordering the
+ * work cannot change a byte. Values outside the contract's exact range are reported
+ * as SPB_ERANGE instead of being silently wrapped.
+ */
+#ifndef SPB200_H
+#define SPB200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+    SPB_OK = 0,
+    SPB_ENOMEM = -1,          /* SP_ENOMEM        (host allocation)                  */
+    SPB_EBADARG = -3,         /* SP_EBADARG                                          */
+    SPB_EBADSTATE = -4,       /* SP_EBADSTATE                                        */
+    SPB_EUNSUPPORTED = -5,    /* SP_EUNSUPPORTED  (shape outside the kernels' set)   */
+    SPB_ECONTEXT_FULL = -33,  /* SP_ECONTEXT_FULL                                    */
+    SPB_ECUDA = -40,          /* SP_ECUDA         (any cudaError_t; detail in text)  */
+    SPB_EOOM = -43,           /* SP_EBACKEND_OOM  (device allocation)                */
+    SPB_ERANGE = -50          /* a value left the exact-arithmetic range             */
+};
+
+/* One OK_Q4B matrix in host memory: the arena layout v2 of frobenius_lift.h:160-173
+ * restricted to all-Q4B rows: codes [rows][ceil(cols/2)] (low nibble = even column,
+ * 4-bit two's complement), bscale [rows][ceil(cols/32)] f16. */
+typedef struct {
+    const uint8_t  *codes;
+    const uint16_t *bscale;
+    int32_t rows, cols;
+} spb_q4b;
+
+/* Per-layer tensors; the fields mirror qwen3_layer (model.h:97-113). Norm pointers
+ * are f32; post_* are the Gemma3 sandwich norms (NULL for Qwen3). */
+typedef struct {
+    const float *attn_norm, *q_norm, *k_norm, *post_attn_norm, *ffn_norm, *post_ffw_norm;
+    spb_q4b wq, wk, wv, wo, wg, wu, wd;
+} spb_layer_desc;
+
+enum { SPB_ARCH_QWEN3 = 0, SPB_ARCH_GEMMA3 = 1 };   /* sp_arch_t values (model.h:24) */
+
+/* Model geometry; mirrors the qwen3_config fields the forward reads (model.h:28-43). */
+typedef struct {
+    int32_t arch;
+    int32_t n_layers, n_embd, n_ff, n_head, n_head_kv, head_dim, n_vocab;
+    int32_t sliding_window;   /* Gemma3 local layers; <= 0 = none                 */
+    float   rope_base;        /* global layers (Gemma3) / every layer (Qwen3)     */
+    float   rope_base_local;  /* Gemma3 local layers (10000, sp_session.c:397)    */
+    int32_t swa_period;       /* Gemma3: layer L global iff L % period == period-1 */
+    int32_t has_qk_norm;
+} spb_config;
+
+typedef struct {
+    spb_config            cfg;
+    const spb_layer_desc *layers;       /* [n_layers] */
+    spb_q4b               token_embd;   /* [n_vocab][n_embd] */
+    spb_q4b               output;       /* LM head; == token_embd when tied */
+    const float          *output_norm;  /* [n_embd] */
+} spb_model_desc;
+
+typedef struct spb_model spb_model;       /* weights resident in one GPU's HBM     */
+typedef struct spb_session spb_session;   /* one resident exact KV cache + state   */
+
+const char *spb_last_error(void);
+int         spb_device_count(void);
+
+/* ---- model ------------------------------------------------------------------
+ * Upload (replaces reading the arena per call, sp_model_bridge.c:114-148 +
+ * forward_dispatch.c:100-106): codes/scales/norms copied once into HBM; Q|K|V rows
+ * stored contiguously so one launch streams all three. Shapes: n_embd, n_head*head_dim
+ * and n_ff multiples of 32; head_dim in {64,128,256}; n_head/n_head_kv <= 8. */
+int     spb_model_upload(const spb_model_desc *desc, int device, spb_model **out);
+/* Same geometry filled on the device by the counter-based generator of the test
+ * fixtures (seeded; identical bytes to the host generator). */
+int     spb_model_synthetic(const spb_config *cfg, uint64_t seed, int device, spb_model **out);
+void    spb_model_free(spb_model *m);
+int64_t spb_model_weight_bytes(const spb_model *m);   /* OK_Q4B bytes streamed per token */
+
+/* ---- resident KV session (the section-6b verbs, sp_l1.h:386-410) ------------ */
+int  spb_session_open(spb_model *m, int pmax, spb_session **out);
+/* ingest n_tok tokens at the live position; logits [n_tok][n_vocab] (host) or NULL */
+int  spb_session_prefill(spb_session *s, const int32_t *tokens, int n_tok, float *logits);
+/* one token; writes the next position's full-vocab logits (host buffer) */
+int  spb_session_decode_step(spb_session *s, int32_t token, float *logits);
+/* like decode_step, and also returns the greedy argmax (first max index) */
+int  spb_session_decode_step_argmax(spb_session *s, int32_t token, float *logits, int32_t *argmax);
+/* n_steps greedy steps entirely on the device (CUDA graph per step, no host sync
+ * between steps): feeds `token`, then each step's argmax; writes the n_steps
+ * argmaxes (host). */
+int  spb_session_decode_greedy(spb_session *s, int32_t token, int n_steps, int32_t *tokens_out);
+int  spb_session_rewind(spb_session *s, int n);          /* O(1): position -= n */
+int  spb_session_position(const spb_session *s);         /* -1 on NULL */
+int  spb_session_clone(const spb_session *s, spb_session **out);   /* deep KV copy */
+void spb_session_close(spb_session *s);
+/* readback of one cached K (which=0) or V (which=1) row: [n_head_kv*head_dim] int32 */
+int  spb_session_kv_read(const spb_session *s, int layer, int pos, int which, int32_t *out);
+/* device stream the session enqueues on (cudaStream_t) */
+void *spb_session_stream(spb_session *s);
+
+/* ---- full forward (the section-6 hook, sp_l1.h:319-321) ----------------------
+ * n_tok tokens from position 0; writes all n_tok x n_vocab logits (host). */
+int  spb_forward(spb_model *m, const int32_t *tokens, int n_tok, float *logits);
+
+/* ---- isolated kernels over device buffers (parity + the dequant-GEMV sweep) --
+ * stream: a cudaStream_t (NULL = legacy default stream). */
+/* y[t][j] = exact OK_Q4B matvec of the f32 rows x[t] (quantized by sp_frob_quant1
+ * over each row's max|x|); n_tok in {1,2,4,8,16}; cols % 32 == 0. Uses a per-device
+ * workspace allocated on first use. */
+int spb_gemv_q4b(const uint8_t *codes, const uint16_t *bscale, int rows, int cols,
+                 const float *x, int n_tok, float *y, void *stream);
+int spb_rmsnorm_exact_dev(const float *x, const float *w, int n, int rows, float *out, void *stream);
+int spb_gelu_exact_dev(const float *x, int n, float *out, void *stream);
+int spb_silu_exact_dev(const float *x, int n, float *out, void *stream);
+/* CORDIC-RoPE of `rows` head vectors of length d at positions pos[r] (device) */
+int spb_rope_cordic_dev(const float *v, int d, int rows, const int32_t *pos, float base,
+                        int32_t *out, void *stream);
+/* error bits raised by the last isolated-kernel call on this thread's device */
+int spb_take_device_errors(void);
+
+/* ---- host-side tables (no device needed) ------------------------------------ */
+int      spb_rope_freq_table(float base, int d, uint64_t *W);      /* [d/2] turns Q64 */
+void     spb_cordic_tables(uint64_t T[30], uint64_t *gain_q62);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SPB200_H */

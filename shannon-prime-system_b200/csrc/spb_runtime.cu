@@ -1,0 +1,794 @@
+// spb_runtime.cu -- host runtime of libspb200.so: model residency in HBM, resident
+// exact KV sessions, the per-token kernel schedule (captured once as a CUDA graph),
+// integer RoPE/CORDIC tables, and the C ABI declared in include/spb200.h.
+//
+// Schedule of one token row (decode; prefill runs the same schedule on chunks of
+// up to 16 rows through the multi-row GEMV):
+//   embed -> per layer { norm(+residual)+quant -> GEMV Q|K|V -> QK-norm+CORDIC-RoPE+KV
+//   store -> cluster attention -> quant -> GEMV O -> norm(+sandwich)+quant -> GEMV
+//   gate|up with the exact GELU/SiLU * up epilogue -> quant -> GEMV down }
+//   -> final norm+quant -> GEMV LM head -> argmax -> position advance.
+// This mirrors kv_step_gemma3 (sp_session.c:380-464) and kv_step (sp_session.c:274-363).
+#include "../../include/spb200.h"
+#include "spb_kernels.cuh"
+
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <vector>
+
+using namespace spb;
+
+// ------------------------------------------------------------------------------ errors
+static thread_local char g_err[512];
+
+static int set_err(int code, const char *fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof g_err, fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+#define CU(call)                                                                              \
+  do {                                                                                        \
+    cudaError_t e_ = (call);                                                                  \
+    if (e_ != cudaSuccess)                                                                    \
+      return set_err(e_ == cudaErrorMemoryAllocation ? SPB_EOOM : SPB_ECUDA, "%s: %s (%s:%d)", \
+                     #call, cudaGetErrorString(e_), __FILE__, __LINE__);                      \
+  } while (0)
+
+extern "C" const char *spb_last_error(void) { return g_err; }
+
+extern "C" int spb_device_count(void) {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess) return 0;
+  return n;
+}
+
+static const char *err_bits_text(uint32_t b) {
+  if (b & ERR_TOKEN) return "token id outside [0, vocab)";
+  if (b & ERR_NORM_RANGE) return "RMSNorm input outside the exact range (|x| < 32768, sum x^2 < 2^31)";
+  if (b & ERR_ACT_RANGE) return "activation outside the exact range (non-finite, or GELU/SiLU |x| >= 2048)";
+  if (b & ERR_ROPE_RANGE) return "q/k outside the exact RoPE range (|x| < 256)";
+  if (b & ERR_V_RANGE) return "v outside the exact range (|v| < 16384)";
+  if (b & ERR_SCORE_RANGE) return "attention score outside the exact range (|z| < 2^17)";
+  return "unknown";
+}
+
+// ------------------------------------------------------------------------------ tables
+// Integer-only tables of the CORDIC-RoPE (builder-defined: turns as Q64, Volder's
+// micro-rotations, pi from Machin's formula with an integer arctangent series).
+typedef unsigned __int128 u128;
+
+static u128 atan_inv_q124(uint32_t m) {   // atan(1/m) * 2^124
+  u128 p = ((u128)1 << 124) / m, m2 = (u128)m * m, sum = 0;
+  bool add = true;
+  for (uint32_t k = 1; p != 0; k += 2) {
+    const u128 t = p / k;
+    sum = add ? sum + t : sum - t;
+    add = !add;
+    p /= m2;
+  }
+  return sum;
+}
+
+static u128 two_pi_q124() { return 2 * (16 * atan_inv_q124(5) - 4 * atan_inv_q124(239)); }
+
+static u128 atan_pow2_q124(int k) {       // atan(2^-k) * 2^124, k >= 1
+  u128 p = (u128)1 << (124 - k), sum = 0;
+  bool add = true;
+  for (uint32_t n = 1; p != 0; n += 2) {
+    const u128 t = p / n;
+    sum = add ? sum + t : sum - t;
+    add = !add;
+    p >>= 2 * k;
+  }
+  return sum;
+}
+
+static u128 ratio_shift(u128 num, u128 den, int shift) {   // round(num * 2^shift / den), num < den
+  u128 r = num, q = 0;
+  for (int i = 0; i < shift; i++) {
+    r <<= 1;
+    q <<= 1;
+    if (r >= den) { r -= den; q |= 1; }
+  }
+  if ((r << 1) >= den) q++;
+  return q;
+}
+
+static u128 isqrt128(u128 v) {
+  u128 res = 0, bit = (u128)1 << 126;
+  while (bit > v) bit >>= 2;
+  while (bit) {
+    if (v >= res + bit) { v -= res + bit; res = (res >> 1) + bit; }
+    else res >>= 1;
+    bit >>= 2;
+  }
+  return res;
+}
+
+extern "C" void spb_cordic_tables(uint64_t T[30], uint64_t *gain_q62) {
+  const u128 P = two_pi_q124();
+  T[0] = 1ull << 61;
+  for (int k = 1; k < 30; k++) T[k] = (uint64_t)ratio_shift(atan_pow2_q124(k), P, 64);
+  u128 g = (u128)1 << 62;
+  for (int k = 0; k < 30; k++) g = (g << 62) / isqrt128(((u128)1 << 124) + ((u128)1 << (124 - 2 * k)));
+  if (gain_q62) *gain_q62 = (uint64_t)g;
+}
+
+extern "C" int spb_rope_freq_table(float base, int d, uint64_t *W) {
+  uint32_t bits;
+  memcpy(&bits, &base, 4);
+  const uint32_t e8 = (bits >> 23) & 0xFFu, mant = bits & 0x7FFFFFu;
+  if ((bits >> 31) || e8 < 127u || e8 == 255u || d <= 0 || (d & 1) || !W)
+    return set_err(SPB_EBADARG, "spb_rope_freq_table: base must be finite and >= 1, d even");
+  u128 y = (u128)(mant | 0x800000u) << 39, L = 0;   // log2(mantissa), Q62, bit by bit
+  for (int j = 1; j <= 62; j++) {
+    y = (y * y) >> 62;
+    if (y >= ((u128)1 << 63)) { y >>= 1; L |= (u128)1 << (62 - j); }
+  }
+  L += (u128)(e8 - 127u) << 62;
+  u128 c[63];                                        // c_j = 2^(-2^-j), Q62
+  c[1] = isqrt128((u128)1 << 123);
+  for (int j = 2; j <= 62; j++) c[j] = isqrt128(c[j - 1] << 62);
+  const u128 P = two_pi_q124();
+  for (int i = 0; i < d / 2; i++) {
+    const u128 t = ((u128)(2 * i) * L) / (u128)d;
+    const u128 n = t >> 62, f = t & (((u128)1 << 62) - 1);
+    u128 r = (u128)1 << 62;
+    for (int j = 1; j <= 62; j++)
+      if ((f >> (62 - j)) & 1) r = (r * c[j]) >> 62;
+    W[i] = n > 126 ? 0 : (uint64_t)ratio_shift(r, P, 126 - (int)n);
+  }
+  return SPB_OK;
+}
+
+// ------------------------------------------------------------------------------ model
+struct DevLayer {
+  DevQ4B qkv, o, g, u, d;
+  const float *attn_norm, *q_norm, *k_norm, *post_attn, *ffn_norm, *post_ffw;
+  bool global;
+  int win;
+};
+
+struct spb_model {
+  int device;
+  spb_config cfg;
+  int E, FF, NH, NKV, HD, QD, KVD, V, NL;
+  bool gemma;
+  uint8_t *wbuf = nullptr;
+  size_t wbytes = 0;
+  std::vector<DevLayer> layers;
+  DevQ4B embd{}, out{};
+  const float *out_norm = nullptr;
+  uint64_t *tabs = nullptr;   // [0,30) CORDIC atan, [32, 32+HD/2) global W, then local W
+  uint64_t gain = 0;
+  float es = 1.0f;
+  int64_t stream_bytes = 0;
+};
+
+static size_t q4b_bytes(int rows, int cols) { return (size_t)rows * (cols / 2) + (size_t)rows * (cols / 32) * 2; }
+
+static int check_cfg(const spb_config &c) {
+  if (c.n_layers <= 0 || c.n_embd <= 0 || c.n_ff <= 0 || c.n_head <= 0 || c.n_head_kv <= 0 || c.n_vocab <= 0)
+    return set_err(SPB_EBADARG, "spb: non-positive model dimension");
+  if (c.arch != SPB_ARCH_QWEN3 && c.arch != SPB_ARCH_GEMMA3) return set_err(SPB_EUNSUPPORTED, "spb: arch %d", c.arch);
+  if (c.head_dim != 64 && c.head_dim != 128 && c.head_dim != 256)
+    return set_err(SPB_EUNSUPPORTED, "spb: head_dim %d not in {64,128,256}", c.head_dim);
+  if (c.n_head % c.n_head_kv || c.n_head / c.n_head_kv > 8)
+    return set_err(SPB_EUNSUPPORTED, "spb: n_head/n_head_kv must be an integer <= 8");
+  if ((c.n_embd & 31) || ((c.n_head * c.head_dim) & 31) || (c.n_ff & 31))
+    return set_err(SPB_EUNSUPPORTED, "spb: n_embd, n_head*head_dim and n_ff must be multiples of 32");
+  if (c.n_embd > 16384) return set_err(SPB_EUNSUPPORTED, "spb: n_embd > 16384");
+  return SPB_OK;
+}
+
+static int model_alloc(const spb_config &c, int device, spb_model **out) {
+  int rc = check_cfg(c);
+  if (rc) return rc;
+  CU(cudaSetDevice(device));
+  spb_model *m = new spb_model();
+  m->device = device;
+  m->cfg = c;
+  m->E = c.n_embd; m->FF = c.n_ff; m->NH = c.n_head; m->NKV = c.n_head_kv; m->HD = c.head_dim;
+  m->QD = c.n_head * c.head_dim; m->KVD = c.n_head_kv * c.head_dim; m->V = c.n_vocab; m->NL = c.n_layers;
+  m->gemma = c.arch == SPB_ARCH_GEMMA3;
+  m->es = sqrtf((float)m->E);
+  // layout: per layer qkv, o, gate, up, down, then norms; embedding; LM head (if untied)
+  size_t off = 0;
+  auto take = [&](size_t n) { size_t o = off; off = (off + n + 255) & ~(size_t)255; return o; };
+  struct Off { size_t qkv_c, qkv_s, o_c, o_s, g_c, g_s, u_c, u_s, d_c, d_s, norms; };
+  std::vector<Off> lo(m->NL);
+  const int QKV = m->QD + 2 * m->KVD;
+  const int nnorm = 4 * m->E + 2 * m->HD;   // attn, post_attn, ffn, post_ffw, q, k
+  for (int L = 0; L < m->NL; L++) {
+    Off &o = lo[L];
+    o.qkv_c = take((size_t)QKV * m->E / 2); o.qkv_s = take((size_t)QKV * (m->E / 32) * 2);
+    o.o_c = take((size_t)m->E * m->QD / 2); o.o_s = take((size_t)m->E * (m->QD / 32) * 2);
+    o.g_c = take((size_t)m->FF * m->E / 2); o.g_s = take((size_t)m->FF * (m->E / 32) * 2);
+    o.u_c = take((size_t)m->FF * m->E / 2); o.u_s = take((size_t)m->FF * (m->E / 32) * 2);
+    o.d_c = take((size_t)m->E * m->FF / 2); o.d_s = take((size_t)m->E * (m->FF / 32) * 2);
+    o.norms = take((size_t)nnorm * 4);
+  }
+  const size_t emb_c = take((size_t)m->V * m->E / 2), emb_s = take((size_t)m->V * (m->E / 32) * 2);
+  const bool untied = !m->gemma;
+  size_t out_c = 0, out_s = 0;
+  if (untied) { out_c = take((size_t)m->V * m->E / 2); out_s = take((size_t)m->V * (m->E / 32) * 2); }
+  const size_t onorm = take((size_t)m->E * 4);
+  const size_t tabs = take((size_t)(32 + m->HD) * 8);
+  m->wbytes = off;
+  cudaError_t e = cudaMalloc(&m->wbuf, off);
+  if (e != cudaSuccess) {
+    delete m;
+    return set_err(SPB_EOOM, "spb_model: cudaMalloc(%zu): %s", off, cudaGetErrorString(e));
+  }
+  uint8_t *B = m->wbuf;
+  m->layers.resize(m->NL);
+  const int period = c.swa_period > 0 ? c.swa_period : 6;
+  for (int L = 0; L < m->NL; L++) {
+    const Off &o = lo[L];
+    DevLayer &d = m->layers[L];
+    d.qkv = {B + o.qkv_c, (const uint16_t *)(B + o.qkv_s), QKV, m->E};
+    d.o = {B + o.o_c, (const uint16_t *)(B + o.o_s), m->E, m->QD};
+    d.g = {B + o.g_c, (const uint16_t *)(B + o.g_s), m->FF, m->E};
+    d.u = {B + o.u_c, (const uint16_t *)(B + o.u_s), m->FF, m->E};
+    d.d = {B + o.d_c, (const uint16_t *)(B + o.d_s), m->E, m->FF};
+    const float *nb = (const float *)(B + o.norms);
+    d.attn_norm = nb; d.post_attn = nb + m->E; d.ffn_norm = nb + 2 * m->E; d.post_ffw = nb + 3 * m->E;
+    d.q_norm = c.has_qk_norm ? nb + 4 * m->E : nullptr;
+    d.k_norm = c.has_qk_norm ? nb + 4 * m->E + m->HD : nullptr;
+    d.global = !m->gemma || (L % period) == period - 1;
+    d.win = (m->gemma && !d.global && c.sliding_window > 0) ? c.sliding_window : -1;
+  }
+  m->embd = {B + emb_c, (const uint16_t *)(B + emb_s), m->V, m->E};
+  m->out = untied ? DevQ4B{B + out_c, (const uint16_t *)(B + out_s), m->V, m->E} : m->embd;
+  m->out_norm = (const float *)(B + onorm);
+  m->tabs = (uint64_t *)(B + tabs);
+  // tables
+  std::vector<uint64_t> ht(32 + m->HD, 0);
+  spb_cordic_tables(ht.data(), &m->gain);
+  rc = spb_rope_freq_table(c.rope_base, m->HD, ht.data() + 32);
+  if (!rc) rc = spb_rope_freq_table(m->gemma ? c.rope_base_local : c.rope_base, m->HD, ht.data() + 32 + m->HD / 2);
+  if (rc) { cudaFree(m->wbuf); delete m; return rc; }
+  e = cudaMemcpy(m->tabs, ht.data(), ht.size() * 8, cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) { cudaFree(m->wbuf); delete m; return set_err(SPB_ECUDA, "spb_model: tables: %s", cudaGetErrorString(e)); }
+  m->stream_bytes = (int64_t)m->NL * (int64_t)(q4b_bytes(QKV, m->E) + q4b_bytes(m->E, m->QD) +
+                                              2 * q4b_bytes(m->FF, m->E) + q4b_bytes(m->E, m->FF)) +
+                    (int64_t)q4b_bytes(m->V, m->E);
+  *out = m;
+  return SPB_OK;
+}
+
+// |acc| bound of the int64 block accumulation: sum_b |k_b| * 32 * 8 * 127 < 2^63
+static bool q4b_bound_ok(const spb_q4b &w) {
+  const int nblk = (w.cols + 31) / 32;
+  const uint64_t lim = (1ull << 63) / (32u * 8u * 127u);
+  for (int r = 0; r < w.rows; r++) {
+    uint64_t s = 0;
+    const uint16_t *bs = w.bscale + (size_t)r * nblk;
+    for (int b = 0; b < nblk; b++) {
+      const uint32_t h = bs[b], e = (h >> 10) & 31u, mant = h & 1023u;
+      if (e == 31) return false;
+      s += e ? (uint64_t)(mant | 1024u) << (e - 1) : mant;
+      if (s >= lim) return false;
+    }
+  }
+  return true;
+}
+
+static int put_q4b(const spb_q4b &w, int rows, int cols, const DevQ4B &dst, int row0, const char *what) {
+  if (!w.codes || !w.bscale || w.rows != rows || w.cols != cols)
+    return set_err(SPB_EBADARG, "spb_model_upload: %s shape [%d x %d], expected [%d x %d]", what, w.rows, w.cols,
+                   rows, cols);
+  if (!q4b_bound_ok(w))
+    return set_err(SPB_ERANGE, "spb_model_upload: %s block scales exceed the exact int64 accumulation bound", what);
+  CU(cudaMemcpy((void *)(dst.codes + (size_t)row0 * (cols / 2)), w.codes, (size_t)rows * (cols / 2),
+                cudaMemcpyHostToDevice));
+  CU(cudaMemcpy((void *)(dst.scales + (size_t)row0 * (cols / 32)), w.bscale, (size_t)rows * (cols / 32) * 2,
+                cudaMemcpyHostToDevice));
+  return SPB_OK;
+}
+
+static int put_f32(const float *src, const float *dst, int n, const char *what) {
+  if (!src) return set_err(SPB_EBADARG, "spb_model_upload: missing %s", what);
+  CU(cudaMemcpy((void *)dst, src, (size_t)n * 4, cudaMemcpyHostToDevice));
+  return SPB_OK;
+}
+
+extern "C" int spb_model_upload(const spb_model_desc *desc, int device, spb_model **out) {
+  if (!desc || !out || !desc->layers) return set_err(SPB_EBADARG, "spb_model_upload: null arg");
+  *out = nullptr;
+  spb_model *m = nullptr;
+  int rc = model_alloc(desc->cfg, device, &m);
+  if (rc) return rc;
+#define PUT(x)                        \
+  do {                                \
+    rc = (x);                         \
+    if (rc) { spb_model_free(m); return rc; } \
+  } while (0)
+  for (int L = 0; L < m->NL; L++) {
+    const spb_layer_desc &s = desc->layers[L];
+    DevLayer &d = m->layers[L];
+    PUT(put_q4b(s.wq, m->QD, m->E, d.qkv, 0, "attn_q"));
+    PUT(put_q4b(s.wk, m->KVD, m->E, d.qkv, m->QD, "attn_k"));
+    PUT(put_q4b(s.wv, m->KVD, m->E, d.qkv, m->QD + m->KVD, "attn_v"));
+    PUT(put_q4b(s.wo, m->E, m->QD, d.o, 0, "attn_output"));
+    PUT(put_q4b(s.wg, m->FF, m->E, d.g, 0, "ffn_gate"));
+    PUT(put_q4b(s.wu, m->FF, m->E, d.u, 0, "ffn_up"));
+    PUT(put_q4b(s.wd, m->E, m->FF, d.d, 0, "ffn_down"));
+    PUT(put_f32(s.attn_norm, d.attn_norm, m->E, "attn_norm"));
+    PUT(put_f32(s.ffn_norm, d.ffn_norm, m->E, "ffn_norm"));
+    if (m->gemma) {
+      PUT(put_f32(s.post_attn_norm, d.post_attn, m->E, "post_attention_norm"));
+      PUT(put_f32(s.post_ffw_norm, d.post_ffw, m->E, "post_ffw_norm"));
+    }
+    if (desc->cfg.has_qk_norm) {
+      PUT(put_f32(s.q_norm, d.q_norm, m->HD, "attn_q_norm"));
+      PUT(put_f32(s.k_norm, d.k_norm, m->HD, "attn_k_norm"));
+    }
+  }
+  PUT(put_q4b(desc->token_embd, m->V, m->E, m->embd, 0, "token_embd"));
+  if (!m->gemma) PUT(put_q4b(desc->output, m->V, m->E, m->out, 0, "output"));
+  PUT(put_f32(desc->output_norm, m->out_norm, m->E, "output_norm"));
+#undef PUT
+  *out = m;
+  return SPB_OK;
+}
+
+// splitmix64 key of a generator stream (matches spmodel.stream_key)
+static uint64_t splitmix64_h(uint64_t z) {
+  z += 0x9E3779B97F4A7C15ull;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+static uint64_t stream_key(uint64_t seed, uint64_t stream) { return splitmix64_h(seed * 0x10001ull + stream); }
+static int scale_exp_field(int cols) { return (int)std::floor(std::log2(1.0 / (8.0 * std::sqrt((double)cols)))) + 15; }
+
+static int synth_matrix(const DevQ4B &d, int row0, int rows, int cols, int tid, uint64_t seed) {
+  CU(launch_synth_codes((uint8_t *)d.codes + (size_t)row0 * (cols / 2), (size_t)rows * (cols / 2),
+                        stream_key(seed, 2ull * tid), 0));
+  CU(launch_synth_scales((uint16_t *)d.scales + (size_t)row0 * (cols / 32), rows, cols / 32, cols / 32,
+                         scale_exp_field(cols), stream_key(seed, 2ull * tid + 1), 0));
+  return SPB_OK;
+}
+
+extern "C" int spb_model_synthetic(const spb_config *cfg, uint64_t seed, int device, spb_model **out) {
+  if (!cfg || !out) return set_err(SPB_EBADARG, "spb_model_synthetic: null arg");
+  *out = nullptr;
+  spb_model *m = nullptr;
+  int rc = model_alloc(*cfg, device, &m);
+  if (rc) return rc;
+  // stream ids: globals 1..3, layer L field f -> 64 + 64 L + f (spmodel.LAYER_FIELDS order)
+  enum { F_ATTN_NORM, F_Q, F_K, F_V, F_O, F_QN, F_KN, F_POST_ATTN, F_FFN_NORM, F_GATE, F_UP, F_DOWN, F_POST_FFW };
+  auto lid = [](int L, int f) { return 64 + 64 * L + f; };
+  for (int L = 0; L < m->NL && !rc; L++) {
+    DevLayer &d = m->layers[L];
+    rc = synth_matrix(d.qkv, 0, m->QD, m->E, lid(L, F_Q), seed);
+    if (!rc) rc = synth_matrix(d.qkv, m->QD, m->KVD, m->E, lid(L, F_K), seed);
+    if (!rc) rc = synth_matrix(d.qkv, m->QD + m->KVD, m->KVD, m->E, lid(L, F_V), seed);
+    if (!rc) rc = synth_matrix(d.o, 0, m->E, m->QD, lid(L, F_O), seed);
+    if (!rc) rc = synth_matrix(d.g, 0, m->FF, m->E, lid(L, F_GATE), seed);
+    if (!rc) rc = synth_matrix(d.u, 0, m->FF, m->E, lid(L, F_UP), seed);
+    if (!rc) rc = synth_matrix(d.d, 0, m->E, m->FF, lid(L, F_DOWN), seed);
+    struct { const float *p; int n, f; } norms[] = {
+        {d.attn_norm, m->E, F_ATTN_NORM}, {d.ffn_norm, m->E, F_FFN_NORM}, {d.post_attn, m->E, F_POST_ATTN},
+        {d.post_ffw, m->E, F_POST_FFW}, {d.q_norm, m->HD, F_QN}, {d.k_norm, m->HD, F_KN}};
+    for (auto &nz : norms)
+      if (!rc && nz.p) {
+        cudaError_t e = launch_synth_norm((float *)nz.p, nz.n, stream_key(seed, 2ull * lid(L, nz.f)), 0);
+        if (e != cudaSuccess) rc = set_err(SPB_ECUDA, "synth norm: %s", cudaGetErrorString(e));
+      }
+  }
+  if (!rc) rc = synth_matrix(m->embd, 0, m->V, m->E, 1, seed);
+  if (!rc && !m->gemma) rc = synth_matrix(m->out, 0, m->V, m->E, 2, seed);
+  if (!rc) {
+    cudaError_t e = launch_synth_norm((float *)m->out_norm, m->E, stream_key(seed, 2ull * 3), 0);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) rc = set_err(SPB_ECUDA, "synth: %s", cudaGetErrorString(e));
+  }
+  if (rc) { spb_model_free(m); return rc; }
+  *out = m;
+  return SPB_OK;
+}
+
+extern "C" void spb_model_free(spb_model *m) {
+  if (!m) return;
+  cudaSetDevice(m->device);
+  cudaFree(m->wbuf);
+  delete m;
+}
+
+extern "C" int64_t spb_model_weight_bytes(const spb_model *m) { return m ? m->stream_bytes : 0; }
+
+// ------------------------------------------------------------------------------ session
+constexpr int NT_MAX = 16;
+
+struct spb_session {
+  spb_model *m;
+  int pmax;
+  int pos;                        // host mirror of pos_dev
+  cudaStream_t st = nullptr;
+  uint8_t *buf = nullptr;         // one allocation for cache + scratch
+  int32_t *kc, *vc;               // [NL][NKV][pmax][HD]
+  float *x, *qkv, *ao, *ap, *gg, *dn, *logits;
+  int32_t *qi;
+  DevAct act;
+  int32_t *pos_dev, *tok_dev, *argmax_dev, *hist_dev;
+  uint32_t *err_dev;
+  int32_t *h_pinned = nullptr;    // pinned staging: [0..NT_MAX) tokens, [NT_MAX] err, [NT_MAX+1] argmax
+  cudaGraphExec_t step_graph = nullptr;
+};
+
+static size_t kv_layer_elems(const spb_model *m, int pmax) { return (size_t)m->NKV * pmax * m->HD; }
+
+extern "C" int spb_session_open(spb_model *m, int pmax, spb_session **out) {
+  if (!m || !out || pmax <= 0) return set_err(SPB_EBADARG, "spb_session_open: bad arg");
+  *out = nullptr;
+  CU(cudaSetDevice(m->device));
+  spb_session *s = new spb_session();
+  s->m = m;
+  s->pmax = pmax;
+  s->pos = 0;
+  const int E = m->E, QKV = m->QD + 2 * m->KVD, maxK = std::max(std::max(E, m->QD), m->FF);
+  size_t off = 0;
+  auto take = [&](size_t n) { size_t o = off; off = (off + n + 255) & ~(size_t)255; return o; };
+  const size_t kvn = (size_t)m->NL * kv_layer_elems(m, pmax);
+  const size_t o_kc = take(kvn * 4), o_vc = take(kvn * 4);
+  const size_t o_x = take((size_t)NT_MAX * E * 4), o_qkv = take((size_t)NT_MAX * QKV * 4);
+  const size_t o_ao = take((size_t)NT_MAX * m->QD * 4), o_ap = take((size_t)NT_MAX * E * 4);
+  const size_t o_gg = take((size_t)NT_MAX * m->FF * 4), o_dn = take((size_t)NT_MAX * E * 4);
+  const size_t o_lg = take((size_t)NT_MAX * m->V * 4), o_qi = take((size_t)NT_MAX * m->QD * 4);
+  const size_t o_aq = take((size_t)NT_MAX * maxK), o_ab = take((size_t)NT_MAX * (maxK / 32) * 4);
+  const size_t o_as = take(NT_MAX * 4), o_pos = take(4), o_tok = take(NT_MAX * 4), o_am = take(NT_MAX * 4);
+  const size_t o_hist = take((size_t)pmax * 4), o_err = take(4);
+  cudaError_t e = cudaMalloc(&s->buf, off);
+  if (e != cudaSuccess) { delete s; return set_err(SPB_EOOM, "spb_session_open: cudaMalloc(%zu): %s", off, cudaGetErrorString(e)); }
+  uint8_t *B = s->buf;
+  s->kc = (int32_t *)(B + o_kc); s->vc = (int32_t *)(B + o_vc);
+  s->x = (float *)(B + o_x); s->qkv = (float *)(B + o_qkv); s->ao = (float *)(B + o_ao);
+  s->ap = (float *)(B + o_ap); s->gg = (float *)(B + o_gg); s->dn = (float *)(B + o_dn);
+  s->logits = (float *)(B + o_lg); s->qi = (int32_t *)(B + o_qi);
+  s->act = {(int8_t *)(B + o_aq), (int32_t *)(B + o_ab), (float *)(B + o_as)};
+  s->pos_dev = (int32_t *)(B + o_pos); s->tok_dev = (int32_t *)(B + o_tok); s->argmax_dev = (int32_t *)(B + o_am);
+  s->hist_dev = (int32_t *)(B + o_hist); s->err_dev = (uint32_t *)(B + o_err);
+  e = cudaStreamCreateWithFlags(&s->st, cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = cudaMallocHost(&s->h_pinned, (NT_MAX + 4) * 4);
+  if (e == cudaSuccess) e = cudaMemsetAsync(s->buf, 0, off, s->st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s->st);
+  if (e != cudaSuccess) { spb_session_close(s); return set_err(SPB_ECUDA, "spb_session_open: %s", cudaGetErrorString(e)); }
+  *out = s;
+  return SPB_OK;
+}
+
+extern "C" void spb_session_close(spb_session *s) {
+  if (!s) return;
+  cudaSetDevice(s->m->device);
+  if (s->st) cudaStreamSynchronize(s->st);
+  if (s->step_graph) cudaGraphExecDestroy(s->step_graph);
+  if (s->st) cudaStreamDestroy(s->st);
+  cudaFreeHost(s->h_pinned);
+  cudaFree(s->buf);
+  delete s;
+}
+
+extern "C" void *spb_session_stream(spb_session *s) { return s ? (void *)s->st : nullptr; }
+extern "C" int spb_session_position(const spb_session *s) { return s ? s->pos : -1; }
+
+// Enqueue the schedule for nt rows (tokens already in tok_dev, positions at pos_dev).
+static cudaError_t enqueue_rows(spb_session *s, int nt, bool want_logits) {
+  spb_model *m = s->m;
+  cudaStream_t st = s->st;
+  const int E = m->E, QKV = m->QD + 2 * m->KVD;
+  const float ascale = 1.0f / sqrtf((float)m->HD);
+  cudaError_t e;
+#define K(x)                        \
+  do {                              \
+    e = (x);                        \
+    if (e != cudaSuccess) return e; \
+  } while (0)
+  K(launch_embed(m->embd, s->tok_dev, nt, m->es, m->gemma ? 1 : 0, s->x, m->V, s->err_dev, st));
+  const size_t kvl = kv_layer_elems(m, s->pmax);
+  for (int L = 0; L < m->NL; L++) {
+    const DevLayer &d = m->layers[L];
+    if (L == 0) {
+      K(launch_norm(s->x, nullptr, nullptr, d.attn_norm, E, nt, s->act, nullptr, s->err_dev, st));
+    } else {
+      const DevLayer &p = m->layers[L - 1];
+      K(launch_norm(s->x, s->dn, m->gemma ? p.post_ffw : nullptr, d.attn_norm, E, nt, s->act, nullptr, s->err_dev, st));
+    }
+    K(launch_gemv(d.qkv, nullptr, s->act, nt, s->qkv, QKV, EPI_STORE, s->err_dev, st));
+    RopeArgs ra;
+    ra.qkv = s->qkv; ra.qi = s->qi; ra.kc = s->kc + (size_t)L * kvl; ra.vc = s->vc + (size_t)L * kvl;
+    ra.q_norm = d.q_norm; ra.k_norm = d.k_norm;
+    ra.W = m->tabs + 32 + (d.global ? 0 : m->HD / 2);
+    ra.T = m->tabs; ra.gain = m->gain; ra.pos_dev = s->pos_dev;
+    ra.NH = m->NH; ra.NKV = m->NKV; ra.HD = m->HD; ra.P = s->pmax; ra.ntok = nt; ra.err = s->err_dev;
+    K(launch_rope_kv(ra, st));
+    AttnArgs aa;
+    aa.qi = s->qi; aa.kc = ra.kc; aa.vc = ra.vc; aa.ao = s->ao; aa.pos_dev = s->pos_dev;
+    aa.NH = m->NH; aa.NKV = m->NKV; aa.HD = m->HD; aa.P = s->pmax; aa.win = d.win; aa.ntok = nt;
+    aa.ascale = ascale; aa.err = s->err_dev;
+    K(launch_attn(aa, st));
+    K(launch_quant(s->ao, m->QD, m->QD, nt, s->act, s->err_dev, st));
+    K(launch_gemv(d.o, nullptr, s->act, nt, s->ap, E, EPI_STORE, s->err_dev, st));
+    K(launch_norm(s->x, s->ap, m->gemma ? d.post_attn : nullptr, d.ffn_norm, E, nt, s->act, nullptr, s->err_dev, st));
+    K(launch_gemv(d.g, &d.u, s->act, nt, s->gg, m->FF, m->gemma ? EPI_GELU_MUL : EPI_SILU_MUL, s->err_dev, st));
+    K(launch_quant(s->gg, m->FF, m->FF, nt, s->act, s->err_dev, st));
+    K(launch_gemv(d.d, nullptr, s->act, nt, s->dn, E, EPI_STORE, s->err_dev, st));
+  }
+  if (want_logits) {
+    const DevLayer &p = m->layers[m->NL - 1];
+    K(launch_norm(s->x, s->dn, m->gemma ? p.post_ffw : nullptr, m->out_norm, E, nt, s->act, nullptr, s->err_dev, st));
+    K(launch_gemv(m->out, nullptr, s->act, nt, s->logits, m->V, EPI_STORE, s->err_dev, st));
+    K(launch_argmax(s->logits, m->V, nt, s->argmax_dev, st));
+  }
+#undef K
+  return cudaSuccess;
+}
+
+// read and clear the device error word; returns SPB_ERANGE on any raised bit
+static int collect_errors(spb_session *s) {
+  uint32_t *h = reinterpret_cast<uint32_t *>(s->h_pinned + NT_MAX);
+  CU(cudaMemcpyAsync(h, s->err_dev, 4, cudaMemcpyDeviceToHost, s->st));
+  CU(cudaMemsetAsync(s->err_dev, 0, 4, s->st));
+  CU(cudaStreamSynchronize(s->st));
+  if (*h) return set_err(SPB_ERANGE, "spb: %s (error bits 0x%x)", err_bits_text(*h), *h);
+  return SPB_OK;
+}
+
+static int sync_pos(spb_session *s) {
+  CU(cudaMemcpyAsync(s->pos_dev, &s->pos, 4, cudaMemcpyHostToDevice, s->st));
+  return SPB_OK;
+}
+
+extern "C" int spb_session_prefill(spb_session *s, const int32_t *tokens, int n_tok, float *logits) {
+  if (!s || !tokens || n_tok <= 0) return set_err(SPB_EBADARG, "spb_session_prefill: bad arg");
+  if (n_tok > s->pmax - s->pos) return set_err(SPB_ECONTEXT_FULL, "spb_session_prefill: context full");
+  CU(cudaSetDevice(s->m->device));
+  const int pos0 = s->pos;
+  int rc = sync_pos(s);
+  if (rc) return rc;
+  int done = 0;
+  while (done < n_tok) {
+    int nt = NT_MAX;
+    while (nt > n_tok - done) nt >>= 1;
+    memcpy(s->h_pinned, tokens + done, (size_t)nt * 4);
+    CU(cudaMemcpyAsync(s->tok_dev, s->h_pinned, (size_t)nt * 4, cudaMemcpyHostToDevice, s->st));
+    CU(enqueue_rows(s, nt, logits != nullptr));
+    CU(launch_advance(s->pos_dev, nt, nullptr, nullptr, s->st));
+    if (logits)
+      CU(cudaMemcpyAsync(logits + (size_t)done * s->m->V, s->logits, (size_t)nt * s->m->V * 4,
+                         cudaMemcpyDeviceToHost, s->st));
+    // the pinned token staging is reused next chunk: wait for the H2D copy
+    CU(cudaStreamSynchronize(s->st));
+    done += nt;
+  }
+  rc = collect_errors(s);
+  if (rc) { s->pos = pos0; sync_pos(s); cudaStreamSynchronize(s->st); return rc; }
+  s->pos = pos0 + n_tok;
+  return SPB_OK;
+}
+
+static int ensure_step_graph(spb_session *s) {
+  if (s->step_graph) return SPB_OK;
+  cudaGraph_t g = nullptr;
+  CU(cudaStreamBeginCapture(s->st, cudaStreamCaptureModeThreadLocal));
+  cudaError_t e = enqueue_rows(s, 1, true);
+  if (e == cudaSuccess) e = launch_advance(s->pos_dev, 1, s->argmax_dev, s->tok_dev, s->st);
+  cudaError_t e2 = cudaStreamEndCapture(s->st, &g);
+  if (e != cudaSuccess || e2 != cudaSuccess) {
+    if (g) cudaGraphDestroy(g);
+    return set_err(SPB_ECUDA, "spb: graph capture: %s", cudaGetErrorString(e != cudaSuccess ? e : e2));
+  }
+  e = cudaGraphInstantiate(&s->step_graph, g, 0);
+  cudaGraphDestroy(g);
+  if (e != cudaSuccess) return set_err(SPB_ECUDA, "spb: graph instantiate: %s", cudaGetErrorString(e));
+  return SPB_OK;
+}
+
+extern "C" int spb_session_decode_step_argmax(spb_session *s, int32_t token, float *logits, int32_t *argmax) {
+  if (!s) return set_err(SPB_EBADARG, "spb_session_decode_step: null session");
+  if (s->pos >= s->pmax) return set_err(SPB_ECONTEXT_FULL, "spb_session_decode_step: context full");
+  CU(cudaSetDevice(s->m->device));
+  int rc = ensure_step_graph(s);
+  if (rc) return rc;
+  s->h_pinned[0] = token;
+  CU(cudaMemcpyAsync(s->tok_dev, s->h_pinned, 4, cudaMemcpyHostToDevice, s->st));
+  CU(cudaGraphLaunch(s->step_graph, s->st));
+  if (logits) CU(cudaMemcpyAsync(logits, s->logits, (size_t)s->m->V * 4, cudaMemcpyDeviceToHost, s->st));
+  if (argmax) CU(cudaMemcpyAsync(s->h_pinned + NT_MAX + 1, s->argmax_dev, 4, cudaMemcpyDeviceToHost, s->st));
+  rc = collect_errors(s);
+  if (rc) { sync_pos(s); cudaStreamSynchronize(s->st); return rc; }
+  if (argmax) *argmax = s->h_pinned[NT_MAX + 1];
+  s->pos += 1;
+  return SPB_OK;
+}
+
+extern "C" int spb_session_decode_step(spb_session *s, int32_t token, float *logits) {
+  return spb_session_decode_step_argmax(s, token, logits, nullptr);
+}
+
+extern "C" int spb_session_decode_greedy(spb_session *s, int32_t token, int n_steps, int32_t *tokens_out) {
+  if (!s || n_steps < 0) return set_err(SPB_EBADARG, "spb_session_decode_greedy: bad arg");
+  if (n_steps > s->pmax - s->pos) return set_err(SPB_ECONTEXT_FULL, "spb_session_decode_greedy: context full");
+  if (n_steps == 0) return SPB_OK;
+  CU(cudaSetDevice(s->m->device));
+  int rc = ensure_step_graph(s);
+  if (rc) return rc;
+  s->h_pinned[0] = token;
+  CU(cudaMemcpyAsync(s->tok_dev, s->h_pinned, 4, cudaMemcpyHostToDevice, s->st));
+  for (int i = 0; i < n_steps; i++) {
+    CU(cudaGraphLaunch(s->step_graph, s->st));
+    // after the step, tok_dev holds this step's argmax (the graph's last node copies it)
+    CU(cudaMemcpyAsync(s->hist_dev + s->pos + i, s->tok_dev, 4, cudaMemcpyDeviceToDevice, s->st));
+  }
+  if (tokens_out)
+    CU(cudaMemcpyAsync(tokens_out, s->hist_dev + s->pos, (size_t)n_steps * 4, cudaMemcpyDeviceToHost, s->st));
+  rc = collect_errors(s);
+  if (rc) { sync_pos(s); cudaStreamSynchronize(s->st); return rc; }
+  s->pos += n_steps;
+  return SPB_OK;
+}
+
+extern "C" int spb_session_rewind(spb_session *s, int n) {
+  if (!s) return set_err(SPB_EBADARG, "spb_session_rewind: null session");
+  if (n < 0 || n > s->pos) return set_err(SPB_EBADARG, "spb_session_rewind: n > position");
+  s->pos -= n;
+  CU(cudaSetDevice(s->m->device));
+  int rc = sync_pos(s);
+  if (rc) return rc;
+  CU(cudaStreamSynchronize(s->st));
+  return SPB_OK;
+}
+
+extern "C" int spb_session_clone(const spb_session *s, spb_session **out) {
+  if (!s || !out) return set_err(SPB_EBADARG, "spb_session_clone: null arg");
+  int rc = spb_session_open(s->m, s->pmax, out);
+  if (rc) return rc;
+  spb_session *c = *out;
+  const size_t kvn = (size_t)s->m->NL * kv_layer_elems(s->m, s->pmax);
+  CU(cudaStreamSynchronize(s->st));
+  CU(cudaMemcpyAsync(c->kc, s->kc, kvn * 4, cudaMemcpyDeviceToDevice, c->st));
+  CU(cudaMemcpyAsync(c->vc, s->vc, kvn * 4, cudaMemcpyDeviceToDevice, c->st));
+  CU(cudaMemcpyAsync(c->hist_dev, s->hist_dev, (size_t)s->pmax * 4, cudaMemcpyDeviceToDevice, c->st));
+  c->pos = s->pos;
+  rc = sync_pos(c);
+  if (rc) return rc;
+  CU(cudaStreamSynchronize(c->st));
+  return SPB_OK;
+}
+
+extern "C" int spb_session_kv_read(const spb_session *s, int layer, int pos, int which, int32_t *out) {
+  if (!s || !out || layer < 0 || layer >= s->m->NL || pos < 0 || pos >= s->pmax)
+    return set_err(SPB_EBADARG, "spb_session_kv_read: bad arg");
+  const spb_model *m = s->m;
+  const int32_t *base = (which ? s->vc : s->kc) + (size_t)layer * kv_layer_elems(m, s->pmax);
+  CU(cudaStreamSynchronize(s->st));
+  for (int g = 0; g < m->NKV; g++)
+    CU(cudaMemcpy(out + (size_t)g * m->HD, base + ((size_t)g * s->pmax + pos) * m->HD, (size_t)m->HD * 4,
+                  cudaMemcpyDeviceToHost));
+  return SPB_OK;
+}
+
+extern "C" int spb_forward(spb_model *m, const int32_t *tokens, int n_tok, float *logits) {
+  if (!m || !tokens || n_tok <= 0 || !logits) return set_err(SPB_EBADARG, "spb_forward: bad arg");
+  spb_session *s = nullptr;
+  int rc = spb_session_open(m, n_tok, &s);
+  if (rc) return rc;
+  rc = spb_session_prefill(s, tokens, n_tok, logits);
+  spb_session_close(s);
+  return rc;
+}
+
+// ------------------------------------------------------------------------------ isolated kernels
+struct DevWork {
+  int device = -1;
+  uint8_t *buf = nullptr;
+  size_t cap = 0;
+  uint32_t *err = nullptr;
+};
+static std::mutex g_work_mu;
+static DevWork g_work[64];
+
+static int work_get(size_t need, uint8_t **buf, uint32_t **err) {
+  int dev = 0;
+  CU(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return set_err(SPB_EBADARG, "spb: device id");
+  std::lock_guard<std::mutex> lk(g_work_mu);
+  DevWork &w = g_work[dev];
+  if (!w.err) CU(cudaMalloc(&w.err, 256));
+  if (!w.err) return SPB_EOOM;
+  if (w.cap < need) {
+    if (w.buf) cudaFree(w.buf);
+    w.buf = nullptr;
+    w.cap = 0;
+    CU(cudaMalloc(&w.buf, need));
+    w.cap = need;
+    CU(cudaMemset(w.err, 0, 256));
+  }
+  *buf = w.buf;
+  *err = w.err;
+  return SPB_OK;
+}
+
+extern "C" int spb_gemv_q4b(const uint8_t *codes, const uint16_t *bscale, int rows, int cols, const float *x,
+                            int n_tok, float *y, void *stream) {
+  if (!codes || !bscale || !x || !y || rows <= 0 || cols <= 0 || (cols & 31))
+    return set_err(SPB_EBADARG, "spb_gemv_q4b: bad arg (cols must be a positive multiple of 32)");
+  if (n_tok != 1 && n_tok != 2 && n_tok != 4 && n_tok != 8 && n_tok != 16)
+    return set_err(SPB_EBADARG, "spb_gemv_q4b: n_tok must be 1, 2, 4, 8 or 16");
+  const size_t need = (size_t)n_tok * cols + (size_t)n_tok * (cols / 32) * 4 + 256 + 64;
+  uint8_t *wb;
+  uint32_t *err;
+  int rc = work_get(need, &wb, &err);
+  if (rc) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  DevAct act{(int8_t *)wb, (int32_t *)(wb + (size_t)n_tok * cols),
+             (float *)(wb + (((size_t)n_tok * cols + (size_t)n_tok * (cols / 32) * 4 + 255) & ~(size_t)255))};
+  CU(launch_quant(x, cols, cols, n_tok, act, err, st));
+  DevQ4B w{codes, bscale, rows, cols};
+  CU(launch_gemv(w, nullptr, act, n_tok, y, rows, EPI_STORE, err, st));
+  return SPB_OK;
+}
+
+extern "C" int spb_take_device_errors(void) {
+  uint8_t *wb;
+  uint32_t *err;
+  int rc = work_get(256, &wb, &err);
+  if (rc) return rc;
+  uint32_t h = 0;
+  CU(cudaMemcpy(&h, err, 4, cudaMemcpyDeviceToHost));
+  CU(cudaMemset(err, 0, 4));
+  return (int)h;
+}
+
+extern "C" int spb_rmsnorm_exact_dev(const float *x, const float *w, int n, int rows, float *out, void *stream) {
+  if (!x || !w || !out || n <= 0 || rows <= 0 || n > 16384) return set_err(SPB_EBADARG, "spb_rmsnorm_exact_dev: bad arg");
+  uint8_t *wb;
+  uint32_t *err;
+  int rc = work_get(256, &wb, &err);
+  if (rc) return rc;
+  CU(launch_rmsnorm_rows(x, w, n, rows, out, err, (cudaStream_t)stream));
+  return SPB_OK;
+}
+
+static int eltwise(const float *x, int n, float *out, void *stream, int op) {
+  if (!x || !out || n <= 0) return set_err(SPB_EBADARG, "spb eltwise: bad arg");
+  uint8_t *wb;
+  uint32_t *err;
+  int rc = work_get(256, &wb, &err);
+  if (rc) return rc;
+  CU(launch_eltwise(x, n, out, op, err, (cudaStream_t)stream));
+  return SPB_OK;
+}
+extern "C" int spb_gelu_exact_dev(const float *x, int n, float *out, void *stream) { return eltwise(x, n, out, stream, 0); }
+extern "C" int spb_silu_exact_dev(const float *x, int n, float *out, void *stream) { return eltwise(x, n, out, stream, 1); }
+
+extern "C" int spb_rope_cordic_dev(const float *v, int d, int rows, const int32_t *pos, float base, int32_t *out,
+                                   void *stream) {
+  if (!v || !pos || !out || rows <= 0 || d <= 0 || (d & 1) || d > 2048) return set_err(SPB_EBADARG, "spb_rope_cordic_dev: bad arg");
+  std::vector<uint64_t> ht(32 + d / 2, 0);
+  uint64_t gain = 0;
+  spb_cordic_tables(ht.data(), &gain);
+  int rc = spb_rope_freq_table(base, d, ht.data() + 32);
+  if (rc) return rc;
+  const size_t need = ht.size() * 8;
+  uint8_t *wb;
+  uint32_t *err;
+  rc = work_get(need, &wb, &err);
+  if (rc) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  CU(cudaMemcpyAsync(wb, ht.data(), need, cudaMemcpyHostToDevice, st));
+  CU(launch_rope_rows(v, d, rows, pos, (const uint64_t *)wb + 32, (const uint64_t *)wb, gain, out, err, st));
+  CU(cudaStreamSynchronize(st));
+  return SPB_OK;
+}

@@ -1,0 +1,83 @@
+"""Generate the golden vectors under tests/golden/ by running the reference's own
+compiled code (oracle/_ref/libspref.so, built from the reference sources by
+`make -C oracle ref`). Re-run: python tests/golden/make_golden.py
+
+Every vector is (seeded input, reference output). The CPU test-suite checks the XREF
+restatement against them, so XREF stays pinned where the reference tree is absent.
+"""
+import ctypes as C
+import os
+import sys
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, os.path.join(ROOT, "oracle"))
+sys.path.insert(0, os.path.join(ROOT, "shannon-prime-system_b200"))
+import spmodel  # noqa: E402
+import xref  # noqa: E402
+
+
+def main():
+    C.CDLL(xref.SPREF_SO, mode=C.RTLD_GLOBAL)
+    R = xref.RefLib()
+    L = R.lib
+    rng = np.random.default_rng(20261201)
+    out = {}
+    # ---- islands (exact_islands.c:60-124), the T_EXACT_ISLANDS sizes and a scale sweep
+    cases = [(3840, 1.0), (3840, 0.01), (4096, 3.0), (512, 40.0), (256, 0.3), (64, 1.0), (128, 7.0),
+             (1, 2.0), (37, 0.5), (15360, 1.0)]
+    for i, (n, sc) in enumerate(cases):
+        x = (rng.standard_normal(n) * sc).astype(np.float32)
+        w = (1.0 + 0.1 * rng.standard_normal(n)).astype(np.float32)
+        y = np.empty(n, np.float32)
+        L.sp_rmsnorm_exact(x.ctypes.data, w.ctypes.data, n, y.ctypes.data)
+        out[f"rms{i}_x"], out[f"rms{i}_w"], out[f"rms{i}_y"] = x, w, y
+    for i, (m, sc) in enumerate([(256, 3.0), (1024, 10.0), (1, 1.0), (8192, 5.0), (33, 0.01)]):
+        z = (rng.standard_normal(m) * sc).astype(np.float32)
+        p = np.empty(m, np.float64)
+        L.sp_softmax_exact(z.ctypes.data, m, p.ctypes.data)
+        out[f"sm{i}_z"], out[f"sm{i}_p"] = z, p
+    for i, (n, sc) in enumerate([(512, 1.0), (4096, 4.0), (2048, 0.05), (1000, 30.0)]):
+        x = (rng.standard_normal(n) * sc).astype(np.float32)
+        y = np.empty(n, np.float32)
+        L.sp_gelu_exact(x.ctypes.data, n, y.ctypes.data)
+        out[f"gelu{i}_x"], out[f"gelu{i}_y"] = x, y
+    # ---- codec: every f16 (weight_dtype.c:9-28) and the quantizer (frobenius_lift.c:27-35)
+    h = np.arange(65536, dtype=np.uint16)
+    f = np.array([L.sp_f16_to_f32(int(v)) for v in h], np.float32)
+    out["f16_bits"], out["f16_f32"] = h, f
+    v = (rng.standard_normal(20000) * 3).astype(np.float32)
+    s = np.float32(np.abs(v).max())
+    v[:6] = [s, -s, 0.0, s / 254, -s / 254, s * 0.999]
+    q = np.array([L.sp_frob_quant1(float(a), float(s)) for a in v], np.int8)
+    out["q1_v"], out["q1_s"], out["q1_q"] = v, np.array([s], np.float32), q
+    # ---- Q4 unpack (frobenius_lift.c:102-107)
+    nib = rng.integers(0, 256, 64, dtype=np.uint8)
+    codes = np.empty(128, np.int8)
+    L.sp_frob_q4_unpack.argtypes = [C.c_void_p, C.c_int, C.c_void_p]
+    L.sp_frob_q4_unpack(nib.ctypes.data, 128, codes.ctypes.data)
+    out["unpack_nib"], out["unpack_codes"] = nib, codes
+    # ---- hashes of the .sp-model format (sp_hash.c)
+    names = [b"", b"token_embd.weight", b"blk.0.attn_q.weight.bscale", bytes(range(97))]
+    out["xxh64"] = np.array([L.sp_xxh64(n, len(n), 0) for n in names], np.uint64)
+    out["crc32"] = np.array([L.sp_crc32(n, len(n)) for n in names], np.uint32)
+    # ---- reference float forward on the micro models (fidelity, not a byte gate)
+    for name in ("micro_gemma", "micro_qwen"):
+        cfg = spmodel.CONFIGS[name]
+        T = spmodel.gen_model(cfg, seed=0)
+        mp, tp = f"/tmp/golden_{name}.sp-model", f"/tmp/golden_{name}.sp-tokenizer"
+        spmodel.write_sp_model(mp, tp, cfg, T)
+        m = R.load(mp, tp)
+        sess = R.session(m, cfg.max_context)
+        toks = spmodel.gen_tokens(11, 20, cfg.n_vocab)
+        rc, lg = R.prefill(sess, toks, cfg.n_vocab)
+        assert rc == 0, R.err()
+        out[f"fwd_{name}_tokens"], out[f"fwd_{name}_logits"] = toks, lg
+    np.savez_compressed(os.path.join(HERE, "reference_vectors.npz"), **out)
+    print("wrote", len(out), "arrays")
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,106 @@
+"""The drop-in: the reference's own libshannonprime session (sp_prefill_chunk /
+sp_decode_step / sp_session_clone / sp_session_rewind) with the B200 backend
+registered through its section-6 and section-6b hooks, byte-identical to XREF."""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+import spb200
+import spmodel
+import xref
+
+pytestmark = pytest.mark.gpu
+
+
+def u32(a):
+    return np.ascontiguousarray(a).view(np.uint32)
+
+
+@pytest.fixture(scope="module", params=["micro_gemma", "micro_qwen"])
+def setup(request, reflib, xr, tmp_path_factory):
+    cfg = spmodel.CONFIGS[request.param]
+    T = spmodel.gen_model(cfg, seed=0)
+    d = tmp_path_factory.mktemp("m")
+    mp, tp = str(d / "m.sp-model"), str(d / "m.sp-tokenizer")
+    spmodel.write_sp_model(mp, tp, cfg, T)
+    model = reflib.load(mp, tp)
+    l1 = spb200.load_l1()
+    yield cfg, T, model, l1
+    reflib.lib.sp_model_unload(model)
+
+
+def test_section6_prefill(reflib, xr, cuda_ok, setup):
+    cfg, T, model, l1 = setup
+    L = reflib.lib
+    s = reflib.session(model, cfg.max_context)
+    fn = C.cast(l1.spb_l1_forward, C.c_void_p)
+    assert L.sp_session_register_forward_backend(s, l1.spb_l1_backend(), fn) == 0
+    toks = spmodel.gen_tokens(31, 24, cfg.n_vocab)
+    want = xr.session(xref.build_desc(cfg, T), cfg.max_context).prefill(toks)
+    rc, lg = reflib.prefill(s, toks[:10], cfg.n_vocab)
+    assert rc == 0, reflib.err()
+    assert np.array_equal(u32(lg), u32(want[9]))
+    rc, lg = reflib.prefill(s, toks[10:], cfg.n_vocab)      # re-runs the whole history
+    assert rc == 0 and np.array_equal(u32(lg), u32(want[-1]))
+    assert reflib.position(s) == 24
+    L.sp_session_destroy(s)
+
+
+def test_section6b_decode(reflib, xr, cuda_ok, setup):
+    cfg, T, model, l1 = setup
+    L = reflib.lib
+    s = reflib.session(model, cfg.max_context)
+    qm = L.sp_session_qwen3_model(s)
+    dt = l1.spb_l1_kvdecode_table()
+    OPEN = C.CFUNCTYPE(C.c_int, C.c_void_p, C.c_int, C.POINTER(C.c_void_p))
+    PRE = C.CFUNCTYPE(C.c_int, C.c_void_p, C.c_void_p, C.c_int)
+    REW = C.CFUNCTYPE(C.c_int, C.c_void_p, C.c_int)
+    POS = C.CFUNCTYPE(C.c_int, C.c_void_p)
+    CLOSE = C.CFUNCTYPE(None, C.c_void_p)
+    fns = (C.c_void_p * 6).from_address(dt)
+    h = C.c_void_p()
+    assert OPEN(fns[0])(qm, cfg.max_context, C.byref(h)) == 0
+    toks = spmodel.gen_tokens(32, 16, cfg.n_vocab)
+    xs = xr.session(xref.build_desc(cfg, T), cfg.max_context)
+    lx = xs.prefill(toks)[-1]
+    # the caller drives prefill on both sides (sp_prefill_chunk does not feed section 6b)
+    rc, _ = reflib.prefill(s, toks, cfg.n_vocab)
+    assert rc == 0
+    assert PRE(fns[1])(h, toks.ctypes.data, toks.size) == 0
+    assert L.sp_session_register_kvdecode_backend(s, h, dt) == 0
+    tok = int(lx.argmax())
+    for i in range(10):
+        lx = xs.step(tok)
+        rc, lg = reflib.decode(s, tok, cfg.n_vocab)
+        assert rc == 0, reflib.err()
+        assert np.array_equal(u32(lg), u32(lx)), f"step {i}"
+        tok = int(lg.argmax())
+    assert POS(fns[4])(h) == 26 and reflib.position(s) == 26
+    # rewind must be mirrored by the caller (sp_session_rewind does not call dt->rewind)
+    assert L.sp_session_rewind(s, 2) == 0 and REW(fns[3])(h, 2) == 0
+    assert xs.rewind(2) == 0
+    lx = xs.step(7)
+    rc, lg = reflib.decode(s, 7, cfg.n_vocab)
+    assert rc == 0 and np.array_equal(u32(lg), u32(lx))
+    # append-only clone row: fork the resident cache
+    h2 = C.c_void_p()
+    assert l1.spb_l1_kvdecode_clone(h, C.byref(h2)) == 0
+    assert POS(fns[4])(h2) == POS(fns[4])(h)
+    # bad token: the backend fails, the session reports SP_EBADSTATE with detail
+    rc, _ = reflib.decode(s, cfg.n_vocab + 1, cfg.n_vocab)
+    assert rc == -4
+    CLOSE(fns[5])(h2)
+    CLOSE(fns[5])(h)
+    L.sp_session_register_kvdecode_backend(s, None, None)
+    L.sp_session_destroy(s)
+
+
+def test_non_q4b_model_rejected(reflib, cuda_ok, tmp_path):
+    """A model whose weights are not OK_Q4B arena tensors is refused with a clear error."""
+    l1 = spb200.load_l1()
+    L = reflib.lib
+    fn = C.cast(l1.spb_l1_forward, C.c_void_p)
+    rc = C.CFUNCTYPE(C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p)(fn.value)(
+        None, None, None, 1, None)
+    assert rc != 0 and b"null model" in L.sp_last_error()

@@ -1,0 +1,111 @@
+"""XREF (the CPU checker) pinned against the reference's own outputs.
+
+Golden vectors (tests/golden/reference_vectors.npz) were produced by running the
+reference's compiled code (tests/golden/make_golden.py); where the compiled reference
+is present (oracle/_ref/libspref.so) the same comparisons also run live on fresh inputs.
+"""
+import os
+
+import numpy as np
+import pytest
+
+from conftest import GOLDEN, rng
+
+G = np.load(os.path.join(GOLDEN, "reference_vectors.npz"))
+
+
+def bits(a):
+    return np.ascontiguousarray(a).view(np.uint32 if a.dtype == np.float32 else np.uint64)
+
+
+@pytest.mark.parametrize("i", range(10))
+def test_rmsnorm_island_golden(xr, i):
+    y = xr.rmsnorm(G[f"rms{i}_x"], G[f"rms{i}_w"])
+    assert np.array_equal(bits(y), bits(G[f"rms{i}_y"]))
+
+
+@pytest.mark.parametrize("i", range(5))
+def test_softmax_island_golden(xr, i):
+    p = xr.softmax(G[f"sm{i}_z"])
+    assert np.array_equal(bits(p), bits(G[f"sm{i}_p"]))
+
+
+@pytest.mark.parametrize("i", range(4))
+def test_gelu_island_golden(xr, i):
+    y = xr.gelu(G[f"gelu{i}_x"])
+    assert np.array_equal(bits(y), bits(G[f"gelu{i}_y"]))
+
+
+def test_f16_all_values_golden(xr):
+    import ctypes as C
+    f = xr.lib.xref_f16_to_f32
+    f.argtypes = [C.c_uint16]
+    f.restype = C.c_float
+    got = np.array([f(int(h)) for h in G["f16_bits"]], np.float32)
+    ref = G["f16_f32"]
+    nan = np.isnan(ref)
+    assert np.array_equal(np.isnan(got), nan)
+    assert np.array_equal(bits(got[~nan]), bits(ref[~nan]))
+
+
+def test_quant1_golden(xr):
+    import ctypes as C
+    f = xr.lib.xref_quant1
+    f.argtypes = [C.c_float, C.c_float]
+    f.restype = C.c_int8
+    s = float(G["q1_s"][0])
+    got = np.array([f(float(v), s) for v in G["q1_v"]], np.int8)
+    assert np.array_equal(got, G["q1_q"])
+
+
+def test_unpack_golden(xr):
+    import ctypes as C
+    out = np.empty(128, np.int8)
+    xr.lib.xref_unpack_q4.argtypes = [C.c_void_p, C.c_int, C.c_void_p]
+    nib = np.ascontiguousarray(G["unpack_nib"])
+    xr.lib.xref_unpack_q4(nib.ctypes.data, 128, out.ctypes.data)
+    assert np.array_equal(out, G["unpack_codes"])
+
+
+def test_hashes_golden():
+    import zlib
+    import spmodel
+    names = [b"", b"token_embd.weight", b"blk.0.attn_q.weight.bscale", bytes(range(97))]
+    assert [spmodel.xxh64(n) for n in names] == [int(v) for v in G["xxh64"]]
+    assert [zlib.crc32(n) & 0xFFFFFFFF for n in names] == [int(v) for v in G["crc32"]]
+
+
+@pytest.mark.parametrize("name", ["micro_gemma", "micro_qwen"])
+def test_xref_fidelity_vs_reference_float_forward(xr, name):
+    """XREF is a fidelity replacement of the reference float forward: same model, same
+    tokens -> logits within 1% relative L2 and the same greedy token."""
+    import spmodel
+    import xref
+    cfg = spmodel.CONFIGS[name]
+    T = spmodel.gen_model(cfg, seed=0)
+    s = xr.session(xref.build_desc(cfg, T), cfg.max_context)
+    lg = s.prefill(G[f"fwd_{name}_tokens"])[-1]
+    ref = G[f"fwd_{name}_logits"]
+    rel = np.linalg.norm(lg - ref) / np.linalg.norm(ref)
+    assert rel < 1e-2, rel
+    assert lg.argmax() == ref.argmax()
+
+
+# ---- live comparisons against the compiled reference (skipped when it is absent)
+def test_islands_live_random(xr, reflib):
+    L = reflib.lib
+    r = rng(5)
+    for _ in range(200):
+        n = int(r.integers(1, 5000))
+        sc = float(10.0 ** r.uniform(-4, 2.5))
+        x = (r.standard_normal(n) * sc).astype(np.float32)
+        w = (1 + 0.1 * r.standard_normal(n)).astype(np.float32)
+        y = np.empty(n, np.float32)
+        L.sp_rmsnorm_exact(x.ctypes.data, w.ctypes.data, n, y.ctypes.data)
+        assert np.array_equal(bits(xr.rmsnorm(x, w)), bits(y))
+        p = np.empty(n, np.float64)
+        L.sp_softmax_exact(x.ctypes.data, n, p.ctypes.data)
+        assert np.array_equal(bits(xr.softmax(x)), bits(p))
+        xg = np.clip(x, -1500, 1500)
+        L.sp_gelu_exact(xg.ctypes.data, n, y.ctypes.data)
+        assert np.array_equal(bits(xr.gelu(xg)), bits(y))
