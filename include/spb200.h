@@ -121,6 +121,19 @@ int  spb_forward(spb_model *m, const int32_t *tokens, int n_tok, float *logits);
  * workspace allocated on first use. */
 int spb_gemv_q4b(const uint8_t *codes, const uint16_t *bscale, int rows, int cols,
                  const float *x, int n_tok, float *y, void *stream);
+/* The activation quantizer alone: n_tok rows of cols floats -> the GEMV's input form:
+ * q [n_tok][cols] int8 (per 8 columns: the 4 even then the 4 odd), bsum [n_tok][cols/32]
+ * int32 block sums of q, scale [n_tok] f32 (max|x|). All device pointers. */
+int spb_quantize_rows(const float *x, int cols, int n_tok, int8_t *q, int32_t *bsum, float *scale,
+                      void *stream);
+/* The dequant-GEMV alone over pre-quantized activations (the form above). */
+int spb_gemv_q4b_q(const uint8_t *codes, const uint16_t *bscale, int rows, int cols, const int8_t *q,
+                   const int32_t *bsum, const float *scale, int n_tok, float *y, void *stream);
+/* Gated pair: y = act(W_gate x) * (W_up x), act 0 = exact GELU (Gemma3), 1 = exact SiLU. */
+int spb_gemv_q4b_gated_q(const uint8_t *codes_g, const uint16_t *bscale_g, const uint8_t *codes_u,
+                         const uint16_t *bscale_u, int rows, int cols, const int8_t *q,
+                         const int32_t *bsum, const float *scale, int n_tok, int act, float *y,
+                         void *stream);
 int spb_rmsnorm_exact_dev(const float *x, const float *w, int n, int rows, float *out, void *stream);
 int spb_gelu_exact_dev(const float *x, int n, float *out, void *stream);
 int spb_silu_exact_dev(const float *x, int n, float *out, void *stream);

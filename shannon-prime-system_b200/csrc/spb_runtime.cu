@@ -740,6 +740,52 @@ extern "C" int spb_gemv_q4b(const uint8_t *codes, const uint16_t *bscale, int ro
   return SPB_OK;
 }
 
+extern "C" int spb_quantize_rows(const float *x, int cols, int n_tok, int8_t *q, int32_t *bsum, float *scale,
+                                 void *stream) {
+  if (!x || !q || !bsum || !scale || cols <= 0 || (cols & 31) || n_tok <= 0)
+    return set_err(SPB_EBADARG, "spb_quantize_rows: bad arg (cols must be a positive multiple of 32)");
+  uint8_t *wb;
+  uint32_t *err;
+  int rc = work_get(256, &wb, &err);
+  if (rc) return rc;
+  CU(launch_quant(x, cols, cols, n_tok, DevAct{q, bsum, scale}, err, (cudaStream_t)stream));
+  return SPB_OK;
+}
+
+static int gemv_q_common(const uint8_t *codes, const uint16_t *bscale, const uint8_t *codes2, const uint16_t *bscale2,
+                         int rows, int cols, const int8_t *q, const int32_t *bsum, const float *scale, int n_tok,
+                         int epi, float *y, void *stream) {
+  if (!codes || !bscale || !q || !bsum || !scale || !y || rows <= 0 || cols <= 0 || (cols & 31))
+    return set_err(SPB_EBADARG, "spb_gemv_q4b_q: bad arg (cols must be a positive multiple of 32)");
+  if (n_tok != 1 && n_tok != 2 && n_tok != 4 && n_tok != 8 && n_tok != 16)
+    return set_err(SPB_EBADARG, "spb_gemv_q4b_q: n_tok must be 1, 2, 4, 8 or 16");
+  if (epi != EPI_STORE && (!codes2 || !bscale2)) return set_err(SPB_EBADARG, "spb_gemv_q4b_gated_q: null up matrix");
+  if (((uintptr_t)q & 15) || ((uintptr_t)codes & 15) || (codes2 && ((uintptr_t)codes2 & 15)))
+    return set_err(SPB_EBADARG, "spb_gemv_q4b_q: codes and q must be 16-byte aligned");
+  uint8_t *wb;
+  uint32_t *err;
+  int rc = work_get(256, &wb, &err);
+  if (rc) return rc;
+  DevQ4B w{codes, bscale, rows, cols}, w2{codes2, bscale2, rows, cols};
+  CU(launch_gemv(w, epi != EPI_STORE ? &w2 : nullptr, DevAct{(int8_t *)q, (int32_t *)bsum, (float *)scale}, n_tok,
+                 y, rows, epi, err, (cudaStream_t)stream));
+  return SPB_OK;
+}
+
+extern "C" int spb_gemv_q4b_q(const uint8_t *codes, const uint16_t *bscale, int rows, int cols, const int8_t *q,
+                              const int32_t *bsum, const float *scale, int n_tok, float *y, void *stream) {
+  return gemv_q_common(codes, bscale, nullptr, nullptr, rows, cols, q, bsum, scale, n_tok, EPI_STORE, y, stream);
+}
+
+extern "C" int spb_gemv_q4b_gated_q(const uint8_t *codes_g, const uint16_t *bscale_g, const uint8_t *codes_u,
+                                    const uint16_t *bscale_u, int rows, int cols, const int8_t *q,
+                                    const int32_t *bsum, const float *scale, int n_tok, int act, float *y,
+                                    void *stream) {
+  if (act != 0 && act != 1) return set_err(SPB_EBADARG, "spb_gemv_q4b_gated_q: act must be 0 (GELU) or 1 (SiLU)");
+  return gemv_q_common(codes_g, bscale_g, codes_u, bscale_u, rows, cols, q, bsum, scale, n_tok,
+                       act == 0 ? EPI_GELU_MUL : EPI_SILU_MUL, y, stream);
+}
+
 extern "C" int spb_take_device_errors(void) {
   uint8_t *wb;
   uint32_t *err;
