@@ -1,0 +1,340 @@
+#!/usr/bin/env python
+"""bench.py -- byte-exact decode tokens/s at the Gemma-3-12B shape (B=1), plus the
+dequant-GEMV's achieved HBM bandwidth against the measured peak.
+
+Workload: Gemma-3-12B-shaped decoder (48 layers, d_model
+3840, 16/8 heads, head_dim 256, FFN 15360 exact-GELU, vocab 262144, sliding window 1024
+on 5 of every 6 layers), random-init OK_Q4B weights generated on the device from a
+seed, batch 1: prefill --prefill random tokens (untimed), W warm-up decode steps, then
+K timed greedy decode steps. A step is one decode token through the whole model.
+
+  value    K tokens / device time of the K steps (CUDA events on the session stream;
+           inputs resident: each step's token is the previous step's device argmax)
+  e2e      the same K steps through the public C ABI call a user makes
+           (spb_session_decode_step_argmax): the token copied host->device from pinned
+           memory and the full-vocab logits copied device->host every step
+  roofline the dequant-GEMV alone, per decode shape, CUDA-event timed over weights
+           larger than L2, weighted by its share of a decode token's bytes
+Multi-GPU (torchrun): independent sessions spread one per GPU (weak scaling); the only
+collectives are the barrier and the max-over-ranks of the timings.
+
+--impl reference times the reference's own CPU decode (oracle/cpu_baseline.py) instead.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "shannon-prime-system_b200")
+ORACLE = os.path.join(ROOT, "oracle")
+sys.path.insert(0, PKG)
+
+METRIC = "byte-exact decode tokens/s (12B shape, B=1/64); dequant-GEMV HBM GB/s vs peak"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=256)
+    p.add_argument("--warmup", type=int, default=8)
+    p.add_argument("--impl", default="spb", choices=["spb", "reference"])
+    p.add_argument("--config", default="gemma12b")
+    p.add_argument("--prefill", type=int, default=2048)
+    p.add_argument("--seed", type=int, default=0)
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-roofline", action="store_true")
+    return p.parse_args()
+
+
+def dist_env():
+    return (int(os.environ.get("RANK", 0)), int(os.environ.get("LOCAL_RANK", 0)),
+            int(os.environ.get("WORLD_SIZE", 1)))
+
+
+# ----------------------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.p = None
+
+    def start(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                                       "--format=csv,noheader,nounits", "-lms", "100"],
+                                      stdout=self.f, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.p = None
+
+    def stop(self):
+        if self.p is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.p.terminate()
+        self.p.wait(timeout=10)
+        self.f.flush()
+        rows = []
+        for line in open(self.f.name):
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        os.unlink(self.f.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"], "samples": 0}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower().startswith("active")})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows),
+                "power_w_max": max(float(r[3]) for r in rows if r[3].replace(".", "").isdigit())}
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        d = json.load(open(path))
+        return float(d["hbm_gbs"]), "measured"
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+# ----------------------------------------------------------------------------- GEMV roofline
+def gemv_shapes(cfg):
+    """(name, rows, cols, gated, launches per decode token) of the decode step's GEMVs."""
+    E, FF = cfg.n_embd, cfg.n_ff
+    return [("qkv", cfg.qd + 2 * cfg.kvd, E, False, cfg.n_layers),
+            ("o", E, cfg.qd, False, cfg.n_layers),
+            ("gate_up", FF, E, True, cfg.n_layers),
+            ("down", E, FF, False, cfg.n_layers),
+            ("lm_head", cfg.n_vocab, E, False, 1)]
+
+
+def gemv_bytes(rows, cols, gated, m=1):
+    mats = 2 if gated else 1
+    return mats * (rows * cols // 2 + rows * (cols // 32) * 2) + m * cols + m * (cols // 32) * 4 + m * rows * 4
+
+
+def gemv_roofline(cfg, spb, device, stream, iters=60):
+    import ctypes as C
+    import torch
+    L2 = 126 * 2 ** 20
+    out = {}
+    tot_b = tot_t = 0.0
+    launches = 0
+    for name, rows, cols, gated, per_tok in gemv_shapes(cfg):
+        mats = 2 if gated else 1
+        wbytes = mats * (rows * cols // 2 + rows * (cols // 32) * 2)
+        copies = max(1, -(-3 * L2 // wbytes))          # rotate so the set exceeds L2 threefold
+        codes = [torch.randint(0, 256, (mats, rows * cols // 2), dtype=torch.uint8, device=device)
+                 for _ in range(copies)]
+        scl = [(torch.randint(0, 1024, (mats, rows * (cols // 32)), dtype=torch.int16, device=device)
+                | (5 << 10)) for _ in range(copies)]
+        x = torch.randn(1, cols, device=device)
+        q = torch.empty(cols, dtype=torch.int8, device=device)
+        bs = torch.empty(cols // 32, dtype=torch.int32, device=device)
+        sc = torch.empty(1, dtype=torch.float32, device=device)
+        y = torch.empty(rows, dtype=torch.float32, device=device)
+        P = lambda t: C.c_void_p(t.data_ptr())
+        spb.spb_quantize_rows(P(x), cols, 1, P(q), P(bs), P(sc), stream.cuda_stream)
+
+        def launch(i):
+            c, s = codes[i % copies], scl[i % copies]
+            if gated:
+                rc = spb.spb_gemv_q4b_gated_q(P(c[0]), P(s[0]), P(c[1]), P(s[1]), rows, cols, P(q), P(bs),
+                                             P(sc), 1, 0, P(y), stream.cuda_stream)
+            else:
+                rc = spb.spb_gemv_q4b_q(P(c[0]), P(s[0]), rows, cols, P(q), P(bs), P(sc), 1, P(y),
+                                        stream.cuda_stream)
+            assert rc == 0, spb.spb_last_error()
+        for i in range(5):
+            launch(i)
+        n = iters if name != "lm_head" else max(10, iters // 3)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for i in range(n):
+            launch(i)
+        e1.record(stream)
+        e1.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / n
+        b = gemv_bytes(rows, cols, gated)
+        out[name] = {"rows": rows, "cols": cols, "gated": gated, "us_per_launch": round(us, 3),
+                     "bytes_per_launch": b, "gbs": round(b / us / 1e3, 1), "launches_per_token": per_tok}
+        tot_b += b * per_tok
+        tot_t += us * per_tok
+        launches += n + 5
+        del codes, scl
+    return out, tot_b, tot_t, launches
+
+
+# ----------------------------------------------------------------------------- arms
+def run_spb(args):
+    import torch
+    import torch.distributed as dist
+    import spb200
+    import spmodel
+
+    rank, local, world = dist_env()
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    spb = spb200.load()
+    cfg = spmodel.CONFIGS[args.config]
+    K, W = args.steps, args.warmup
+    pmax = args.prefill + W + K + 8
+    m = spb200.Model.synthetic(cfg, seed=args.seed + rank, device=local)
+    s = m.session(pmax)
+    stream = torch.cuda.ExternalStream(s.stream(), device=torch.device("cuda", local))
+    toks = spmodel.gen_tokens(args.seed + 100 + rank, args.prefill, cfg.n_vocab)
+    t0 = time.perf_counter()
+    s.prefill(toks, logits=False)
+    prefill_s = time.perf_counter() - t0
+    tok = int(toks[-1])
+    s.greedy(tok, W)
+
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+    smi_index = vis.split(",")[local] if vis else str(local)
+    clocks = ClockSampler(smi_index)
+    clocks.start()
+    time.sleep(0.3)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(ms):
+        if world == 1:
+            return ms
+        t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # value: K greedy steps, inputs resident on the device
+    pos0 = s.position()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    generated = s.greedy(tok, K)
+    e1.record(stream)
+    e1.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1))
+    barrier()
+
+    # e2e: the same positions again through the host-buffer API
+    s.rewind(s.position() - pos0)
+    host_logits = torch.empty(cfg.n_vocab, dtype=torch.float32).pin_memory()
+    import numpy as np
+    lg_np = host_logits.numpy()
+    barrier()
+    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t_e2e = tok
+    e2.record(stream)
+    e2e_tokens = []
+    for _ in range(K):
+        _, t_e2e = s.step_argmax(t_e2e, out=lg_np)
+        e2e_tokens.append(t_e2e)
+    e3.record(stream)
+    e3.synchronize()
+    ms_e2e = max_over_ranks(e2.elapsed_time(e3))
+    assert e2e_tokens == generated.tolist(), "host-API trajectory differs from the device-resident one"
+    barrier()
+
+    roof = None
+    if not args.no_roofline:
+        shapes, tot_b, tot_us, gl = gemv_roofline(cfg, spb, torch.device("cuda", local), stream)
+        peak, peak_kind = peaks()
+        achieved = tot_b / tot_us / 1e3
+        roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(achieved / peak, 4), "traffic": None,
+                "peak_source": f"{peak_kind} hbm_gbs (burst copy)", "kernel": "k_gemv (OK_Q4B dequant-GEMV, M=1)",
+                "algorithmic_bytes_per_token": int(tot_b), "gemv_us_per_token": round(tot_us, 1),
+                "per_shape": shapes}
+    clk = clocks.stop()
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        sys.path.insert(0, ORACLE)
+        import cpu_baseline
+        r = cpu_baseline.measure(cfg, procs=min(os.cpu_count() or 1, 32), steps=1)
+        if r:
+            cpu = {"value": round(r["value"], 5), "unit": "tokens/s", "cores": r["cores"], "kind": "reference",
+                   "sample": r["sample"]}
+
+    kernels_per_step = 1 + 10 * cfg.n_layers + 4
+    line = {
+        "metric": METRIC, "value": round(world * K / (ms / 1e3), 3), "unit": "tokens/s",
+        "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": round(ms / K, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8xint4->int64 (exact)",
+        "data": "synthetic (random-init OK_Q4B weights from a seed, uniform random tokens)",
+        "config": {"workload": f"{cfg.name} decode B=1 after a {args.prefill}-token prefill (BASELINE configs[2])",
+                   "model": "Gemma-3-12B shape: 48L d3840 16/8 heads hd256 FFN15360 vocab262144 SWA1024 (5 of 6)",
+                   "global_batch": world, "seq_len": args.prefill + W + K,
+                   "ctx_at_timing": [args.prefill + W, args.prefill + W + K],
+                   "parallelism": f"sessions spread: {world} independent session(s), one per GPU",
+                   "l2": "weights 6.6 GB per step >> 126 MB L2: every step streams from HBM",
+                   "weight_bytes_per_token": m.weight_bytes(), "prefill_s_untimed": round(prefill_s, 3)},
+        "e2e": {"value": round(world * K / (ms_e2e / 1e3), 3), "unit": "tokens/s", "h2d_bytes_per_step": 4,
+                "d2h_bytes_per_step": cfg.n_vocab * 4 + 4 + 4},
+        "gpu_launches": kernels_per_step * K,
+        "clocks": clk,
+        "roofline": roof,
+        "cpu_baseline": cpu,
+    }
+    s.close()
+    m.free()
+    if world > 1:
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def run_reference(args):
+    rank, _, world = dist_env()
+    if rank != 0:
+        return
+    sys.path.insert(0, ORACLE)
+    import cpu_baseline
+    import spmodel
+    cfg = spmodel.CONFIGS[args.config]
+    procs = os.cpu_count() or 1
+    # each step is one sampled token per process (a 1-layer slice, scaled); bounded to ~2 min
+    steps = max(1, min(args.steps, 8))
+    t0 = time.perf_counter()
+    r = cpu_baseline.measure(cfg, procs=procs, steps=steps)
+    wall = time.perf_counter() - t0
+    if r is None:
+        print(json.dumps({"impl": "reference", "unavailable": "reference library oracle/_ref/libspref.so not built"}))
+        return
+    v = round(r["value"], 5)
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "steps_sampled_per_process": steps,
+        "ms_per_step": round(1e3 / v, 1), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic", "config": {"workload": f"{cfg.name} decode B=1 (BASELINE configs[2])",
+                                                        "model": cfg.name, "global_batch": 1},
+        "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": r["cores"], "kind": "reference",
+                         "sample": r["sample"]},
+        "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "wall_s": round(wall, 1)}), flush=True)
+
+
+if __name__ == "__main__":
+    a = parse()
+    if a.impl == "reference":
+        run_reference(a)
+    else:
+        run_spb(a)
