@@ -143,6 +143,13 @@ int spb_rope_cordic_dev(const float *v, int d, int rows, const int32_t *pos, flo
 /* error bits raised by the last isolated-kernel call on this thread's device */
 int spb_take_device_errors(void);
 
+/* Record the spb_* kernel calls a caller makes on `stream` between begin and end into
+ * one instantiated CUDA graph, replayed by spb_graph_launch without per-call host cost. */
+int  spb_graph_begin(void *stream);
+int  spb_graph_end(void *stream, void **graph_exec);
+int  spb_graph_launch(void *graph_exec, void *stream);
+void spb_graph_free(void *graph_exec);
+
 /* ---- host-side tables (no device needed) ------------------------------------ */
 int      spb_rope_freq_table(float base, int d, uint64_t *W);      /* [d/2] turns Q64 */
 void     spb_cordic_tables(uint64_t T[30], uint64_t *gain_q62);

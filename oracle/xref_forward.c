@@ -139,6 +139,7 @@ void xref_session_destroy(xref_session *s) {
 
 static int norm(const float *x, const float *w, int n, float *out) {
     if (!rms_ok(x, n)) return XREF_ERANGE;
+    for (int i = 0; i < n; i++) if (!(fabsf(w[i]) < 32768.0f)) return XREF_ERANGE;
     xref_rmsnorm_exact(x, w, n, out);
     return XREF_OK;
 }

@@ -1,0 +1,67 @@
+// spb_async.cuh -- TMA bulk copies (cp.async.bulk) and mbarriers for sm_100a, with bounded
+// waits: every wait gives up after a fixed number of try_wait polls, raises an error bit
+// and lets the caller continue, so no kernel can spin forever.
+//
+// Only plain (non-multicast) bulk copies global -> this CTA's shared memory are used.
+#pragma once
+#include <cstdint>
+
+#include "spb_kernels.cuh"
+
+namespace spb {
+
+constexpr uint32_t MBAR_POLL_LIMIT = 1u << 22;
+
+__device__ __forceinline__ uint32_t smem_addr(const void *p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+
+// make barrier initialisation visible to the async proxy and the other threads
+__device__ __forceinline__ void mbar_init_fence() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+// order this CTA's earlier generic-proxy shared-memory accesses before later async-proxy writes
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
+               : "memory");
+}
+
+// 1-D bulk copy global -> shared of this CTA; dst, src 16-byte aligned, bytes % 16 == 0
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_addr(dst)),
+      "l"(src), "r"(bytes), "r"(smem_addr(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// wait for phase `parity` of `bar`; false (and ERR_TIMEOUT raised) after the poll limit
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint32_t *err) {
+  for (uint32_t i = 0; i < MBAR_POLL_LIMIT; i++)
+    if (mbar_try_wait(bar, parity)) return true;
+  if (err) atomicOr(err, ERR_TIMEOUT);
+  return false;
+}
+
+}  // namespace spb

@@ -111,16 +111,15 @@ __device__ __forceinline__ float silu_exact(float x) {
   return __double2float_rn(__dmul_rn(__ll2double_rn(g), 0x1p-30));
 }
 
-// floor(sqrt(v))
+// floor(sqrt(v)): a correctly rounded double sqrt gives the answer to within one or
+// two units; the integer checks s*s <= v < (s+1)^2 then make it exact.
 __device__ __forceinline__ uint64_t isqrt_u64(uint64_t v) {
-  uint64_t res = 0, bit = 1ull << 62;
-  while (bit > v) bit >>= 2;
-  while (bit) {
-    if (v >= res + bit) { v -= res + bit; res = (res >> 1) + bit; }
-    else res >>= 1;
-    bit >>= 2;
-  }
-  return res;
+  if (v == 0) return 0;
+  uint64_t s = (uint64_t)__dsqrt_rn(__ull2double_rn(v));
+  if (s > 0xFFFFFFFFull) s = 0xFFFFFFFFull;
+  while (s * s > v) s--;
+  while (s < 0xFFFFFFFFull && (s + 1) * (s + 1) <= v) s++;
+  return s;
 }
 
 // (hi:lo) / d for unsigned 128-bit numerator, 64-bit divisor; returns the low 64 bits
@@ -140,8 +139,55 @@ __device__ __forceinline__ uint64_t udiv128_lo(uint64_t hi, uint64_t lo, uint64_
   return q;
 }
 
+// floor((hi:lo) / d) when hi < d and the quotient is below 2^62: a double-precision
+// estimate, one residual-based refinement, and exact +-1 steps on the 128-bit residual.
+// Returns false (caller falls back to the long division) outside that range.
+__device__ __forceinline__ bool udiv128_fast(uint64_t hi, uint64_t lo, uint64_t d, uint64_t &q_out) {
+  if (hi >= d) return false;
+  const double dd = __ull2double_rn(d);
+  const double nd = __dadd_rn(__dmul_rn(__ull2double_rn(hi), 18446744073709551616.0), __ull2double_rn(lo));
+  const double qe = __ddiv_rn(nd, dd);
+  if (!(qe < 4611686018427387904.0)) return false;   // 2^62
+  uint64_t q = (uint64_t)qe;
+  for (int it = 0; it < 2; it++) {
+    // residual r = N - q*d as a signed 128-bit value
+    const uint64_t plo = q * d, phi = __umul64hi(q, d);
+    const uint64_t rlo = lo - plo;
+    const int64_t rhi = (int64_t)(hi - phi - (lo < plo ? 1ull : 0ull));
+    if (rhi == 0 && rlo < d) { q_out = q; return true; }
+    if (it == 1) {
+      // final exact steps: the estimate is now within a few units
+      int64_t h = rhi;
+      uint64_t l = rlo;
+      for (int k = 0; k < 8; k++) {
+        if (h < 0) {              // r < 0: q -= 1, r += d
+          const uint64_t nl = l + d;
+          h += (nl < l) ? 1 : 0;
+          l = nl;
+          q -= 1;
+        } else if (h > 0 || l >= d) {   // r >= d: q += 1, r -= d
+          const uint64_t nl = l - d;
+          h -= (l < d) ? 1 : 0;
+          l = nl;
+          q += 1;
+        } else {
+          q_out = q;
+          return true;
+        }
+      }
+      return false;
+    }
+    const double rd = __dadd_rn(__dmul_rn(__ll2double_rn(rhi), 18446744073709551616.0), __ull2double_rn(rlo));
+    const double corr = floor(__ddiv_rn(rd, dd));
+    q = (uint64_t)((int64_t)q + __double2ll_rz(corr));
+  }
+  return false;
+}
+
 // floor(n * 2^72 / ss) truncated to 64 bits (the RMSNorm island's uint64 quotient).
 __device__ __forceinline__ uint64_t rms_quotient(uint32_t n, uint64_t ss) {
+  uint64_t q;
+  if (udiv128_fast((uint64_t)n << 8, 0ull, ss, q)) return q;
   return udiv128_lo((uint64_t)n << 8, 0ull, ss);
 }
 
@@ -153,14 +199,18 @@ __device__ __forceinline__ int64_t floordiv_s128(int64_t hi, uint64_t lo, uint64
     alo = ~lo + 1ull;
     ahi = ~(uint64_t)hi + (alo == 0 ? 1ull : 0ull);
   }
-  uint64_t r = ahi % d;
-  uint64_t q = 0;
+  uint64_t q = 0, r = 0;
+  if (udiv128_fast(ahi, alo, d, q)) {
+    r = alo - q * d;   // the true remainder is < d < 2^64, so its low word is exact
+  } else {
+    r = ahi % d;
 #pragma unroll 1
-  for (int i = 63; i >= 0; i--) {
-    uint64_t top = r >> 63;
-    r = (r << 1) | ((alo >> i) & 1ull);
-    q <<= 1;
-    if (top || r >= d) { r -= d; q |= 1ull; }
+    for (int i = 63; i >= 0; i--) {
+      uint64_t top = r >> 63;
+      r = (r << 1) | ((alo >> i) & 1ull);
+      q <<= 1;
+      if (top || r >= d) { r -= d; q |= 1ull; }
+    }
   }
   if (!neg) return (int64_t)q;
   return r ? -(int64_t)q - 1 : -(int64_t)q;

@@ -4,23 +4,28 @@
 // under oracle/ states the same rules in C and the parity tests compare bytes):
 //
 //   k_gemv     OK_Q4B dequant-matvec/GEMM replacing matmul_arena's Q4B branch
-//              (forward_dispatch.c:69-86). 4-bit codes stream once from HBM in 16-byte
-//              vectors (one 32-column scale block per lane), are unpacked in registers
-//              (nibble ^ 8 gives code + 8 in [0,15]; the -8 * sum(x) correction is the
-//              precomputed per-block activation sum), multiplied with int8 activations
-//              by dp4a into an exact int32 block sum, scaled by the f16 block scale taken
-//              as an integer mantissa/shift and accumulated exactly in int64; warp-shuffle
-//              reduction; one rounding per output.
-//   k_quant    activation quantizer sp_frob_quant1 over max|u| (frobenius_lift.c:27-35).
+//              (forward_dispatch.c:69-86). Each warp owns a group of rows; every lane
+//              issues all of its 16-byte code vectors for the whole group before using any
+//              (one 32-column scale block per vector), so a warp keeps ~4-8 KB in flight.
+//              Nibbles are unpacked in registers (nibble ^ 8 = code + 8 in [0,15]; the
+//              -8 * sum(x) correction is the per-block activation sum), multiplied with the
+//              int8 activations by dp4a into an exact int32 block sum, scaled by the f16 block
+//              scale taken as integer mantissa and shift, accumulated exactly in int64, and
+//              reduced by warp shuffles; one rounding per output.
+//   k_quant_*  activation quantizer sp_frob_quant1 over max|u| (frobenius_lift.c:27-35);
+//              the max comes from the producing kernel (atomicMax of the f32 bits).
 //   k_norm     residual add + exact RMSNorm island (exact_islands.c:60-79) + quantizer.
 //   k_rope_kv  QK-norm island + CORDIC-RoPE onto the 2^16 score grid + KV-cache store
 //              (replaces sp_rope_neox, forward_kernels.c:31-41, and the KV memcpy,
 //              sp_session.c:433-436).
 //   k_attn     session-resident KV-decode attention (sp_attn_head, forward_kernels.c:
 //              59-81) with exact int64 scores, the softmax island's integer exponentials
-//              (exact_islands.c:82-97) and an exact 128-bit V-sum; one 8-CTA cluster per
-//              KV head splits the positions and exchanges max / partial sums through
-//              distributed shared memory.
+//              (exact_islands.c:82-97) and an exact 128-bit V-sum. One thread-block cluster
+//              per KV head splits the positions; each CTA streams its K then V slice through
+//              a ring of shared-memory stages filled by TMA bulk copies; the cluster
+//              exchanges the integer max and the partial sums through distributed shared
+//              memory.
+#include "spb_async.cuh"
 #include "spb_exact.cuh"
 #include "spb_kernels.cuh"
 
@@ -30,6 +35,61 @@
 namespace cg = cooperative_groups;
 
 namespace spb {
+
+// ------------------------------------------------------------------------------ launch helpers
+// Programmatic dependent launch: every kernel of the schedule lets its successor be
+// scheduled as soon as all of its own CTAs have started (griddepcontrol.launch_dependents),
+// and waits for its predecessor's completion (griddepcontrol.wait, a hardware wait, not a
+// spin) only right before it reads the predecessor's output. GEMVs issue their first weight
+// loads before that wait, so the weight stream overlaps the previous kernel's tail. Without
+// the launch attribute both instructions are no-ops.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+static int pdl_enabled() {
+  static int on = -1;
+  if (on < 0) {
+    const char *e = getenv("SPB_PDL");
+    on = (e && e[0] == '0') ? 0 : 1;
+  }
+  return on;
+}
+
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, int cluster,
+                            Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  if (pdl_enabled()) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    na++;
+  }
+  if (cluster > 1) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = cluster;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = 1;
+    na++;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
+// llround(x * 2^16) for |x| < 32768: x * 2^16 is exact in fp32 and below 2^31, its
+// fractional part is exact too, so this equals the islands' llround((double)x * 65536.0)
+__device__ __forceinline__ int32_t q16_round(float x) {
+  const float v = __fmul_rn(x, 65536.0f);
+  const float t = truncf(v);
+  const float f = __fsub_rn(v, t);
+  return (int32_t)t + (f >= 0.5f ? 1 : 0) - (f <= -0.5f ? 1 : 0);
+}
 
 // ------------------------------------------------------------------------------ GEMV
 constexpr int GEMV_THREADS = 256;
@@ -43,36 +103,90 @@ __device__ __forceinline__ uint4 ld_stream_u4(const uint8_t *p) {
   return v;
 }
 
-__device__ __forceinline__ int32_t block_dot(const uint4 cw, const int32_t *xw) {
-  // xw: the 8 activation words of this 32-column block (even cols, odd cols per group)
+// exact int32 dot of one 32-column block: 16 code bytes against the 8 activation words
+// (x0: words 0-3, x1: words 4-7; each 8-column group is [even cols][odd cols])
+__device__ __forceinline__ int32_t block_dot(const uint4 cw, const int4 x0, const int4 x1) {
   const uint32_t w[4] = {cw.x, cw.y, cw.z, cw.w};
+  const int32_t xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
   int32_t s = 0;
 #pragma unroll
   for (int g = 0; g < 4; g++) {
-    int32_t lo = (int32_t)((w[g] & 0x0F0F0F0Fu) ^ 0x08080808u);
-    int32_t hi = (int32_t)(((w[g] >> 4) & 0x0F0F0F0Fu) ^ 0x08080808u);
-    s = __dp4a(lo, xw[2 * g], s);
-    s = __dp4a(hi, xw[2 * g + 1], s);
+    const int32_t lo = (int32_t)((w[g] & 0x0F0F0F0Fu) ^ 0x08080808u);
+    const int32_t hi = (int32_t)(((w[g] >> 4) & 0x0F0F0F0Fu) ^ 0x08080808u);
+    s = __dp4a(lo, xv[2 * g], s);
+    s = __dp4a(hi, xv[2 * g + 1], s);
   }
   return s;
 }
 
-__device__ __forceinline__ int64_t scale_term(uint32_t h, int32_t isum) {
-  int32_t m, sh;
-  f16_scale_parts(h, m, sh);
-  return (int64_t)((uint64_t)(int64_t)(m * isum) << sh);
+// acc += k * isum with the f16 block scale as k = m * 2^sh (|m| < 2^11, sh < 30):
+// one 32-bit multiply (|m*isum| < 2^26) and one widening multiply-add by 2^sh.
+__device__ __forceinline__ void scale_acc(int64_t &acc, uint32_t h, int32_t isum) {
+  const uint32_t e = (h >> 10) & 31u;
+  int32_t m = (int32_t)(e ? ((h & 1023u) | 1024u) : (h & 1023u));
+  if (h & 0x8000u) m = -m;
+  const int32_t pw = 1 << (e ? e - 1 : 0);
+  acc += (int64_t)(m * isum) * (int64_t)pw;
 }
 
-template <int NT, int EPI>
-__global__ void __launch_bounds__(GEMV_THREADS)
-k_gemv(DevQ4B w, DevQ4B w2, DevAct act, float *__restrict__ y, int ldy, uint32_t *err) {
-  extern __shared__ __align__(16) uint8_t smem_raw[];
-  const int K = w.cols, nblk = K >> 5, kw = K >> 2;
-  int32_t *xw = reinterpret_cast<int32_t *>(smem_raw);            // [NT][K/4]
-  int32_t *xs = xw + NT * kw;                                       // [NT][nblk]
-  double *dsc = reinterpret_cast<double *>(xs + ((NT * nblk + 1) & ~1));  // [NT]
+// Greedy-argmax key: f32 bits mapped to an order-preserving uint32 in the high word, the
+// complemented row index in the low word, so a 64-bit max picks the largest value and,
+// among equal values, the lowest index (the first maximum).
+__device__ __forceinline__ unsigned long long argmax_key(float v, int row) {
+  const uint32_t b = __float_as_uint(v);
+  const uint32_t o = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+  return ((unsigned long long)o << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)row);
+}
 
-  {  // stage activations (already quantized, interleaved) into shared memory
+// NT token rows, epilogue EPI, NCH 16-byte vectors per lane per row (cols <= 1024*NCH),
+// RPW rows per warp group. ymax (nullable): per-token max |y| via atomicMax of f32 bits.
+template <int NT, int EPI, int NCH, int RPW>
+__global__ void __launch_bounds__(GEMV_THREADS)
+k_gemv(DevQ4B w, DevQ4B w2, DevAct act, float *__restrict__ y, int ldy, uint32_t *err, uint32_t *ymax,
+       unsigned long long *amax) {
+  constexpr int NM = (EPI == EPI_STORE) ? 1 : 2;
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  __shared__ float wmax[GEMV_WARPS][NT];
+  const int K = w.cols, nblk = K >> 5, kw = K >> 2;
+  int32_t *xw = reinterpret_cast<int32_t *>(smem_raw);                    // [NT][K/4]
+  int32_t *xs = xw + NT * kw;                                               // [NT][nblk]
+  double *dsc = reinterpret_cast<double *>(xs + ((NT * nblk + 1) & ~1));   // [NT]
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int rows = w.rows;
+  const size_t rstride = (size_t)(K >> 1);
+  const int ngroups = (rows + RPW - 1) / RPW;
+  const int gstride = gridDim.x * GEMV_WARPS;
+  int g = blockIdx.x * GEMV_WARPS + warp;
+
+  uint4 cw[NM][RPW][NCH];
+  uint32_t hw[NM][RPW][NCH];
+  auto load_group = [&](int grp) {
+#pragma unroll
+    for (int r = 0; r < RPW; r++) {
+      const int row = grp * RPW + r;
+#pragma unroll
+      for (int j = 0; j < NCH; j++) {
+        const int b = lane + 32 * j;
+        if (row < rows && b < nblk) {
+          cw[0][r][j] = ld_stream_u4(w.codes + (size_t)row * rstride + (size_t)b * 16);
+          hw[0][r][j] = __ldg(w.scales + (size_t)row * nblk + b);
+          if (NM == 2) {
+            cw[NM - 1][r][j] = ld_stream_u4(w2.codes + (size_t)row * rstride + (size_t)b * 16);
+            hw[NM - 1][r][j] = __ldg(w2.scales + (size_t)row * nblk + b);
+          }
+        } else {
+          cw[0][r][j] = make_uint4(0u, 0u, 0u, 0u);
+          hw[0][r][j] = 0u;
+          if (NM == 2) { cw[NM - 1][r][j] = make_uint4(0u, 0u, 0u, 0u); hw[NM - 1][r][j] = 0u; }
+        }
+      }
+    }
+  };
+  pdl_trigger();
+  if (g < ngroups) load_group(g);   // weight loads are in flight while the predecessor drains
+  pdl_wait();
+
+  {
     const int4 *src = reinterpret_cast<const int4 *>(act.q);
     int4 *dst = reinterpret_cast<int4 *>(xw);
     for (int i = threadIdx.x; i < NT * (K >> 4); i += GEMV_THREADS) dst[i] = src[i];
@@ -82,115 +196,208 @@ k_gemv(DevQ4B w, DevQ4B w2, DevAct act, float *__restrict__ y, int ldy, uint32_t
   }
   __syncthreads();
 
-  const int lane = threadIdx.x & 31;
-  const int warp = threadIdx.x >> 5;
-  const size_t rstride = (size_t)(K >> 1);
-  for (int row = blockIdx.x * GEMV_WARPS + warp; row < w.rows; row += gridDim.x * GEMV_WARPS) {
-    int64_t acc[NT], acc2[NT];
+  float lmax[NT];
+  unsigned long long lkey[NT];   // greedy argmax: orderable (value, ~row) key per token
 #pragma unroll
-    for (int t = 0; t < NT; t++) { acc[t] = 0; acc2[t] = 0; }
-    const uint8_t *crow = w.codes + (size_t)row * rstride;
-    const uint16_t *srow = w.scales + (size_t)row * nblk;
-    const uint8_t *crow2 = nullptr;
-    const uint16_t *srow2 = nullptr;
-    if (EPI != EPI_STORE) {
-      crow2 = w2.codes + (size_t)row * rstride;
-      srow2 = w2.scales + (size_t)row * nblk;
-    }
-#pragma unroll 4
-    for (int b = lane; b < nblk; b += 32) {
-      const uint4 cw = ld_stream_u4(crow + (size_t)b * 16);
-      const uint32_t h = __ldg(srow + b);
-      uint4 cw2;
-      uint32_t h2 = 0;
+  for (int t = 0; t < NT; t++) { lmax[t] = 0.0f; lkey[t] = 0ull; }
+  // deferred epilogue: lane j keeps the j-th reduced output of this warp until 32 are
+  // pending, then all lanes convert (and apply GELU/SiLU * up) in parallel
+  int64_t pa = 0, pa2 = 0;
+  int prow = -1, ptok = 0, npend = 0;
+  auto flush = [&]() {
+    if (prow >= 0) {
+      const double d = dsc[ptok];
+      float v = __double2float_rn(__dmul_rn(__ll2double_rn(pa), d));
       if (EPI != EPI_STORE) {
-        cw2 = ld_stream_u4(crow2 + (size_t)b * 16);
-        h2 = __ldg(srow2 + b);
+        const float u = __double2float_rn(__dmul_rn(__ll2double_rn(pa2), d));
+        if (!(fabsf(v) < 2048.0f)) { raise_err(err, ERR_ACT_RANGE); v = 0.0f; }
+        const float gv = (EPI == EPI_GELU_MUL) ? gelu_exact(v) : silu_exact(v);
+        v = __fmul_rn(gv, u);
       }
+      y[(size_t)ptok * ldy + prow] = v;
+      const unsigned long long key = argmax_key(v, prow);
+#pragma unroll
+      for (int t = 0; t < NT; t++)
+        if (ptok == t) {
+          lmax[t] = fmaxf(lmax[t], fabsf(v));
+          if (key > lkey[t]) lkey[t] = key;
+        }
+    }
+    prow = -1;
+    npend = 0;
+  };
+
+  for (; g < ngroups; g += gstride) {
+    int64_t acc[NM][RPW][NT];
+#pragma unroll
+    for (int m = 0; m < NM; m++)
+#pragma unroll
+      for (int r = 0; r < RPW; r++)
+#pragma unroll
+        for (int t = 0; t < NT; t++) acc[m][r][t] = 0;
+#pragma unroll
+    for (int j = 0; j < NCH; j++) {
+      const int b = lane + 32 * j;
+      if (b < nblk) {
+#pragma unroll
+        for (int t = 0; t < NT; t++) {
+          const int4 *xb = reinterpret_cast<const int4 *>(xw + t * kw + b * 8);
+          const int4 x0 = xb[0], x1 = xb[1];
+          const int32_t corr = -8 * xs[t * nblk + b];
+#pragma unroll
+          for (int m = 0; m < NM; m++)
+#pragma unroll
+            for (int r = 0; r < RPW; r++)
+              scale_acc(acc[m][r][t], hw[m][r][j], block_dot(cw[m][r][j], x0, x1) + corr);
+        }
+      }
+    }
+    const int g0 = g;
+    if (g + gstride < ngroups) load_group(g + gstride);   // next group's loads overlap the reduction
+#pragma unroll
+    for (int r = 0; r < RPW; r++) {
+      const int row = g0 * RPW + r;
 #pragma unroll
       for (int t = 0; t < NT; t++) {
-        const int32_t *xb = xw + t * kw + b * 8;
-        const int32_t corr = -8 * xs[t * nblk + b];
-        acc[t] += scale_term(h, block_dot(cw, xb) + corr);
-        if (EPI != EPI_STORE) acc2[t] += scale_term(h2, block_dot(cw2, xb) + corr);
+#pragma unroll
+        for (int m = 0; m < NM; m++) acc[m][r][t] = warp_sum_i64(acc[m][r][t]);
+        if (lane == npend && row < rows) {
+          pa = acc[0][r][t];
+          pa2 = acc[NM - 1][r][t];
+          prow = row;
+          ptok = t;
+        }
+        if (++npend == 32) flush();
       }
     }
+  }
+  flush();
+  if (ymax) {   // per-token max |y| of this CTA -> one atomic per token
 #pragma unroll
     for (int t = 0; t < NT; t++) {
-      acc[t] = warp_sum_i64(acc[t]);
-      if (EPI != EPI_STORE) acc2[t] = warp_sum_i64(acc2[t]);
+      const float mt = warp_max_f(lmax[t]);   // every lane owns outputs after the deferred epilogue
+      if (lane == 0) wmax[warp][t] = mt;
     }
-    if (lane < NT) {
-      int64_t a = acc[0], a2 = acc2[0];
+    __syncthreads();
+    if (threadIdx.x < NT) {
+      float m = 0.0f;
+      for (int i = 0; i < GEMV_WARPS; i++) m = fmaxf(m, wmax[i][threadIdx.x]);
+      if (!(m <= 3.402823466e38f)) raise_err(err, ERR_ACT_RANGE);
+      else atomicMax(ymax + threadIdx.x, __float_as_uint(m));
+    }
+  }
+  if (amax) {   // per-token greedy argmax of this CTA -> one 64-bit atomic per token
+    __shared__ unsigned long long wkey[GEMV_WARPS][NT];
 #pragma unroll
-      for (int t = 1; t < NT; t++)
-        if (lane == t) { a = acc[t]; a2 = acc2[t]; }
-      const double d = dsc[lane];
-      float v = __double2float_rn(__dmul_rn(__ll2double_rn(a), d));
-      if (EPI != EPI_STORE) {
-        float u = __double2float_rn(__dmul_rn(__ll2double_rn(a2), d));
-        if (!(fabsf(v) < 2048.0f)) { raise_err(err, ERR_ACT_RANGE); v = 0.0f; }
-        float g = (EPI == EPI_GELU_MUL) ? gelu_exact(v) : silu_exact(v);
-        v = __fmul_rn(g, u);
+    for (int t = 0; t < NT; t++) {
+      unsigned long long k = lkey[t];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long ok = __shfl_xor_sync(0xffffffffu, k, o);
+        k = ok > k ? ok : k;
       }
-      y[(size_t)lane * ldy + row] = v;
+      if (lane == 0) wkey[warp][t] = k;
+    }
+    __syncthreads();
+    if (threadIdx.x < NT) {
+      unsigned long long k = 0ull;
+      for (int i = 0; i < GEMV_WARPS; i++) k = wkey[i][threadIdx.x] > k ? wkey[i][threadIdx.x] : k;
+      atomicMax(amax + threadIdx.x, k);
     }
   }
 }
 
-template <int NT, int EPI>
-static cudaError_t gemv_dispatch(const DevQ4B &w, const DevQ4B &w2, const DevAct &act, float *y, int ldy,
-                                 uint32_t *err, cudaStream_t st, int grid_limit) {
+template <int NT, int EPI, int NCH, int RPW>
+static cudaError_t gemv_launch(const DevQ4B &w, const DevQ4B &w2, const DevAct &act, float *y, int ldy,
+                               uint32_t *err, uint32_t *ymax, unsigned long long *amax, cudaStream_t st,
+                               int grid_limit) {
   const int K = w.cols, nblk = K >> 5;
-  size_t smem = (size_t)NT * K + (size_t)(((NT * nblk + 1) & ~1)) * 4 + (size_t)NT * 8;
-  auto kern = k_gemv<NT, EPI>;
+  const size_t smem = (size_t)NT * K + (size_t)(((NT * nblk + 1) & ~1)) * 4 + (size_t)NT * 8;
+  auto kern = k_gemv<NT, EPI, NCH, RPW>;
+  static int occ = 0, nsm = 0;
+  static size_t occ_smem = 0;
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
   }
-  int grid = (w.rows + GEMV_WARPS - 1) / GEMV_WARPS;
+  if (occ == 0 || occ_smem != smem) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, GEMV_THREADS, smem);
+    if (occ < 1) occ = 1;
+    occ_smem = smem;
+  }
+  const int ngroups = (w.rows + RPW - 1) / RPW;
+  int grid = (ngroups + GEMV_WARPS - 1) / GEMV_WARPS;
+  const int resident = nsm * occ;
+  if (grid > resident) grid = resident;       // persistent: each warp walks several groups
   if (grid_limit > 0 && grid > grid_limit) grid = grid_limit;
-  kern<<<grid, GEMV_THREADS, smem, st>>>(w, w2, act, y, ldy, err);
-  return cudaGetLastError();
+  return launch_k(kern, dim3(grid), dim3(GEMV_THREADS), smem, st, 1, w, w2, act, y, ldy, err, ymax, amax);
+}
+
+// rows per warp group: keep ~16 vectors of 16 bytes per lane in flight
+template <int NT, int EPI, int NCH>
+static cudaError_t gemv_rpw(const DevQ4B &w, const DevQ4B &w2, const DevAct &act, float *y, int ldy,
+                            uint32_t *err, uint32_t *ymax, unsigned long long *amax, cudaStream_t st,
+                            int grid_limit) {
+  constexpr int NM = (EPI == EPI_STORE) ? 1 : 2;
+  constexpr int R0 = 16 / (NCH * NM);
+  constexpr int RPW = NT > 1 ? 1 : (R0 < 1 ? 1 : (R0 > 4 ? 4 : R0));
+  return gemv_launch<NT, EPI, NCH, RPW>(w, w2, act, y, ldy, err, ymax, amax, st, grid_limit);
+}
+
+template <int NT, int EPI>
+static cudaError_t gemv_nch(const DevQ4B &w, const DevQ4B &w2, const DevAct &act, float *y, int ldy,
+                            uint32_t *err, uint32_t *ymax, unsigned long long *amax, cudaStream_t st,
+                            int grid_limit) {
+  const int per_lane = ((w.cols >> 5) + 31) / 32;
+  if (per_lane <= 1) return gemv_rpw<NT, EPI, 1>(w, w2, act, y, ldy, err, ymax, amax, st, grid_limit);
+  if (per_lane <= 4) return gemv_rpw<NT, EPI, 4>(w, w2, act, y, ldy, err, ymax, amax, st, grid_limit);
+  if (per_lane <= 16) return gemv_rpw<NT, EPI, 16>(w, w2, act, y, ldy, err, ymax, amax, st, grid_limit);
+  return cudaErrorInvalidValue;
 }
 
 template <int EPI>
 static cudaError_t gemv_nt(const DevQ4B &w, const DevQ4B &w2, const DevAct &act, int ntok, float *y, int ldy,
-                           uint32_t *err, cudaStream_t st, int grid_limit) {
+                           uint32_t *err, uint32_t *ymax, unsigned long long *amax, cudaStream_t st,
+                           int grid_limit) {
   switch (ntok) {
-    case 1: return gemv_dispatch<1, EPI>(w, w2, act, y, ldy, err, st, grid_limit);
-    case 2: return gemv_dispatch<2, EPI>(w, w2, act, y, ldy, err, st, grid_limit);
-    case 4: return gemv_dispatch<4, EPI>(w, w2, act, y, ldy, err, st, grid_limit);
-    case 8: return gemv_dispatch<8, EPI>(w, w2, act, y, ldy, err, st, grid_limit);
-    case 16: return gemv_dispatch<16, EPI>(w, w2, act, y, ldy, err, st, grid_limit);
+    case 1: return gemv_nch<1, EPI>(w, w2, act, y, ldy, err, ymax, amax, st, grid_limit);
+    case 2: return gemv_nch<2, EPI>(w, w2, act, y, ldy, err, ymax, amax, st, grid_limit);
+    case 4: return gemv_nch<4, EPI>(w, w2, act, y, ldy, err, ymax, amax, st, grid_limit);
+    case 8: return gemv_nch<8, EPI>(w, w2, act, y, ldy, err, ymax, amax, st, grid_limit);
+    case 16: return gemv_nch<16, EPI>(w, w2, act, y, ldy, err, ymax, amax, st, grid_limit);
     default: return cudaErrorInvalidValue;
   }
 }
 
 cudaError_t launch_gemv(const DevQ4B &w, const DevQ4B *w2, const DevAct &act, int ntok, float *y, int ldy,
-                        int epi, uint32_t *err, cudaStream_t st, int grid_limit) {
-  if ((w.cols & 31) || w.cols <= 0 || w.rows <= 0) return cudaErrorInvalidValue;
+                        int epi, uint32_t *err, cudaStream_t st, int grid_limit, uint32_t *ymax,
+                        unsigned long long *amax) {
+  if ((w.cols & 31) || w.cols <= 0 || w.rows <= 0 || w.cols > 16384) return cudaErrorInvalidValue;
   if (epi != EPI_STORE && (!w2 || w2->rows != w.rows || w2->cols != w.cols)) return cudaErrorInvalidValue;
   // the staged activations of all rows must fit shared memory: split the token rows
   const size_t per_tok = (size_t)w.cols + (size_t)(w.cols >> 5) * 4 + 8;
   if (ntok > 1 && per_tok * ntok > 160 * 1024) {
     const int h = ntok / 2;
     const DevAct a2{act.q + (size_t)h * w.cols, act.bsum + (size_t)h * (w.cols >> 5), act.scale + h};
-    cudaError_t e = launch_gemv(w, w2, act, h, y, ldy, epi, err, st, grid_limit);
+    cudaError_t e = launch_gemv(w, w2, act, h, y, ldy, epi, err, st, grid_limit, ymax, amax);
     if (e != cudaSuccess) return e;
-    return launch_gemv(w, w2, a2, h, y + (size_t)h * ldy, ldy, epi, err, st, grid_limit);
+    return launch_gemv(w, w2, a2, h, y + (size_t)h * ldy, ldy, epi, err, st, grid_limit, ymax ? ymax + h : nullptr,
+                       amax ? amax + h : nullptr);
   }
   const DevQ4B ww2 = w2 ? *w2 : w;
   switch (epi) {
-    case EPI_STORE: return gemv_nt<EPI_STORE>(w, ww2, act, ntok, y, ldy, err, st, grid_limit);
-    case EPI_GELU_MUL: return gemv_nt<EPI_GELU_MUL>(w, ww2, act, ntok, y, ldy, err, st, grid_limit);
-    case EPI_SILU_MUL: return gemv_nt<EPI_SILU_MUL>(w, ww2, act, ntok, y, ldy, err, st, grid_limit);
+    case EPI_STORE: return gemv_nt<EPI_STORE>(w, ww2, act, ntok, y, ldy, err, ymax, amax, st, grid_limit);
+    case EPI_GELU_MUL: return gemv_nt<EPI_GELU_MUL>(w, ww2, act, ntok, y, ldy, err, ymax, amax, st, grid_limit);
+    case EPI_SILU_MUL: return gemv_nt<EPI_SILU_MUL>(w, ww2, act, ntok, y, ldy, err, ymax, amax, st, grid_limit);
     default: return cudaErrorInvalidValue;
   }
 }
 
 // ------------------------------------------------------------------------------ quantizer
-constexpr int QUANT_THREADS = 1024;
+constexpr int QUANT_THREADS = 256;
 
 // interleaved byte position of column c inside its 32-column block
 __device__ __forceinline__ int perm_pos(int c) {
@@ -213,7 +420,19 @@ __device__ float block_max(float v, float *red) {
   return red[32];
 }
 
-// quantize n (multiple of 32) values from src (shared or global) into one act row
+// quantize one row of K (multiple of 32) values with a known scale s, one warp per block
+__device__ __forceinline__ void quant_blocks(const float *src, int K, float s, int8_t *q, int32_t *bsum,
+                                             int b0, int bstride) {
+  const int lane = threadIdx.x & 31;
+  for (int b = b0; b < (K >> 5); b += bstride) {
+    const int32_t v = quant1(src[(b << 5) + lane], s);
+    q[(b << 5) + perm_pos(lane)] = (int8_t)v;
+    const int32_t sum = warp_sum_i32(v);
+    if (lane == 0) bsum[b] = sum;
+  }
+}
+
+// a whole row in one CTA: max, then quantize (used inside k_norm)
 __device__ void quant_row(const float *src, int K, int8_t *q, int32_t *bsum, float *scale_out, float *red,
                           uint32_t *err) {
   float m = 0.0f;
@@ -225,30 +444,52 @@ __device__ void quant_row(const float *src, int K, int8_t *q, int32_t *bsum, flo
   }
   if (bad) raise_err(err, ERR_ACT_RANGE);
   const float s = block_max(m, red);
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  for (int b = warp; b < (K >> 5); b += nw) {
-    const int c = (b << 5) + lane;
-    const int32_t v = quant1(src[c], s);
-    q[(b << 5) + perm_pos(lane)] = (int8_t)v;
-    const int32_t sum = warp_sum_i32(v);
-    if (lane == 0) bsum[b] = sum;
-  }
+  quant_blocks(src, K, s, q, bsum, threadIdx.x >> 5, blockDim.x >> 5);
   if (threadIdx.x == 0) *scale_out = s;
 }
 
-__global__ void __launch_bounds__(QUANT_THREADS)
-k_quant(const float *u, int ldu, int K, DevAct act, uint32_t *err) {
+// per-row max |u| into slot[t] (f32 bits), for callers without a producing kernel
+__global__ void __launch_bounds__(1024) k_rowmax(const float *u, int ldu, int K, uint32_t *slot, uint32_t *err) {
   __shared__ float red[33];
+  pdl_trigger();
+  pdl_wait();
   const int t = blockIdx.x;
-  quant_row(u + (size_t)t * ldu, K, act.q + (size_t)t * K, act.bsum + (size_t)t * (K >> 5), act.scale + t,
-            red, err);
+  float m = 0.0f;
+  bool bad = false;
+  for (int i = threadIdx.x; i < K; i += blockDim.x) {
+    const float a = fabsf(u[(size_t)t * ldu + i]);
+    if (!(a <= 3.402823466e38f)) bad = true;
+    else m = fmaxf(m, a);
+  }
+  if (bad) raise_err(err, ERR_ACT_RANGE);
+  m = block_max(m, red);
+  if (threadIdx.x == 0) slot[t] = __float_as_uint(m);
 }
 
-cudaError_t launch_quant(const float *u, int ldu, int K, int ntok, const DevAct &act, uint32_t *err,
-                         cudaStream_t st) {
+// grid (ceil(nblk/8), ntok): warp w of CTA x quantizes block 8x+w with the row's max
+__global__ void __launch_bounds__(QUANT_THREADS)
+k_quant_blocks(const float *u, int ldu, int K, const uint32_t *maxslot, DevAct act) {
+  pdl_trigger();
+  pdl_wait();
+  const int t = blockIdx.y;
+  const float s = __uint_as_float(maxslot[t]);
+  const int b = blockIdx.x * (QUANT_THREADS / 32) + (threadIdx.x >> 5);
+  if (b < (K >> 5))
+    quant_blocks(u + (size_t)t * ldu, K, s, act.q + (size_t)t * K, act.bsum + (size_t)t * (K >> 5), b, 1 << 30);
+  if (blockIdx.x == 0 && threadIdx.x == 0) act.scale[t] = s;
+}
+
+cudaError_t launch_quant(const float *u, int ldu, int K, int ntok, const DevAct &act, const uint32_t *maxslot,
+                         uint32_t *err, cudaStream_t st) {
   if (K & 31) return cudaErrorInvalidValue;
-  k_quant<<<ntok, QUANT_THREADS, 0, st>>>(u, ldu, K, act, err);
-  return cudaGetLastError();
+  if (!maxslot) {   // no producer max: compute it into act.scale (as f32 bits) first
+    uint32_t *slot = reinterpret_cast<uint32_t *>(act.scale);
+    cudaError_t e = launch_k(k_rowmax, dim3(ntok), dim3(1024), 0, st, 1, u, ldu, K, slot, err);
+    if (e != cudaSuccess) return e;
+    maxslot = slot;
+  }
+  dim3 grid(((K >> 5) + QUANT_THREADS / 32 - 1) / (QUANT_THREADS / 32), ntok);
+  return launch_k(k_quant_blocks, grid, dim3(QUANT_THREADS), 0, st, 1, u, ldu, K, maxslot, act);
 }
 
 // ------------------------------------------------------------------------------ RMSNorm
@@ -280,51 +521,146 @@ __device__ acc128 block_sum128(acc128 v, acc128 *red) {
   return red[32];
 }
 
-// Exact RMSNorm island over n values (any thread count): dst may alias nothing in src.
-__device__ void block_rmsnorm(const float *src, const float *w, int n, float *dst, acc128 *red,
-                              uint64_t *inv_sh, uint32_t *err) {
+// island pieces: per-thread partial sum of (q16(x))^2, the inverse rms from the exact total,
+// and one output y = (float)((double)(int64)(xi * inv * wi) * 2^-52) (exact_islands.c:60-79)
+__device__ __forceinline__ acc128 rms_partial(const float *src, int n, uint32_t *err) {
   acc128 ss{0ull, 0ll};
   bool bad = false;
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
     const float x = src[i];
-    if (!(fabsf(x) < 32768.0f)) bad = true;
-    const int64_t xi = bad ? 0 : llround_d((double)x * 65536.0);
+    if (!(fabsf(x) < 32768.0f)) { bad = true; continue; }
+    const int64_t xi = q16_round(x);
     acc128_add(ss, xi * xi);
   }
-  const acc128 tot = block_sum128(ss, red);
-  if (threadIdx.x == 0) {
-    uint64_t inv = 0;
-    if (tot.hi != 0 || (tot.lo >> 63)) {
-      raise_err(err, ERR_NORM_RANGE);
-    } else if (tot.lo != 0) {
-      inv = isqrt_u64(rms_quotient((uint32_t)n, tot.lo));
-    }
-    *inv_sh = inv;
-  }
   if (bad) raise_err(err, ERR_NORM_RANGE);
+  return ss;
+}
+
+__device__ __forceinline__ uint64_t rms_inv(const acc128 &tot, int n, uint32_t *err) {
+  if (tot.hi != 0 || (tot.lo >> 63)) {
+    raise_err(err, ERR_NORM_RANGE);
+    return 0;
+  }
+  return tot.lo ? isqrt_u64(rms_quotient((uint32_t)n, tot.lo)) : 0ull;
+}
+
+__device__ __forceinline__ float rms_apply(float x, float w, uint64_t inv, uint32_t *err) {
+  if (!(fabsf(w) < 32768.0f)) { raise_err(err, ERR_NORM_RANGE); w = 0.0f; }
+  const int64_t xi = q16_round(fabsf(x) < 32768.0f ? x : 0.0f), wi = q16_round(w);
+  const int64_t yi = (int64_t)((uint64_t)xi * inv * (uint64_t)wi);
+  return __double2float_rn(__dmul_rn(__ll2double_rn(yi), 0x1p-52));
+}
+
+// Exact RMSNorm island over n values in one CTA (any thread count); dst must not alias src.
+__device__ void block_rmsnorm(const float *src, const float *w, int n, float *dst, acc128 *red,
+                              uint64_t *inv_sh, uint32_t *err) {
+  const acc128 tot = block_sum128(rms_partial(src, n, err), red);
+  if (threadIdx.x == 0) *inv_sh = rms_inv(tot, n, err);
   __syncthreads();
   const uint64_t inv = *inv_sh;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    const int64_t xi = llround_d((double)src[i] * 65536.0);
-    const int64_t wi = llround_d((double)w[i] * 65536.0);
-    const int64_t yi = (int64_t)((uint64_t)xi * inv * (uint64_t)wi);
-    dst[i] = __double2float_rn(__dmul_rn(__ll2double_rn(yi), 0x1p-52));
-  }
+  for (int i = threadIdx.x; i < n; i += blockDim.x) dst[i] = rms_apply(src[i], w[i], inv, err);
   __syncthreads();
 }
 
+// ---- norm block as one 8-CTA cluster per token row: each CTA owns E/8 columns, the
+// exact sums of squares and the quantizer's max are exchanged through DSMEM.
+constexpr int NORM_CL = 8;
+constexpr int NORM_CL_THREADS = 256;
+
+__global__ void __launch_bounds__(NORM_CL_THREADS)
+k_norm_cl(float *x, const float *add, const float *add_w, const float *out_w, int E, DevAct act, float *nx_out,
+          uint32_t *err, uint32_t *zero_slot) {
+  cg::cluster_group cluster = cg::this_cluster();
+  extern __shared__ __align__(16) float csm[];
+  const int ns = E / NORM_CL;
+  float *xb = csm;        // [ns] residual slice after the add
+  float *nb = csm + ns;   // [ns] normed slice
+  __shared__ acc128 red[33];
+  __shared__ acc128 part[2];
+  __shared__ float fred[33];
+  __shared__ float mx_loc;
+  __shared__ float s_all;
+  __shared__ uint64_t inv_sh;
+  const int rank = (int)cluster.block_rank();
+  const int t = blockIdx.y;
+  const int off = rank * ns;
+  pdl_trigger();
+  pdl_wait();
+  if (zero_slot && rank == 0 && threadIdx.x == 0) zero_slot[t] = 0u;
+  float *xr = x + (size_t)t * E + off;
+  if (add) {
+    const float *ar = add + (size_t)t * E + off;
+    if (add_w) {   // sandwich post-norm of `add`, then the residual add
+      const acc128 p = block_sum128(rms_partial(ar, ns, err), red);
+      if (threadIdx.x == 0) part[0] = p;
+      cluster.sync();
+      if (threadIdx.x == 0) {
+        acc128 tot{0ull, 0ll};
+        for (int r = 0; r < NORM_CL; r++) acc128_add(tot, *cluster.map_shared_rank(&part[0], r));
+        inv_sh = rms_inv(tot, E, err);
+      }
+      __syncthreads();
+      const uint64_t inv = inv_sh;
+      for (int i = threadIdx.x; i < ns; i += blockDim.x)
+        xb[i] = __fadd_rn(xr[i], rms_apply(ar[i], add_w[off + i], inv, err));
+    } else {
+      for (int i = threadIdx.x; i < ns; i += blockDim.x) xb[i] = __fadd_rn(xr[i], ar[i]);
+    }
+    for (int i = threadIdx.x; i < ns; i += blockDim.x) xr[i] = xb[i];
+  } else {
+    for (int i = threadIdx.x; i < ns; i += blockDim.x) xb[i] = xr[i];
+  }
+  __syncthreads();
+  {
+    const acc128 p = block_sum128(rms_partial(xb, ns, err), red);
+    if (threadIdx.x == 0) part[1] = p;
+  }
+  cluster.sync();
+  if (threadIdx.x == 0) {
+    acc128 tot{0ull, 0ll};
+    for (int r = 0; r < NORM_CL; r++) acc128_add(tot, *cluster.map_shared_rank(&part[1], r));
+    inv_sh = rms_inv(tot, E, err);
+  }
+  __syncthreads();
+  const uint64_t inv = inv_sh;
+  float m = 0.0f;
+  for (int i = threadIdx.x; i < ns; i += blockDim.x) {
+    const float v = rms_apply(xb[i], out_w[off + i], inv, err);
+    nb[i] = v;
+    m = fmaxf(m, fabsf(v));
+    if (nx_out) nx_out[(size_t)t * E + off + i] = v;
+  }
+  m = block_max(m, fred);
+  if (threadIdx.x == 0) mx_loc = m;
+  cluster.sync();
+  if (threadIdx.x == 0) {
+    float s = 0.0f;
+    for (int r = 0; r < NORM_CL; r++) s = fmaxf(s, *cluster.map_shared_rank(&mx_loc, r));
+    s_all = s;
+    if (rank == 0) act.scale[t] = s;
+  }
+  __syncthreads();
+  quant_blocks(nb, ns, s_all, act.q + (size_t)t * E + off, act.bsum + (size_t)t * (E >> 5) + (off >> 5),
+               threadIdx.x >> 5, blockDim.x >> 5);
+  cluster.sync();   // remote CTAs may still be reading this CTA's shared memory
+}
+
+// single-CTA fallback for widths that do not split into 8 slices of 32-column blocks
 constexpr int NORM_THREADS = 1024;
 
 __global__ void __launch_bounds__(NORM_THREADS)
 k_norm(float *x, const float *add, const float *add_w, const float *out_w, int E, DevAct act, float *nx_out,
-       uint32_t *err) {
+       uint32_t *err, uint32_t *zero_slot) {
   extern __shared__ __align__(16) float nsm[];
   float *tbuf = nsm;          // [E]
   float *nbuf = nsm + E;      // [E]
   __shared__ acc128 red[33];
   __shared__ uint64_t inv_sh;
   __shared__ float fred[33];
+  pdl_trigger();
+  pdl_wait();
   const int t = blockIdx.x;
+  if (zero_slot && threadIdx.x == 0) zero_slot[t] = 0u;
   float *xr = x + (size_t)t * E;
   if (add) {
     const float *ar = add + (size_t)t * E;
@@ -343,15 +679,20 @@ k_norm(float *x, const float *add, const float *add_w, const float *out_w, int E
 }
 
 cudaError_t launch_norm(float *x, const float *add, const float *add_w, const float *out_w, int E, int ntok,
-                        const DevAct &act, float *nx_out, uint32_t *err, cudaStream_t st) {
+                        const DevAct &act, float *nx_out, uint32_t *err, cudaStream_t st, uint32_t *zero_slot) {
   if (E & 31) return cudaErrorInvalidValue;
+  if (E % (NORM_CL * 32) == 0) {
+    const size_t smem = (size_t)2 * (E / NORM_CL) * sizeof(float);
+    return launch_k(k_norm_cl, dim3(NORM_CL, ntok), dim3(NORM_CL_THREADS), smem, st, NORM_CL, x, add, add_w, out_w,
+                    E, act, nx_out, err, zero_slot);
+  }
   const size_t smem = (size_t)2 * E * sizeof(float);
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(k_norm, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
   }
-  k_norm<<<ntok, NORM_THREADS, smem, st>>>(x, add, add_w, out_w, E, act, nx_out, err);
-  return cudaGetLastError();
+  return launch_k(k_norm, dim3(ntok), dim3(NORM_THREADS), smem, st, 1, x, add, add_w, out_w, E, act, nx_out, err,
+                  zero_slot);
 }
 
 // ------------------------------------------------------------------------------ RoPE + KV
@@ -397,11 +738,14 @@ __global__ void k_rope_kv(RopeArgs a) {
   float *nbuf = rsm + a.HD;     // [HD] normed
   __shared__ acc128 red[33];
   __shared__ uint64_t inv_sh;
+  pdl_trigger();
+  pdl_wait();
   const int head = blockIdx.x, t = blockIdx.y;
   const int HD = a.HD, half = HD >> 1, QD = a.NH * HD, KVD = a.NKV * HD;
   const float *row = a.qkv + (size_t)t * (QD + 2 * KVD);
   const int p = a.pos_dev[0] + t;
   const int i = threadIdx.x;   // pair index, blockDim.x == half
+  if (a.zero_slot && head == 0 && i == 0) a.zero_slot[t] = 0u;
   if (head >= a.NH + a.NKV) {  // V head: quantize to the 2^16 grid
     const int g = head - a.NH - a.NKV;
     const float *src = row + QD + KVD + g * HD;
@@ -439,27 +783,36 @@ __global__ void k_rope_kv(RopeArgs a) {
 cudaError_t launch_rope_kv(const RopeArgs &a, cudaStream_t st) {
   if (a.HD & 1 || a.HD / 2 > 1024) return cudaErrorInvalidValue;
   dim3 grid(a.NH + 2 * a.NKV, a.ntok);
-  k_rope_kv<<<grid, a.HD / 2, 2 * a.HD * sizeof(float), st>>>(a);
-  return cudaGetLastError();
+  return launch_k(k_rope_kv, grid, dim3(a.HD / 2), 2 * a.HD * sizeof(float), st, 1, a);
 }
 
 // ------------------------------------------------------------------------------ attention
-constexpr int ATTN_CL = 8;         // CTAs per cluster (portable size)
 constexpr int ATTN_THREADS = 256;
+constexpr int ATTN_STAGES = 3;
 
-template <int HD, int G>
-__global__ void __cluster_dims__(ATTN_CL, 1, 1) __launch_bounds__(ATTN_THREADS)
-k_attn(AttnArgs a, int cmax) {
+// positions per ring stage (32 KB of int32 K or V per stage)
+template <int HD>
+struct AttnSub {
+  static constexpr int SUB = 8192 / HD;
+};
+
+template <int HD, int G, int CL>
+__global__ void __launch_bounds__(ATTN_THREADS) k_attn(AttnArgs a, int cmax) {
   cg::cluster_group cluster = cg::this_cluster();
-  extern __shared__ __align__(16) uint8_t asm_raw[];
-  constexpr int EPL = HD / 32;                 // q/k elements per lane
+  constexpr int SUB = AttnSub<HD>::SUB;
+  constexpr int EPL = HD / 32;                 // q/k elements per lane in the score dot
   constexpr int GROUPS = ATTN_THREADS / HD;    // position groups in the V-sum
-  int32_t *qs = reinterpret_cast<int32_t *>(asm_raw);        // [G][HD]
-  int32_t *sc = qs + G * HD;                                  // [G][cmax] scores, then e
+  constexpr int DPR = HD / CL;                 // head dims each rank finalizes
+  extern __shared__ __align__(128) uint8_t asm_raw[];
+  int32_t *ring = reinterpret_cast<int32_t *>(asm_raw);            // [STAGES][SUB*HD]
+  int32_t *qs = ring + ATTN_STAGES * SUB * HD;                       // [G][HD]
+  int32_t *sc = qs + G * HD;                                         // [G][cmax] scores, then e
   acc128 *nacc = reinterpret_cast<acc128 *>(sc + ((G * cmax + 3) & ~3));  // [GROUPS][G][HD]
-  __shared__ int32_t mx_loc[8];
-  __shared__ int64_t s_loc[8];
-  __shared__ int32_t mx_all[8];
+  __shared__ __align__(8) uint64_t full[ATTN_STAGES];
+  __shared__ int32_t mx_loc[G];
+  __shared__ int64_t s_loc[G];
+  __shared__ int32_t mx_all[G];
+  __shared__ float fred[33];
 
   const int rank = (int)cluster.block_rank();
   const int g = blockIdx.y, t = blockIdx.z;
@@ -467,58 +820,89 @@ k_attn(AttnArgs a, int cmax) {
   const int p = a.pos_dev[0] + t;
   const int s0 = (a.win >= 0 && p - a.win + 1 > 0) ? p - a.win + 1 : 0;
   const int n = p - s0 + 1;
-  const int c = (n + ATTN_CL - 1) / ATTN_CL;
+  const int c = (n + CL - 1) / CL;
   const int c0 = s0 + rank * c;
   const int c1 = min(c0 + c, p + 1);
   const int cn = max(c1 - c0, 0);
+  const int nsub = (cn + SUB - 1) / SUB;
+  const int total = 2 * nsub;                 // K slices, then V slices
   const int32_t *kbase = a.kc + (size_t)g * a.P * HD;
   const int32_t *vbase = a.vc + (size_t)g * a.P * HD;
-
-  for (int i = threadIdx.x; i < G * HD; i += ATTN_THREADS) qs[i] = a.qi[(size_t)t * QD + (size_t)g * G * HD + i];
-  if (threadIdx.x < 8) { mx_loc[threadIdx.x] = INT32_MIN; s_loc[threadIdx.x] = 0; }
-  __syncthreads();
-
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  // ---- phase 1: exact scores -> 2^14 grid
-  for (int pp = c0 + warp; pp < c1; pp += ATTN_THREADS / 32) {
-    const int32_t *kr = kbase + (size_t)pp * HD + lane * EPL;
-    int32_t kv[EPL];
-    if constexpr (EPL == 8) {
-      const int4 u0 = *reinterpret_cast<const int4 *>(kr);
-      const int4 u1 = *reinterpret_cast<const int4 *>(kr + 4);
-      kv[0] = u0.x; kv[1] = u0.y; kv[2] = u0.z; kv[3] = u0.w;
-      kv[4] = u1.x; kv[5] = u1.y; kv[6] = u1.z; kv[7] = u1.w;
-    } else if constexpr (EPL == 4) {
-      const int4 u0 = *reinterpret_cast<const int4 *>(kr);
-      kv[0] = u0.x; kv[1] = u0.y; kv[2] = u0.z; kv[3] = u0.w;
-    } else {
+
+  auto issue = [&](int i) {                   // one bulk copy: slice i -> ring stage i % STAGES
+    const int j = i < nsub ? i : i - nsub;
+    const int pos = c0 + j * SUB;
+    const int len = min(SUB, c1 - pos);
+    const uint32_t bytes = (uint32_t)len * HD * 4;
+    uint64_t *bar = &full[i % ATTN_STAGES];
+    mbar_arrive_expect_tx(bar, bytes);
+    bulk_g2s(ring + (i % ATTN_STAGES) * SUB * HD, (i < nsub ? kbase : vbase) + (size_t)pos * HD, bytes, bar);
+  };
+
+  // K/V rows before this launch's first new position were written by earlier steps, so a
+  // CTA whose slice ends before it can start its copies before the predecessor finishes
+  const bool early = c1 <= a.pos_dev[0];
+  pdl_trigger();
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < ATTN_STAGES; s++) mbar_init(&full[s], 1);
+    mbar_init_fence();
+    if (early)
+      for (int i = 0; i < min(ATTN_STAGES, total); i++) issue(i);
+  }
+  pdl_wait();
+  for (int i = threadIdx.x; i < G * HD; i += ATTN_THREADS) qs[i] = a.qi[(size_t)t * QD + (size_t)g * G * HD + i];
+  if (threadIdx.x < G) { mx_loc[threadIdx.x] = INT32_MIN; s_loc[threadIdx.x] = 0; }
+  __syncthreads();
+  if (threadIdx.x == 0 && !early)
+    for (int i = 0; i < min(ATTN_STAGES, total); i++) issue(i);
+
+  // ---- phase 1: exact scores of this CTA's positions -> the 2^14 grid
+  for (int i = 0; i < nsub; i++) {
+    const int stage = i % ATTN_STAGES;
+    mbar_wait(&full[stage], (uint32_t)(i / ATTN_STAGES) & 1u, a.err);
+    const int32_t *buf = ring + stage * SUB * HD;
+    const int len = min(SUB, cn - i * SUB);
+    for (int pp = warp; pp < len; pp += ATTN_THREADS / 32) {
+      const int32_t *kr = buf + pp * HD + lane * EPL;
+      int32_t kv[EPL];
 #pragma unroll
-      for (int e = 0; e < EPL; e++) kv[e] = kr[e];
-    }
-#pragma unroll
-    for (int h = 0; h < G; h++) {
-      const int32_t *qh = qs + h * HD + lane * EPL;
-      int64_t s = 0;
-#pragma unroll
-      for (int e = 0; e < EPL; e++) s += (int64_t)qh[e] * (int64_t)kv[e];
-      s = warp_sum_i64(s);
-      if (lane == 0) {
-        float z = __fmul_rn(__double2float_rn(__dmul_rn(__ll2double_rn(s), 0x1p-32)), a.ascale);
-        if (!(fabsf(z) < 131072.0f)) { raise_err(a.err, ERR_SCORE_RANGE); z = 0.0f; }
-        const int32_t zi = (int32_t)llround_d((double)z * 16384.0);
-        sc[h * cmax + (pp - c0)] = zi;
-        atomicMax(&mx_loc[h], zi);
+      for (int e = 0; e < EPL; e += 2) {
+        const int2 u = *reinterpret_cast<const int2 *>(kr + e);
+        kv[e] = u.x;
+        kv[e + 1] = u.y;
       }
+#pragma unroll
+      for (int h = 0; h < G; h++) {
+        const int32_t *qh = qs + h * HD + lane * EPL;
+        int64_t s = 0;
+#pragma unroll
+        for (int e = 0; e < EPL; e++) s += (int64_t)qh[e] * (int64_t)kv[e];
+        s = warp_sum_i64(s);
+        if (lane == 0) {
+          float z = __fmul_rn(__double2float_rn(__dmul_rn(__ll2double_rn(s), 0x1p-32)), a.ascale);
+          if (!(fabsf(z) < 131072.0f)) { raise_err(a.err, ERR_SCORE_RANGE); z = 0.0f; }
+          const int32_t zi = (int32_t)llround_d((double)z * 16384.0);
+          sc[h * cmax + i * SUB + pp] = zi;
+          atomicMax(&mx_loc[h], zi);
+        }
+      }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0 && i + ATTN_STAGES < total) {
+      fence_proxy_async_smem();
+      issue(i + ATTN_STAGES);
     }
   }
   cluster.sync();
   if (threadIdx.x < G) {
     int32_t m = INT32_MIN;
-    for (int r = 0; r < ATTN_CL; r++) m = max(m, *cluster.map_shared_rank(&mx_loc[threadIdx.x], r));
+    for (int r = 0; r < CL; r++) m = max(m, *cluster.map_shared_rank(&mx_loc[threadIdx.x], r));
     mx_all[threadIdx.x] = m;
   }
   __syncthreads();
   // ---- phase 2: integer exponentials and their exact sum
+#pragma unroll
   for (int h = 0; h < G; h++) {
     int64_t part = 0;
     for (int j = threadIdx.x; j < cn; j += ATTN_THREADS) {
@@ -531,21 +915,31 @@ k_attn(AttnArgs a, int cmax) {
     if (lane == 0 && part) atomicAdd(reinterpret_cast<unsigned long long *>(&s_loc[h]), (unsigned long long)part);
   }
   __syncthreads();
-  // ---- phase 3: exact 128-bit V-sum over this CTA's positions
-  {
-    const int d = threadIdx.x % HD, grp = threadIdx.x / HD;
-    acc128 acc[G];
+  // ---- phase 3: exact 128-bit V-sum, V slices streamed through the same ring
+  const int d = threadIdx.x % HD, grp = threadIdx.x / HD;
+  acc128 acc[G];
 #pragma unroll
-    for (int h = 0; h < G; h++) acc[h] = acc128{0ull, 0ll};
+  for (int h = 0; h < G; h++) acc[h] = acc128{0ull, 0ll};
+  for (int i = nsub; i < total; i++) {
+    const int stage = i % ATTN_STAGES;
+    mbar_wait(&full[stage], (uint32_t)(i / ATTN_STAGES) & 1u, a.err);
+    const int32_t *buf = ring + stage * SUB * HD;
+    const int j0 = (i - nsub) * SUB;
+    const int len = min(SUB, cn - j0);
 #pragma unroll 4
-    for (int j = grp; j < cn; j += GROUPS) {
-      const int64_t v = vbase[(size_t)(c0 + j) * HD + d];
+    for (int pp = grp; pp < len; pp += GROUPS) {
+      const int64_t v = buf[pp * HD + d];
 #pragma unroll
-      for (int h = 0; h < G; h++) acc128_add(acc[h], (int64_t)sc[h * cmax + j] * v);
+      for (int h = 0; h < G; h++) acc128_add(acc[h], (int64_t)sc[h * cmax + j0 + pp] * v);
     }
-#pragma unroll
-    for (int h = 0; h < G; h++) nacc[(grp * G + h) * HD + d] = acc[h];
+    __syncthreads();
+    if (threadIdx.x == 0 && i + ATTN_STAGES < total) {
+      fence_proxy_async_smem();
+      issue(i + ATTN_STAGES);
+    }
   }
+#pragma unroll
+  for (int h = 0; h < G; h++) nacc[(grp * G + h) * HD + d] = acc[h];
   __syncthreads();
   if (GROUPS > 1) {
     for (int i = threadIdx.x; i < G * HD; i += ATTN_THREADS) {
@@ -555,51 +949,95 @@ k_attn(AttnArgs a, int cmax) {
     }
   }
   cluster.sync();
-  // ---- phase 4: combine partials across the cluster; rank r finalizes HD/CL dims
-  {
-    constexpr int DPR = HD / ATTN_CL;
-    for (int i = threadIdx.x; i < G * DPR; i += ATTN_THREADS) {
-      const int h = i / DPR, d = rank * DPR + (i % DPR);
-      acc128 N{0ull, 0ll};
-      int64_t S = 0;
-      for (int r = 0; r < ATTN_CL; r++) {
-        acc128_add(N, *cluster.map_shared_rank(&nacc[h * HD + d], r));
-        S += *cluster.map_shared_rank(&s_loc[h], r);
-      }
-      // N * 2^16 (|N| < 2^78 so the shift stays inside 128 bits)
-      const int64_t hi = (int64_t)(((uint64_t)N.hi << 16) | (N.lo >> 48));
-      const uint64_t lo = N.lo << 16;
-      const int64_t qd = floordiv_s128(hi, lo, (uint64_t)S);
-      const float o = __double2float_rn(__dmul_rn(__ll2double_rn(qd), 0x1p-32));
-      a.ao[(size_t)t * QD + ((size_t)g * G + h) * HD + d] = o;
+  // ---- phase 4: combine the cluster's partials; rank r finalizes HD/CL dims per head
+  float omax = 0.0f;
+  for (int i = threadIdx.x; i < G * DPR; i += ATTN_THREADS) {
+    const int h = i / DPR, dd = rank * DPR + (i % DPR);
+    acc128 N{0ull, 0ll};
+    int64_t S = 0;
+    for (int r = 0; r < CL; r++) {
+      acc128_add(N, *cluster.map_shared_rank(&nacc[h * HD + dd], r));
+      S += *cluster.map_shared_rank(&s_loc[h], r);
     }
+    const int64_t hi = (int64_t)(((uint64_t)N.hi << 16) | (N.lo >> 48));   // N * 2^16, |N| < 2^78
+    const uint64_t lo = N.lo << 16;
+    const int64_t qd = floordiv_s128(hi, lo, (uint64_t)S);
+    const float o = __double2float_rn(__dmul_rn(__ll2double_rn(qd), 0x1p-32));
+    a.ao[(size_t)t * QD + ((size_t)g * G + h) * HD + dd] = o;
+    omax = fmaxf(omax, fabsf(o));
+  }
+  if (a.ao_max) {
+    omax = block_max(omax, fred);
+    if (threadIdx.x == 0) atomicMax(a.ao_max + t, __float_as_uint(omax));
   }
   cluster.sync();
 }
 
+template <int HD, int G, int CL>
+static cudaError_t attn_launch(const AttnArgs &a, int cmax, size_t smem, cudaStream_t st) {
+  auto kern = k_attn<HD, G, CL>;
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    if (e != cudaSuccess) return e;
+    if (CL > 8) {
+      e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+      if (e != cudaSuccess) return e;
+    }
+    configured = true;
+  }
+  return launch_k(kern, dim3(CL, a.NKV, a.ntok), dim3(ATTN_THREADS), smem, st, CL, a, cmax);
+}
+
+template <int HD, int G>
+static size_t attn_smem(int cmax) {
+  constexpr int SUB = AttnSub<HD>::SUB;
+  return (size_t)ATTN_STAGES * SUB * HD * 4 + (size_t)G * HD * 4 + (size_t)((G * cmax + 3) & ~3) * 4 +
+         (size_t)(ATTN_THREADS / HD) * G * HD * sizeof(acc128);
+}
+
+template <int HD, int G>
+static cudaError_t attn_cl(const AttnArgs &a, cudaStream_t st) {
+  // 16-CTA clusters where the device can co-schedule them (asked once, before any launch,
+  // so a graph capture never sees a failed launch), else the portable 8
+  static int cl = 0;
+  if (cl == 0) {
+    cl = 8;
+    auto k16 = k_attn<HD, G, 16>;
+    if (cudaFuncSetAttribute(k16, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess &&
+        cudaFuncSetAttribute(k16, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) == cudaSuccess) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(16, 1, 1);
+      cfg.blockDim = dim3(ATTN_THREADS);
+      cfg.dynamicSmemBytes = attn_smem<HD, G>((a.P + 15) / 16);
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = 16;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      int nclusters = 0;
+      if (cudaOccupancyMaxActiveClusters(&nclusters, k16, &cfg) == cudaSuccess && nclusters >= 4) cl = 16;
+    }
+    (void)cudaGetLastError();
+  }
+  const int cmax = (a.P + cl - 1) / cl;
+  const size_t smem = attn_smem<HD, G>(cmax);
+  if (smem > 200 * 1024) return cudaErrorInvalidValue;
+  return cl == 16 ? attn_launch<HD, G, 16>(a, cmax, smem, st) : attn_launch<HD, G, 8>(a, cmax, smem, st);
+}
+
 cudaError_t launch_attn(const AttnArgs &a, cudaStream_t st) {
   const int G = a.NH / a.NKV;
-  if (G > 8 || a.NH % a.NKV || a.P <= 0) return cudaErrorInvalidValue;
-  const int cmax = (a.P + ATTN_CL - 1) / ATTN_CL;
-  const int groups = ATTN_THREADS / a.HD;
-  const size_t smem = (size_t)G * a.HD * 4 + (size_t)((G * cmax + 3) & ~3) * 4 +
-                      (size_t)groups * G * a.HD * sizeof(acc128);
-  dim3 grid(ATTN_CL, a.NKV, a.ntok);
-  cudaError_t e = cudaSuccess;
-  void (*kern)(AttnArgs, int) = nullptr;
+  if (a.NH % a.NKV || a.P <= 0) return cudaErrorInvalidValue;
 #define SPB_ATTN_CASE(HDV, GV) \
-  if (a.HD == HDV && G == GV) kern = k_attn<HDV, GV>;
+  if (a.HD == HDV && G == GV) return attn_cl<HDV, GV>(a, st);
   SPB_ATTN_CASE(64, 1) SPB_ATTN_CASE(64, 2) SPB_ATTN_CASE(64, 4) SPB_ATTN_CASE(64, 8)
   SPB_ATTN_CASE(128, 1) SPB_ATTN_CASE(128, 2) SPB_ATTN_CASE(128, 4) SPB_ATTN_CASE(128, 8)
   SPB_ATTN_CASE(256, 1) SPB_ATTN_CASE(256, 2) SPB_ATTN_CASE(256, 4) SPB_ATTN_CASE(256, 8)
 #undef SPB_ATTN_CASE
-  if (!kern) return cudaErrorInvalidValue;
-  if (smem > 48 * 1024) {
-    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-  }
-  kern<<<grid, ATTN_THREADS, smem, st>>>(a, cmax);
-  return cudaGetLastError();
+  return cudaErrorInvalidValue;
 }
 
 // ------------------------------------------------------------------------------ misc
@@ -610,6 +1048,7 @@ __device__ __forceinline__ float f16_value(uint32_t h) {
 
 __global__ void k_embed(DevQ4B emb, const int32_t *tok_dev, float scale, int use_scale, float *x, int vocab,
                         uint32_t *err) {
+  pdl_trigger();
   const int t = blockIdx.x;
   int tok = tok_dev[t];
   if (tok < 0 || tok >= vocab) {
@@ -634,52 +1073,31 @@ cudaError_t launch_embed(const DevQ4B &emb, const int32_t *tok_dev, int ntok, fl
   return cudaGetLastError();
 }
 
-__global__ void k_argmax(const float *v, int n, int32_t *out) {
-  const int t = blockIdx.x;
-  const float *r = v + (size_t)t * n;
-  float best = -INFINITY;
-  int bi = 0x7fffffff;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    const float x = r[i];
-    if (x > best || (x == best && i < bi)) { best = x; bi = i; }
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const float ob = __shfl_xor_sync(0xffffffffu, best, o);
-    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-    if (ob > best || (ob == best && oi < bi)) { best = ob; bi = oi; }
-  }
-  __shared__ float sb[32];
-  __shared__ int si[32];
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  if (lane == 0) { sb[warp] = best; si[warp] = bi; }
-  __syncthreads();
-  if (warp == 0) {
-    best = lane < nw ? sb[lane] : -INFINITY;
-    bi = lane < nw ? si[lane] : 0x7fffffff;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ob = __shfl_xor_sync(0xffffffffu, best, o);
-      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-      if (ob > best || (ob == best && oi < bi)) { best = ob; bi = oi; }
-    }
-    if (lane == 0) out[t] = bi == 0x7fffffff ? 0 : bi;
+// decode the keys left by the LM-head GEMV into token ids and clear them for the next step
+__global__ void k_argmax_take(unsigned long long *keys, int ntok, int32_t *out) {
+  pdl_trigger();
+  pdl_wait();
+  const int t = threadIdx.x;
+  if (t < ntok) {
+    const unsigned long long k = keys[t];
+    out[t] = (int32_t)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull));
+    keys[t] = 0ull;
   }
 }
 
-cudaError_t launch_argmax(const float *v, int n, int ntok, int32_t *out, cudaStream_t st) {
-  k_argmax<<<ntok, 1024, 0, st>>>(v, n, out);
-  return cudaGetLastError();
+cudaError_t launch_argmax_take(unsigned long long *keys, int ntok, int32_t *out, cudaStream_t st) {
+  return launch_k(k_argmax_take, dim3(1), dim3(32), 0, st, 1, keys, ntok, out);
 }
 
 __global__ void k_advance(int32_t *pos_dev, int n, const int32_t *src_tok, int32_t *dst_tok) {
+  pdl_trigger();
+  pdl_wait();
   pos_dev[0] += n;
   if (src_tok && dst_tok) dst_tok[0] = src_tok[0];
 }
 
 cudaError_t launch_advance(int32_t *pos_dev, int n, const int32_t *src_tok, int32_t *dst_tok, cudaStream_t st) {
-  k_advance<<<1, 1, 0, st>>>(pos_dev, n, src_tok, dst_tok);
-  return cudaGetLastError();
+  return launch_k(k_advance, dim3(1), dim3(1), 0, st, 1, pos_dev, n, src_tok, dst_tok);
 }
 
 // ------------------------------------------------------------------------------ synthetic weights

@@ -13,6 +13,7 @@ enum : uint32_t {
   ERR_V_RANGE = 1u << 3,      // |v| >= 16384
   ERR_SCORE_RANGE = 1u << 4,  // |score| >= 2^17
   ERR_TOKEN = 1u << 5,        // token id outside [0, vocab)
+  ERR_TIMEOUT = 1u << 6,      // a bounded wait on an asynchronous copy gave up
 };
 
 
@@ -39,19 +40,25 @@ enum GemvEpi : int {
   EPI_SILU_MUL = 2,   // y[t][j] = silu_exact(gate_j) * up_j
 };
 
-// y[t][j] for t < ntok over `w` (and `w2` for the gated epilogues).
+// y[t][j] for t < ntok over `w` (and `w2` for the gated epilogues). ymax (nullable):
+// per-token slots receiving atomicMax of the f32 bits of max |y| (the next quantizer's scale).
+// amax (nullable, zero on entry): per-token 64-bit greedy-argmax keys (first maximum).
 cudaError_t launch_gemv(const DevQ4B &w, const DevQ4B *w2, const DevAct &act, int ntok, float *y,
-                        int ldy, int epi, uint32_t *err, cudaStream_t st, int grid_limit = 0);
+                        int ldy, int epi, uint32_t *err, cudaStream_t st, int grid_limit = 0,
+                        uint32_t *ymax = nullptr, unsigned long long *amax = nullptr);
 
-// Quantize ntok rows of K floats (row stride ldu) into `act` (max |u| per row).
-cudaError_t launch_quant(const float *u, int ldu, int K, int ntok, const DevAct &act, uint32_t *err,
-                         cudaStream_t st);
+// Quantize ntok rows of K floats (row stride ldu) into `act`. maxslot: per-row max |u| as
+// f32 bits already produced upstream; NULL computes it first.
+cudaError_t launch_quant(const float *u, int ldu, int K, int ntok, const DevAct &act,
+                         const uint32_t *maxslot, uint32_t *err, cudaStream_t st);
 
 // Residual + RMSNorm + quantization block (one CTA per token row):
 //   if add:    t = add_w ? rmsnorm_exact(add, add_w) : add;  x += t
 //   nx = rmsnorm_exact(x, out_w);  act <- quant(nx);  (nx also stored when nx_out)
+// zero_slot (nullable): per-row max slots cleared for the next producing kernel.
 cudaError_t launch_norm(float *x, const float *add, const float *add_w, const float *out_w, int E,
-                        int ntok, const DevAct &act, float *nx_out, uint32_t *err, cudaStream_t st);
+                        int ntok, const DevAct &act, float *nx_out, uint32_t *err, cudaStream_t st,
+                        uint32_t *zero_slot = nullptr);
 
 struct RopeArgs {
   const float *qkv;        // [ntok][QD + 2*KVD] projections
@@ -64,6 +71,7 @@ struct RopeArgs {
   const int32_t *pos_dev;  // device position of token row 0 (rows t use pos+t)
   int NH, NKV, HD, P, ntok;
   uint32_t *err;
+  uint32_t *zero_slot;     // nullable: per-row max slots cleared for the attention output
 };
 cudaError_t launch_rope_kv(const RopeArgs &a, cudaStream_t st);
 
@@ -75,12 +83,14 @@ struct AttnArgs {
   int NH, NKV, HD, P, win, ntok;
   float ascale;
   uint32_t *err;
+  uint32_t *ao_max;        // nullable: per-row atomicMax of the f32 bits of max |ao|
 };
 cudaError_t launch_attn(const AttnArgs &a, cudaStream_t st);
 
 cudaError_t launch_embed(const DevQ4B &emb, const int32_t *tok_dev, int ntok, float scale, int use_scale,
                          float *x, int vocab, uint32_t *err, cudaStream_t st);
-cudaError_t launch_argmax(const float *v, int n, int ntok, int32_t *out, cudaStream_t st);
+// token ids from the LM-head GEMV's argmax keys (and clear the keys)
+cudaError_t launch_argmax_take(unsigned long long *keys, int ntok, int32_t *out, cudaStream_t st);
 cudaError_t launch_advance(int32_t *pos_dev, int n, const int32_t *src_tok, int32_t *dst_tok,
                            cudaStream_t st);
 

@@ -59,6 +59,7 @@ static const char *err_bits_text(uint32_t b) {
   if (b & ERR_ROPE_RANGE) return "q/k outside the exact RoPE range (|x| < 256)";
   if (b & ERR_V_RANGE) return "v outside the exact range (|v| < 16384)";
   if (b & ERR_SCORE_RANGE) return "attention score outside the exact range (|z| < 2^17)";
+  if (b & ERR_TIMEOUT) return "a bounded wait on an asynchronous copy gave up";
   return "unknown";
 }
 
@@ -424,6 +425,8 @@ struct spb_session {
   DevAct act;
   int32_t *pos_dev, *tok_dev, *argmax_dev, *hist_dev;
   uint32_t *err_dev;
+  uint32_t *ao_max, *gg_max;      // [NT_MAX] per-row max |y| slots (f32 bits) of the producers
+  unsigned long long *amax_keys;  // [NT_MAX] greedy-argmax keys of the LM head (zero between steps)
   int32_t *h_pinned = nullptr;    // pinned staging: [0..NT_MAX) tokens, [NT_MAX] err, [NT_MAX+1] argmax
   cudaGraphExec_t step_graph = nullptr;
 };
@@ -449,7 +452,8 @@ extern "C" int spb_session_open(spb_model *m, int pmax, spb_session **out) {
   const size_t o_lg = take((size_t)NT_MAX * m->V * 4), o_qi = take((size_t)NT_MAX * m->QD * 4);
   const size_t o_aq = take((size_t)NT_MAX * maxK), o_ab = take((size_t)NT_MAX * (maxK / 32) * 4);
   const size_t o_as = take(NT_MAX * 4), o_pos = take(4), o_tok = take(NT_MAX * 4), o_am = take(NT_MAX * 4);
-  const size_t o_hist = take((size_t)pmax * 4), o_err = take(4);
+  const size_t o_hist = take((size_t)pmax * 4), o_err = take(4), o_slots = take(2 * NT_MAX * 4);
+  const size_t o_keys = take(NT_MAX * 8);
   cudaError_t e = cudaMalloc(&s->buf, off);
   if (e != cudaSuccess) { delete s; return set_err(SPB_EOOM, "spb_session_open: cudaMalloc(%zu): %s", off, cudaGetErrorString(e)); }
   uint8_t *B = s->buf;
@@ -460,6 +464,8 @@ extern "C" int spb_session_open(spb_model *m, int pmax, spb_session **out) {
   s->act = {(int8_t *)(B + o_aq), (int32_t *)(B + o_ab), (float *)(B + o_as)};
   s->pos_dev = (int32_t *)(B + o_pos); s->tok_dev = (int32_t *)(B + o_tok); s->argmax_dev = (int32_t *)(B + o_am);
   s->hist_dev = (int32_t *)(B + o_hist); s->err_dev = (uint32_t *)(B + o_err);
+  s->ao_max = (uint32_t *)(B + o_slots); s->gg_max = s->ao_max + NT_MAX;
+  s->amax_keys = (unsigned long long *)(B + o_keys);
   e = cudaStreamCreateWithFlags(&s->st, cudaStreamNonBlocking);
   if (e == cudaSuccess) e = cudaMallocHost(&s->h_pinned, (NT_MAX + 4) * 4);
   if (e == cudaSuccess) e = cudaMemsetAsync(s->buf, 0, off, s->st);
@@ -512,24 +518,28 @@ static cudaError_t enqueue_rows(spb_session *s, int nt, bool want_logits) {
     ra.W = m->tabs + 32 + (d.global ? 0 : m->HD / 2);
     ra.T = m->tabs; ra.gain = m->gain; ra.pos_dev = s->pos_dev;
     ra.NH = m->NH; ra.NKV = m->NKV; ra.HD = m->HD; ra.P = s->pmax; ra.ntok = nt; ra.err = s->err_dev;
+    ra.zero_slot = s->ao_max;
     K(launch_rope_kv(ra, st));
     AttnArgs aa;
     aa.qi = s->qi; aa.kc = ra.kc; aa.vc = ra.vc; aa.ao = s->ao; aa.pos_dev = s->pos_dev;
     aa.NH = m->NH; aa.NKV = m->NKV; aa.HD = m->HD; aa.P = s->pmax; aa.win = d.win; aa.ntok = nt;
-    aa.ascale = ascale; aa.err = s->err_dev;
+    aa.ascale = ascale; aa.err = s->err_dev; aa.ao_max = s->ao_max;
     K(launch_attn(aa, st));
-    K(launch_quant(s->ao, m->QD, m->QD, nt, s->act, s->err_dev, st));
+    K(launch_quant(s->ao, m->QD, m->QD, nt, s->act, s->ao_max, s->err_dev, st));
     K(launch_gemv(d.o, nullptr, s->act, nt, s->ap, E, EPI_STORE, s->err_dev, st));
-    K(launch_norm(s->x, s->ap, m->gemma ? d.post_attn : nullptr, d.ffn_norm, E, nt, s->act, nullptr, s->err_dev, st));
-    K(launch_gemv(d.g, &d.u, s->act, nt, s->gg, m->FF, m->gemma ? EPI_GELU_MUL : EPI_SILU_MUL, s->err_dev, st));
-    K(launch_quant(s->gg, m->FF, m->FF, nt, s->act, s->err_dev, st));
+    K(launch_norm(s->x, s->ap, m->gemma ? d.post_attn : nullptr, d.ffn_norm, E, nt, s->act, nullptr, s->err_dev, st,
+                  s->gg_max));
+    K(launch_gemv(d.g, &d.u, s->act, nt, s->gg, m->FF, m->gemma ? EPI_GELU_MUL : EPI_SILU_MUL, s->err_dev, st, 0,
+                  s->gg_max));
+    K(launch_quant(s->gg, m->FF, m->FF, nt, s->act, s->gg_max, s->err_dev, st));
     K(launch_gemv(d.d, nullptr, s->act, nt, s->dn, E, EPI_STORE, s->err_dev, st));
   }
   if (want_logits) {
     const DevLayer &p = m->layers[m->NL - 1];
     K(launch_norm(s->x, s->dn, m->gemma ? p.post_ffw : nullptr, m->out_norm, E, nt, s->act, nullptr, s->err_dev, st));
-    K(launch_gemv(m->out, nullptr, s->act, nt, s->logits, m->V, EPI_STORE, s->err_dev, st));
-    K(launch_argmax(s->logits, m->V, nt, s->argmax_dev, st));
+    K(launch_gemv(m->out, nullptr, s->act, nt, s->logits, m->V, EPI_STORE, s->err_dev, st, 0, nullptr,
+                  s->amax_keys));
+    K(launch_argmax_take(s->amax_keys, nt, s->argmax_dev, st));
   }
 #undef K
   return cudaSuccess;
@@ -734,7 +744,7 @@ extern "C" int spb_gemv_q4b(const uint8_t *codes, const uint16_t *bscale, int ro
   cudaStream_t st = (cudaStream_t)stream;
   DevAct act{(int8_t *)wb, (int32_t *)(wb + (size_t)n_tok * cols),
              (float *)(wb + (((size_t)n_tok * cols + (size_t)n_tok * (cols / 32) * 4 + 255) & ~(size_t)255))};
-  CU(launch_quant(x, cols, cols, n_tok, act, err, st));
+  CU(launch_quant(x, cols, cols, n_tok, act, nullptr, err, st));
   DevQ4B w{codes, bscale, rows, cols};
   CU(launch_gemv(w, nullptr, act, n_tok, y, rows, EPI_STORE, err, st));
   return SPB_OK;
@@ -748,7 +758,7 @@ extern "C" int spb_quantize_rows(const float *x, int cols, int n_tok, int8_t *q,
   uint32_t *err;
   int rc = work_get(256, &wb, &err);
   if (rc) return rc;
-  CU(launch_quant(x, cols, cols, n_tok, DevAct{q, bsum, scale}, err, (cudaStream_t)stream));
+  CU(launch_quant(x, cols, cols, n_tok, DevAct{q, bsum, scale}, nullptr, err, (cudaStream_t)stream));
   return SPB_OK;
 }
 
@@ -784,6 +794,33 @@ extern "C" int spb_gemv_q4b_gated_q(const uint8_t *codes_g, const uint16_t *bsca
   if (act != 0 && act != 1) return set_err(SPB_EBADARG, "spb_gemv_q4b_gated_q: act must be 0 (GELU) or 1 (SiLU)");
   return gemv_q_common(codes_g, bscale_g, codes_u, bscale_u, rows, cols, q, bsum, scale, n_tok,
                        act == 0 ? EPI_GELU_MUL : EPI_SILU_MUL, y, stream);
+}
+
+extern "C" int spb_graph_begin(void *stream) {
+  CU(cudaStreamBeginCapture((cudaStream_t)stream, cudaStreamCaptureModeRelaxed));
+  return SPB_OK;
+}
+
+extern "C" int spb_graph_end(void *stream, void **graph_exec) {
+  if (!graph_exec) return set_err(SPB_EBADARG, "spb_graph_end: null out");
+  cudaGraph_t g = nullptr;
+  CU(cudaStreamEndCapture((cudaStream_t)stream, &g));
+  cudaGraphExec_t ex = nullptr;
+  cudaError_t e = cudaGraphInstantiate(&ex, g, 0);
+  cudaGraphDestroy(g);
+  if (e != cudaSuccess) return set_err(SPB_ECUDA, "spb_graph_end: %s", cudaGetErrorString(e));
+  *graph_exec = ex;
+  return SPB_OK;
+}
+
+extern "C" int spb_graph_launch(void *graph_exec, void *stream) {
+  if (!graph_exec) return set_err(SPB_EBADARG, "spb_graph_launch: null graph");
+  CU(cudaGraphLaunch((cudaGraphExec_t)graph_exec, (cudaStream_t)stream));
+  return SPB_OK;
+}
+
+extern "C" void spb_graph_free(void *graph_exec) {
+  if (graph_exec) cudaGraphExecDestroy((cudaGraphExec_t)graph_exec);
 }
 
 extern "C" int spb_take_device_errors(void) {

@@ -27,7 +27,7 @@ CORE_SYMBOLS = [
     "spb_session_stream", "spb_forward", "spb_gemv_q4b", "spb_quantize_rows", "spb_gemv_q4b_q",
     "spb_gemv_q4b_gated_q", "spb_rmsnorm_exact_dev", "spb_gelu_exact_dev",
     "spb_silu_exact_dev", "spb_rope_cordic_dev", "spb_take_device_errors", "spb_rope_freq_table",
-    "spb_cordic_tables",
+    "spb_cordic_tables", "spb_graph_begin", "spb_graph_end", "spb_graph_launch", "spb_graph_free",
 ]
 L1_SYMBOLS = ["spb_l1_forward", "spb_l1_backend", "spb_l1_kvdecode_table", "spb_l1_kvdecode_clone",
               "spb_l1_set_device", "spb_l1_release_model"]
@@ -138,6 +138,8 @@ def load(path: str = CORE_SO):
         "spb_take_device_errors": ([], C.c_int),
         "spb_rope_freq_table": ([C.c_float, C.c_int, vp], C.c_int),
         "spb_cordic_tables": ([vp, vp], None),
+        "spb_graph_begin": ([vp], C.c_int), "spb_graph_end": ([vp, C.POINTER(vp)], C.c_int),
+        "spb_graph_launch": ([vp, vp], C.c_int), "spb_graph_free": ([vp], None),
     }
     for name, (args, res) in sig.items():
         f = getattr(L, name)

@@ -118,7 +118,8 @@ def test_gemv_lm_head_full_size(xr, spb, cuda_ok):
     y = torch.empty((m, rows), dtype=torch.float32, device="cuda")
     spb200.check(spb.spb_gemv_q4b(ptr(dc), ptr(ds), rows, cols, ptr(dx), m, ptr(y), None))
     y2 = torch.empty_like(y)
-    spb200.check(spb.spb_gemv_q4b(ptr(dc), ptr(ds), rows, cols, ptr(dx * 8), m, ptr(y2), None))
+    dx8 = dx * 8   # referenced until the kernel has run
+    spb200.check(spb.spb_gemv_q4b(ptr(dc), ptr(ds), rows, cols, ptr(dx8), m, ptr(y2), None))
     sync()
     yh = y.cpu().numpy()
     assert np.array_equal(u32(yh * np.float32(8)), u32(y2.cpu().numpy()))
