@@ -121,6 +121,17 @@ int  spb_forward(spb_model *m, const int32_t *tokens, int n_tok, float *logits);
  * workspace allocated on first use. */
 int spb_gemv_q4b(const uint8_t *codes, const uint16_t *bscale, int rows, int cols,
                  const float *x, int n_tok, float *y, void *stream);
+/* spb_gemv_q4b without any device allocation (no counterpart in the reference; it exists for
+ * callers that may not call cudaMalloc, e.g. when the device memory is already owned by
+ * another pool or a latency-critical path must avoid the allocator's implicit device sync).
+ * Same arguments and bytes as spb_gemv_q4b. Its scratch is one fixed array inside the
+ * library (about 288 KB per GPU, held until the process exits): n_tok * cols must be at most
+ * 262144, else SPB_EBADARG. All calls on a device share that scratch, so calls that can
+ * overlap on the GPU race; serialise them. The first call on a device sets up the scratch's
+ * device address and should come before any stream capture. Inputs must be finite: this
+ * variant does not report range errors. */
+int spb_gemv_q4b_noalloc(const uint8_t *codes, const uint16_t *bscale, int rows, int cols,
+                         const float *x, int n_tok, float *y, void *stream);
 /* The activation quantizer alone: n_tok rows of cols floats -> the GEMV's input form:
  * q [n_tok][cols] int8 (per 8 columns: the 4 even then the 4 odd), bsum [n_tok][cols/32]
  * int32 block sums of q, scale [n_tok] f32 (max|x|). All device pointers. */

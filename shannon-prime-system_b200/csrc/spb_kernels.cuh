@@ -100,6 +100,9 @@ cudaError_t launch_synth_scales(uint16_t *dst, int rows, int nblk_src, int nblk_
                                 uint64_t key, cudaStream_t st);
 cudaError_t launch_synth_norm(float *dst, int n, uint64_t key, cudaStream_t st);
 
+// store `msg` as this thread's spb_last_error() text and return `code` (host runtime)
+int record_error(int code, const char *msg);
+
 // isolated islands (parity tests)
 cudaError_t launch_rmsnorm_rows(const float *x, const float *w, int n, int rows, float *out, uint32_t *err,
                                 cudaStream_t st);

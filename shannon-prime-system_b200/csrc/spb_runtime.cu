@@ -46,6 +46,8 @@ static int set_err(int code, const char *fmt, ...) {
 
 extern "C" const char *spb_last_error(void) { return g_err; }
 
+int spb::record_error(int code, const char *msg) { return set_err(code, "%s", msg); }
+
 extern "C" int spb_device_count(void) {
   int n = 0;
   if (cudaGetDeviceCount(&n) != cudaSuccess) return 0;

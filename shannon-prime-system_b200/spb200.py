@@ -24,7 +24,8 @@ CORE_SYMBOLS = [
     "spb_model_weight_bytes", "spb_session_open", "spb_session_prefill", "spb_session_decode_step",
     "spb_session_decode_step_argmax", "spb_session_decode_greedy", "spb_session_rewind",
     "spb_session_position", "spb_session_clone", "spb_session_close", "spb_session_kv_read",
-    "spb_session_stream", "spb_forward", "spb_gemv_q4b", "spb_quantize_rows", "spb_gemv_q4b_q",
+    "spb_session_stream", "spb_forward", "spb_gemv_q4b", "spb_gemv_q4b_noalloc", "spb_quantize_rows",
+    "spb_gemv_q4b_q",
     "spb_gemv_q4b_gated_q", "spb_rmsnorm_exact_dev", "spb_gelu_exact_dev",
     "spb_silu_exact_dev", "spb_rope_cordic_dev", "spb_take_device_errors", "spb_rope_freq_table",
     "spb_cordic_tables", "spb_graph_begin", "spb_graph_end", "spb_graph_launch", "spb_graph_free",
@@ -127,6 +128,7 @@ def load(path: str = CORE_SO):
         "spb_session_stream": ([vp], vp),
         "spb_forward": ([vp, vp, C.c_int, vp], C.c_int),
         "spb_gemv_q4b": ([vp, vp, C.c_int, C.c_int, vp, C.c_int, vp, vp], C.c_int),
+        "spb_gemv_q4b_noalloc": ([vp, vp, C.c_int, C.c_int, vp, C.c_int, vp, vp], C.c_int),
         "spb_quantize_rows": ([vp, C.c_int, C.c_int, vp, vp, vp, vp], C.c_int),
         "spb_gemv_q4b_q": ([vp, vp, C.c_int, C.c_int, vp, vp, vp, C.c_int, vp, vp], C.c_int),
         "spb_gemv_q4b_gated_q": ([vp, vp, vp, vp, C.c_int, C.c_int, vp, vp, vp, C.c_int, C.c_int, vp, vp],
