@@ -31,6 +31,8 @@ import sys
 import tempfile
 import time
 
+import numpy as np
+
 ROOT = os.path.dirname(os.path.abspath(__file__))
 PKG = os.path.join(ROOT, "shannon-prime-system_b200")
 ORACLE = os.path.join(ROOT, "oracle")
@@ -51,6 +53,8 @@ def parse():
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-roofline", action="store_true")
+    p.add_argument("--trace", action="store_true",
+                   help="also print the persistent decode kernel's per-phase times (one extra step)")
     # profiling-size overrides (smaller device footprint for ncu captures); a line printed
     # with either set is not the configs[2] measurement and says so in config.workload
     p.add_argument("--layers", type=int, default=0)
@@ -207,6 +211,41 @@ def gemv_roofline(cfg, spb, device, stream, iters=60):
     return out, tot_b, tot_t, launches
 
 
+PHASES = ["norm", "qkv_gemv", "barrier", "attention", "barrier", "quantize", "o_gemv", "barrier", "norm",
+          "gate_up_gemv", "barrier", "quantize", "down_gemv", "barrier"]
+
+
+def trace_report(tr, n_layers):
+    """Per-phase microseconds of one persistent decode step, averaged over the layers:
+    `cta0` from CTA 0's clock, `spread` = latest minus earliest CTA at the phase's end."""
+    t0, late, early = tr[:, 0].astype(np.int64), tr[:, 1].astype(np.int64), tr[:, 2].astype(np.int64)
+    out = {}
+    for i, name in enumerate(PHASES):
+        d = [(t0[1 + L * 14 + i] - t0[L * 14 + i]) / 1e3 for L in range(n_layers)]
+        sp = [(late[1 + L * 14 + i] - early[1 + L * 14 + i]) / 1e3 for L in range(n_layers)]
+        out[f"{i:02d}_{name}"] = {"cta0": round(float(np.mean(d)), 2), "spread": round(float(np.mean(sp)), 2)}
+    f = 1 + n_layers * 14
+    out["final_norm"] = round((t0[f] - t0[f - 1]) / 1e3, 2)
+    out["lm_head"] = round((t0[f + 1] - t0[f]) / 1e3, 2)
+    out["last_barrier"] = round((t0[f + 2] - t0[f + 1]) / 1e3, 2)
+    out["total"] = round((t0[f + 2] - t0[0]) / 1e3, 2)
+    return out
+
+
+def tile_report(tiles, pts):
+    """CTA 0's ring tiles: copy latency (issue -> found complete) and the gap between
+    consecutive issues, as percentiles, over the last 256 tiles of the step (the LM head)."""
+    t = tiles.astype(np.int64)
+    n = int(np.count_nonzero(t[:, 0]))
+    sel = t[max(0, n - 256):n]
+    lat = (sel[:, 1] - sel[:, 0]) / 1e3
+    gap = np.diff(sel[:, 0]) / 1e3
+    cons = np.diff(sel[:, 1]) / 1e3
+    q = lambda v: [round(float(np.percentile(v, x)), 2) for x in (10, 50, 90)]
+    return {"tiles": n, "latency_p10_50_90": q(lat), "issue_gap_p10_50_90": q(gap),
+            "consume_gap_p10_50_90": q(cons)}
+
+
 # ----------------------------------------------------------------------------- arms
 def run_spb(args):
     import torch
@@ -293,6 +332,10 @@ def run_spb(args):
                 "algorithmic_bytes_per_token": int(tot_b), "gemv_us_per_token": round(tot_us, 1),
                 "per_shape": shapes}
     clk = clocks.stop()
+    if args.trace and rank == 0:
+        pts, tiles = s.decode_trace(int(generated[-1]))
+        print(json.dumps({"decode_phase_trace_us": trace_report(pts, cfg.n_layers),
+                          "tile_latency_us": tile_report(tiles, pts)}), file=sys.stderr)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

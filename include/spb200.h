@@ -97,10 +97,22 @@ int  spb_session_prefill(spb_session *s, const int32_t *tokens, int n_tok, float
 int  spb_session_decode_step(spb_session *s, int32_t token, float *logits);
 /* like decode_step, and also returns the greedy argmax (first max index) */
 int  spb_session_decode_step_argmax(spb_session *s, int32_t token, float *logits, int32_t *argmax);
-/* n_steps greedy steps entirely on the device (CUDA graph per step, no host sync
- * between steps): feeds `token`, then each step's argmax; writes the n_steps
- * argmaxes (host). */
+/* n_steps greedy steps entirely on the device (no host sync between steps): feeds
+ * `token`, then each step's argmax; writes the n_steps argmaxes (host). */
 int  spb_session_decode_greedy(spb_session *s, int32_t token, int n_steps, int32_t *tokens_out);
+/* How decode steps run (process-wide): 0 = the multi-kernel schedule replayed as a CUDA
+ * graph (default), 1 = one persistent cooperative kernel per step where the model shape
+ * and context fit it. Any other value only queries. Returns the previous mode. Both give
+ * byte-identical results. */
+int  spb_decode_mode(int mode);
+/* One decode step through the persistent kernel with its phase trace on (diagnostics):
+ * out receives 3 * (2 + 14 * n_layers + 2) words, per trace point the %globaltimer
+ * nanoseconds of CTA 0, of the latest and of the earliest CTA. Points: kernel start; per
+ * layer: norm, QKV GEMV, barrier, attention, barrier, quantize, O GEMV, barrier, norm,
+ * gate/up GEMV, barrier, quantize, down GEMV, barrier; then final norm, LM head, barrier.
+ * With cap >= that + 8192, the next 8192 words are CTA 0's first 4096 ring tiles as
+ * (copy issued, found complete) time pairs. */
+int  spb_session_decode_trace(spb_session *s, int32_t token, uint64_t *out, int cap);
 int  spb_session_rewind(spb_session *s, int n);          /* O(1): position -= n */
 int  spb_session_position(const spb_session *s);         /* -1 on NULL */
 int  spb_session_clone(const spb_session *s, spb_session **out);   /* deep KV copy */

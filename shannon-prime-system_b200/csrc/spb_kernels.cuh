@@ -100,6 +100,62 @@ cudaError_t launch_synth_scales(uint16_t *dst, int rows, int nblk_src, int nblk_
                                 uint64_t key, cudaStream_t st);
 cudaError_t launch_synth_norm(float *dst, int n, uint64_t key, cudaStream_t st);
 
+// ---- the decode step as one persistent kernel (spb_decode.cu) ----
+// Weights and tables of one layer as the persistent kernel reads them (a device array of
+// n_layers entries, built once per model).
+struct DecLayer {
+  DevQ4B qkv, o, g, u, d;
+  const float *attn_norm, *post_attn, *ffn_norm, *post_ffw;
+  const float *q_norm, *k_norm;   // nullable when the model has no QK-norm
+  const uint64_t *W;              // CORDIC turn table of this layer's RoPE base [HD/2]
+  int win;                        // sliding window, -1 for global attention
+  int pad_;
+};
+
+struct DecodeArgs {
+  const DecLayer *layers;         // device [NL]
+  DevQ4B embd, out;
+  const float *out_norm;
+  const uint64_t *T;              // CORDIC arctangent table [30]
+  uint64_t gain;
+  int NL, E, FF, NH, NKV, HD, QD, KVD, V, P, gemma;
+  float es, ascale;
+  int32_t *kc, *vc;               // KV cache base, [NL][NKV][P][HD]
+  size_t kvl;                     // elements per layer of the cache
+  int32_t *pos_dev, *tok_dev, *argmax_dev;   // position in, token in / next token out
+  float *x2;                      // [2][E] residual ping-pong
+  float *qkv, *ao, *ap, *gg, *dn, *logits;
+  uint32_t *slots;                // [NL][2] max |attention out|, max |gate*up| (f32 bits); zero on entry
+  int32_t *pmx;                   // [grid][G] per-CTA attention partial maxima
+  int64_t *psum;                  // [grid][G] per-CTA exponential sums
+  uint64_t *pnum;                 // [grid][G][HD][2] per-CTA 128-bit V-sums (lo, hi)
+  uint32_t *sync;                 // [(3 + NKV) * 32] counters (zero on entry, reset by the kernel)
+  unsigned long long *amax;       // greedy-argmax key (zero on entry, cleared by the kernel)
+  uint32_t *err;
+  // nullable: per trace point k, [k][0] = CTA 0's %globaltimer, [k][1] = the latest and
+  // [k][2] = the earliest CTA (host-initialised to 0 and ~0)
+  unsigned long long *trace;
+};
+// trace points: DEC_TRACE_PER_LAYER per layer, then the final norm, LM head, last barrier;
+// after the points, CTA 0's per-tile record [DEC_TRACE_TILES][2]: the time the producer
+// issued the tile's copy and the time warp 0 found it complete
+constexpr int DEC_TRACE_PER_LAYER = 14;
+constexpr int DEC_TRACE_TILES = 4096;
+__host__ __device__ inline int decode_trace_points(int nl) { return 1 + nl * DEC_TRACE_PER_LAYER + 3; }
+__host__ __device__ inline int decode_trace_words(int nl) { return 3 * decode_trace_points(nl) + 2 * DEC_TRACE_TILES; }
+
+// words of DecodeArgs::sync: the grid counter, the exit counter, the abort word, then one
+// counter per KV head, each on its own 128-byte line
+constexpr int DEC_SYNC_WORDS_PER = 32;
+inline int decode_sync_words(int nkv) { return (3 + nkv) * DEC_SYNC_WORDS_PER; }
+
+// Whether the persistent kernel covers this model shape and context length on `grid` CTAs
+// (one per SM); 0 if so, else a reason string.
+const char *decode_unsupported(const DecodeArgs &a, int grid, int ctx);
+// CTAs the persistent kernel runs with on the current device (0 if it cannot be resident)
+int decode_grid();
+cudaError_t launch_decode(const DecodeArgs &a, int grid, cudaStream_t st);
+
 // store `msg` as this thread's spb_last_error() text and return `code` (host runtime)
 int record_error(int code, const char *msg);
 

@@ -176,6 +176,7 @@ struct spb_model {
   uint64_t gain = 0;
   float es = 1.0f;
   int64_t stream_bytes = 0;
+  DecLayer *dec_layers = nullptr;   // device [NL]: the persistent decode kernel's view of the layers
 };
 
 static size_t q4b_bytes(int rows, int cols) { return (size_t)rows * (cols / 2) + (size_t)rows * (cols / 32) * 2; }
@@ -263,6 +264,22 @@ static int model_alloc(const spb_config &c, int device, spb_model **out) {
   if (rc) { cudaFree(m->wbuf); delete m; return rc; }
   e = cudaMemcpy(m->tabs, ht.data(), ht.size() * 8, cudaMemcpyHostToDevice);
   if (e != cudaSuccess) { cudaFree(m->wbuf); delete m; return set_err(SPB_ECUDA, "spb_model: tables: %s", cudaGetErrorString(e)); }
+  {
+    std::vector<DecLayer> dl(m->NL);
+    for (int L = 0; L < m->NL; L++) {
+      const DevLayer &d = m->layers[L];
+      dl[L] = DecLayer{d.qkv, d.o, d.g, d.u, d.d, d.attn_norm, d.post_attn, d.ffn_norm, d.post_ffw,
+                       d.q_norm, d.k_norm, m->tabs + 32 + (d.global ? 0 : m->HD / 2), d.win, 0};
+    }
+    e = cudaMalloc(&m->dec_layers, sizeof(DecLayer) * m->NL);
+    if (e == cudaSuccess) e = cudaMemcpy(m->dec_layers, dl.data(), sizeof(DecLayer) * m->NL, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+      cudaFree(m->dec_layers);
+      cudaFree(m->wbuf);
+      delete m;
+      return set_err(SPB_ECUDA, "spb_model: layer table: %s", cudaGetErrorString(e));
+    }
+  }
   m->stream_bytes = (int64_t)m->NL * (int64_t)(q4b_bytes(QKV, m->E) + q4b_bytes(m->E, m->QD) +
                                               2 * q4b_bytes(m->FF, m->E) + q4b_bytes(m->E, m->FF)) +
                     (int64_t)q4b_bytes(m->V, m->E);
@@ -406,6 +423,7 @@ extern "C" int spb_model_synthetic(const spb_config *cfg, uint64_t seed, int dev
 extern "C" void spb_model_free(spb_model *m) {
   if (!m) return;
   cudaSetDevice(m->device);
+  cudaFree(m->dec_layers);
   cudaFree(m->wbuf);
   delete m;
 }
@@ -431,7 +449,25 @@ struct spb_session {
   unsigned long long *amax_keys;  // [NT_MAX] greedy-argmax keys of the LM head (zero between steps)
   int32_t *h_pinned = nullptr;    // pinned staging: [0..NT_MAX) tokens, [NT_MAX] err, [NT_MAX+1] argmax
   cudaGraphExec_t step_graph = nullptr;
+  int dgrid = 0;                  // CTAs of the persistent decode kernel (0: not available)
+  DecodeArgs dargs{};             // its arguments (fixed for the session's lifetime)
+  unsigned long long *trace_dev = nullptr;   // phase trace of the persistent kernel (on request)
 };
+
+// 1: decode steps run as the persistent kernel where it covers the shape; 0 (default, the
+// faster of the two at the 12B shape today): always the multi-kernel graph
+static int g_decode_mode = 0;
+
+extern "C" int spb_decode_mode(int mode) {
+  const int prev = g_decode_mode;
+  if (mode == 0 || mode == 1) g_decode_mode = mode;
+  return prev;
+}
+
+// the persistent kernel serves a step whose new token lands at position `pos`
+static bool use_decode_kernel(const spb_session *s, int pos) {
+  return g_decode_mode == 1 && s->dgrid > 0 && decode_unsupported(s->dargs, s->dgrid, pos + 1) == nullptr;
+}
 
 static size_t kv_layer_elems(const spb_model *m, int pmax) { return (size_t)m->NKV * pmax * m->HD; }
 
@@ -456,6 +492,13 @@ extern "C" int spb_session_open(spb_model *m, int pmax, spb_session **out) {
   const size_t o_as = take(NT_MAX * 4), o_pos = take(4), o_tok = take(NT_MAX * 4), o_am = take(NT_MAX * 4);
   const size_t o_hist = take((size_t)pmax * 4), o_err = take(4), o_slots = take(2 * NT_MAX * 4);
   const size_t o_keys = take(NT_MAX * 8);
+  const int G = m->NH / m->NKV;
+  s->dgrid = decode_grid();
+  (void)cudaGetLastError();
+  const int dg = std::max(s->dgrid, 1);
+  const size_t o_dsync = take((size_t)decode_sync_words(m->NKV) * 4), o_dslots = take((size_t)m->NL * 2 * 4);
+  const size_t o_pmx = take((size_t)dg * G * 4), o_psum = take((size_t)dg * G * 8);
+  const size_t o_pnum = take((size_t)dg * G * m->HD * 16);
   cudaError_t e = cudaMalloc(&s->buf, off);
   if (e != cudaSuccess) { delete s; return set_err(SPB_EOOM, "spb_session_open: cudaMalloc(%zu): %s", off, cudaGetErrorString(e)); }
   uint8_t *B = s->buf;
@@ -468,6 +511,20 @@ extern "C" int spb_session_open(spb_model *m, int pmax, spb_session **out) {
   s->hist_dev = (int32_t *)(B + o_hist); s->err_dev = (uint32_t *)(B + o_err);
   s->ao_max = (uint32_t *)(B + o_slots); s->gg_max = s->ao_max + NT_MAX;
   s->amax_keys = (unsigned long long *)(B + o_keys);
+  {
+    DecodeArgs &a = s->dargs;
+    a.layers = m->dec_layers; a.embd = m->embd; a.out = m->out; a.out_norm = m->out_norm;
+    a.T = m->tabs; a.gain = m->gain;
+    a.NL = m->NL; a.E = E; a.FF = m->FF; a.NH = m->NH; a.NKV = m->NKV; a.HD = m->HD; a.QD = m->QD;
+    a.KVD = m->KVD; a.V = m->V; a.P = pmax; a.gemma = m->gemma ? 1 : 0;
+    a.es = m->es; a.ascale = 1.0f / sqrtf((float)m->HD);
+    a.kc = s->kc; a.vc = s->vc; a.kvl = kv_layer_elems(m, pmax);
+    a.pos_dev = s->pos_dev; a.tok_dev = s->tok_dev; a.argmax_dev = s->argmax_dev;
+    a.x2 = s->x; a.qkv = s->qkv; a.ao = s->ao; a.ap = s->ap; a.gg = s->gg; a.dn = s->dn; a.logits = s->logits;
+    a.slots = (uint32_t *)(B + o_dslots); a.pmx = (int32_t *)(B + o_pmx); a.psum = (int64_t *)(B + o_psum);
+    a.pnum = (uint64_t *)(B + o_pnum); a.sync = (uint32_t *)(B + o_dsync); a.amax = s->amax_keys;
+    a.err = s->err_dev;
+  }
   e = cudaStreamCreateWithFlags(&s->st, cudaStreamNonBlocking);
   if (e == cudaSuccess) e = cudaMallocHost(&s->h_pinned, (NT_MAX + 4) * 4);
   if (e == cudaSuccess) e = cudaMemsetAsync(s->buf, 0, off, s->st);
@@ -482,6 +539,7 @@ extern "C" void spb_session_close(spb_session *s) {
   cudaSetDevice(s->m->device);
   if (s->st) cudaStreamSynchronize(s->st);
   if (s->step_graph) cudaGraphExecDestroy(s->step_graph);
+  cudaFree(s->trace_dev);
   if (s->st) cudaStreamDestroy(s->st);
   cudaFreeHost(s->h_pinned);
   cudaFree(s->buf);
@@ -611,16 +669,53 @@ extern "C" int spb_session_decode_step_argmax(spb_session *s, int32_t token, flo
   if (!s) return set_err(SPB_EBADARG, "spb_session_decode_step: null session");
   if (s->pos >= s->pmax) return set_err(SPB_ECONTEXT_FULL, "spb_session_decode_step: context full");
   CU(cudaSetDevice(s->m->device));
-  int rc = ensure_step_graph(s);
+  const bool persistent = use_decode_kernel(s, s->pos);
+  int rc = persistent ? SPB_OK : ensure_step_graph(s);
   if (rc) return rc;
   s->h_pinned[0] = token;
   CU(cudaMemcpyAsync(s->tok_dev, s->h_pinned, 4, cudaMemcpyHostToDevice, s->st));
-  CU(cudaGraphLaunch(s->step_graph, s->st));
+  if (persistent && launch_decode(s->dargs, s->dgrid, s->st) != cudaSuccess) {
+    // the cooperative launch did not fit beside other work on the device: this session
+    // falls back to the multi-kernel schedule from here on
+    (void)cudaGetLastError();
+    s->dgrid = 0;
+    rc = ensure_step_graph(s);
+    if (rc) return rc;
+    CU(cudaGraphLaunch(s->step_graph, s->st));
+  } else if (!persistent) {
+    CU(cudaGraphLaunch(s->step_graph, s->st));
+  }
   if (logits) CU(cudaMemcpyAsync(logits, s->logits, (size_t)s->m->V * 4, cudaMemcpyDeviceToHost, s->st));
   if (argmax) CU(cudaMemcpyAsync(s->h_pinned + NT_MAX + 1, s->argmax_dev, 4, cudaMemcpyDeviceToHost, s->st));
   rc = collect_errors(s);
   if (rc) { sync_pos(s); cudaStreamSynchronize(s->st); return rc; }
   if (argmax) *argmax = s->h_pinned[NT_MAX + 1];
+  s->pos += 1;
+  return SPB_OK;
+}
+
+// One persistent decode step with the phase trace on: out receives decode_trace_points(NL)
+// triples (CTA 0 time, latest CTA, earliest CTA) of %globaltimer nanoseconds.
+extern "C" int spb_session_decode_trace(spb_session *s, int32_t token, uint64_t *out, int cap) {
+  if (!s || !out) return set_err(SPB_EBADARG, "spb_session_decode_trace: bad arg");
+  const int np = decode_trace_points(s->m->NL), nw = decode_trace_words(s->m->NL);
+  if (cap < 3 * np) return set_err(SPB_EBADARG, "spb_session_decode_trace: need %d words", 3 * np);
+  if (s->pos >= s->pmax) return set_err(SPB_ECONTEXT_FULL, "spb_session_decode_trace: context full");
+  CU(cudaSetDevice(s->m->device));
+  if (!use_decode_kernel(s, s->pos))
+    return set_err(SPB_EUNSUPPORTED, "spb_session_decode_trace: the persistent kernel does not serve this step");
+  if (!s->trace_dev) CU(cudaMalloc(&s->trace_dev, (size_t)nw * 8));
+  std::vector<uint64_t> init((size_t)nw, 0ull);
+  for (int k = 0; k < np; k++) init[3 * k + 2] = ~0ull;
+  CU(cudaMemcpy(s->trace_dev, init.data(), init.size() * 8, cudaMemcpyHostToDevice));
+  s->h_pinned[0] = token;
+  CU(cudaMemcpyAsync(s->tok_dev, s->h_pinned, 4, cudaMemcpyHostToDevice, s->st));
+  DecodeArgs a = s->dargs;
+  a.trace = s->trace_dev;
+  CU(launch_decode(a, s->dgrid, s->st));
+  CU(cudaMemcpyAsync(out, s->trace_dev, (size_t)std::min(cap, nw) * 8, cudaMemcpyDeviceToHost, s->st));
+  int rc = collect_errors(s);
+  if (rc) { sync_pos(s); cudaStreamSynchronize(s->st); return rc; }
   s->pos += 1;
   return SPB_OK;
 }
@@ -634,12 +729,14 @@ extern "C" int spb_session_decode_greedy(spb_session *s, int32_t token, int n_st
   if (n_steps > s->pmax - s->pos) return set_err(SPB_ECONTEXT_FULL, "spb_session_decode_greedy: context full");
   if (n_steps == 0) return SPB_OK;
   CU(cudaSetDevice(s->m->device));
-  int rc = ensure_step_graph(s);
+  int rc = SPB_OK;
+  if (!use_decode_kernel(s, s->pos) || !use_decode_kernel(s, s->pos + n_steps - 1)) rc = ensure_step_graph(s);
   if (rc) return rc;
   s->h_pinned[0] = token;
   CU(cudaMemcpyAsync(s->tok_dev, s->h_pinned, 4, cudaMemcpyHostToDevice, s->st));
   for (int i = 0; i < n_steps; i++) {
-    CU(cudaGraphLaunch(s->step_graph, s->st));
+    if (use_decode_kernel(s, s->pos + i)) CU(launch_decode(s->dargs, s->dgrid, s->st));
+    else CU(cudaGraphLaunch(s->step_graph, s->st));
     // after the step, tok_dev holds this step's argmax (the graph's last node copies it)
     CU(cudaMemcpyAsync(s->hist_dev + s->pos + i, s->tok_dev, 4, cudaMemcpyDeviceToDevice, s->st));
   }

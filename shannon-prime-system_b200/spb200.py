@@ -29,6 +29,7 @@ CORE_SYMBOLS = [
     "spb_gemv_q4b_gated_q", "spb_rmsnorm_exact_dev", "spb_gelu_exact_dev",
     "spb_silu_exact_dev", "spb_rope_cordic_dev", "spb_take_device_errors", "spb_rope_freq_table",
     "spb_cordic_tables", "spb_graph_begin", "spb_graph_end", "spb_graph_launch", "spb_graph_free",
+    "spb_decode_mode", "spb_session_decode_trace",
 ]
 L1_SYMBOLS = ["spb_l1_forward", "spb_l1_backend", "spb_l1_kvdecode_table", "spb_l1_kvdecode_clone",
               "spb_l1_set_device", "spb_l1_release_model"]
@@ -122,6 +123,8 @@ def load(path: str = CORE_SO):
         "spb_session_decode_step": ([vp, i32, vp], C.c_int),
         "spb_session_decode_step_argmax": ([vp, i32, vp, vp], C.c_int),
         "spb_session_decode_greedy": ([vp, i32, C.c_int, vp], C.c_int),
+        "spb_decode_mode": ([C.c_int], C.c_int),
+        "spb_session_decode_trace": ([vp, i32, vp, C.c_int], C.c_int),
         "spb_session_rewind": ([vp, C.c_int], C.c_int), "spb_session_position": ([vp], C.c_int),
         "spb_session_clone": ([vp, C.POINTER(vp)], C.c_int), "spb_session_close": ([vp], None),
         "spb_session_kv_read": ([vp, C.c_int, C.c_int, C.c_int, vp], C.c_int),
@@ -232,6 +235,14 @@ class Session:
         am = C.c_int32()
         check(load().spb_session_decode_step_argmax(self.h, int(token), lg.ctypes.data, C.byref(am)))
         return lg, am.value
+
+    def decode_trace(self, token):
+        """One decode step through the persistent kernel with its phase trace; returns an
+        array [points][3] of %globaltimer ns (CTA 0, latest CTA, earliest CTA)."""
+        npts = 1 + self.model.cfg.n_layers * 14 + 3
+        out = np.zeros(3 * npts + 2 * 4096, np.uint64)
+        check(load().spb_session_decode_trace(self.h, int(token), out.ctypes.data, out.size))
+        return out[:3 * npts].reshape(npts, 3), out[3 * npts:].reshape(4096, 2)
 
     def greedy(self, token, n):
         out = np.empty(n, np.int32)
