@@ -53,6 +53,8 @@ def parse():
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-roofline", action="store_true")
+    p.add_argument("--decode-mode", type=int, default=None, choices=[0, 1],
+                   help="0: multi-kernel graph per step, 1: persistent kernel per step (default: the library's)")
     p.add_argument("--trace", action="store_true",
                    help="also print the persistent decode kernel's per-phase times (one extra step)")
     # profiling-size overrides (smaller device footprint for ncu captures); a line printed
@@ -215,17 +217,34 @@ PHASES = ["norm", "qkv_gemv", "barrier", "attention", "barrier", "quantize", "o_
           "gate_up_gemv", "barrier", "quantize", "down_gemv", "barrier"]
 
 
-def trace_report(tr, n_layers):
+def trace_report(tr, n_layers, sm_mhz=1965.0):
     """Per-phase microseconds of one persistent decode step, averaged over the layers:
-    `cta0` from CTA 0's clock, `spread` = latest minus earliest CTA at the phase's end."""
-    t0, late, early = tr[:, 0].astype(np.int64), tr[:, 1].astype(np.int64), tr[:, 2].astype(np.int64)
+    `cta0` from CTA 0's SM cycle counter (at sm_mhz), `spread` = latest minus earliest CTA
+    (%globaltimer) at the phase's end."""
+    t0 = tr[:, 0].astype(np.float64) * (1e3 / sm_mhz)   # cycles -> ns
+    late, early = tr[:, 1].astype(np.int64), tr[:, 2].astype(np.int64)
+    P = 24   # trace points per layer
     out = {}
+    # phase ends of layer L: 1 + P L + i; the previous point of phase 0 is the previous layer's
+    # last phase end (or the kernel start)
+    prev = lambda L, i: 1 + P * L + i - 1 if i > 0 else (0 if L == 0 else 1 + P * (L - 1) + 13)
     for i, name in enumerate(PHASES):
-        d = [(t0[1 + L * 14 + i] - t0[L * 14 + i]) / 1e3 for L in range(n_layers)]
-        sp = [(late[1 + L * 14 + i] - early[1 + L * 14 + i]) / 1e3 for L in range(n_layers)]
+        d = [(t0[1 + P * L + i] - t0[prev(L, i)]) / 1e3 for L in range(n_layers)]
+        sp = [(late[1 + P * L + i] - early[1 + P * L + i]) / 1e3 for L in range(n_layers)]
         out[f"{i:02d}_{name}"] = {"cta0": round(float(np.mean(d)), 2), "spread": round(float(np.mean(sp)), 2)}
-    f = 1 + n_layers * 14
-    out["final_norm"] = round((t0[f] - t0[f - 1]) / 1e3, 2)
+    # inside attention (between the post-QKV barrier and the attention end) and the first norm
+    sub = {"attn_rope": (2, 14), "attn_scores": (14, 15), "attn_head_barrier1": (15, 16), "attn_exp": (16, 17),
+           "attn_vsum": (17, 18), "attn_head_barrier2": (18, 19), "attn_finalize": (19, 3),
+           "norm_inputs": (-1, 20), "norm_postnorm": (20, 21), "norm_residual": (21, 22), "norm_apply": (22, 23),
+           "norm_quantize": (23, 0)}
+    for name, (i0, i1) in sub.items():
+        d = []
+        for L in range(n_layers):
+            a_ = prev(L, 0) if i0 < 0 else 1 + P * L + i0
+            d.append((t0[1 + P * L + i1] - t0[a_]) / 1e3)
+        out[name] = round(float(np.mean(d)), 2)
+    last, f = 1 + P * (n_layers - 1) + 13, 1 + P * n_layers   # last layer's end; final norm point
+    out["final_norm"] = round((t0[f] - t0[last]) / 1e3, 2)
     out["lm_head"] = round((t0[f + 1] - t0[f]) / 1e3, 2)
     out["last_barrier"] = round((t0[f + 2] - t0[f + 1]) / 1e3, 2)
     out["total"] = round((t0[f + 2] - t0[0]) / 1e3, 2)
@@ -260,6 +279,8 @@ def run_spb(args):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
     spb = spb200.load()
+    if args.decode_mode is not None:
+        spb.spb_decode_mode(args.decode_mode)
     cfg = bench_config(args)
     K, W = args.steps, args.warmup
     pmax = args.prefill + W + K + 8
@@ -334,7 +355,7 @@ def run_spb(args):
     clk = clocks.stop()
     if args.trace and rank == 0:
         pts, tiles = s.decode_trace(int(generated[-1]))
-        print(json.dumps({"decode_phase_trace_us": trace_report(pts, cfg.n_layers),
+        print(json.dumps({"decode_phase_trace_us": trace_report(pts, cfg.n_layers, clk.get("sm_mhz") or 1965.0),
                           "tile_latency_us": tile_report(tiles, pts)}), file=sys.stderr)
 
     cpu = None

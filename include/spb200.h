@@ -106,10 +106,13 @@ int  spb_session_decode_greedy(spb_session *s, int32_t token, int n_steps, int32
  * byte-identical results. */
 int  spb_decode_mode(int mode);
 /* One decode step through the persistent kernel with its phase trace on (diagnostics):
- * out receives 3 * (2 + 14 * n_layers + 2) words, per trace point the %globaltimer
- * nanoseconds of CTA 0, of the latest and of the earliest CTA. Points: kernel start; per
+ * out receives 3 * (2 + 24 * n_layers + 2) words, per trace point CTA 0's SM clock
+ * cycles and the %globaltimer nanoseconds of the latest and of the earliest CTA. Points: kernel start; per
  * layer: norm, QKV GEMV, barrier, attention, barrier, quantize, O GEMV, barrier, norm,
- * gate/up GEMV, barrier, quantize, down GEMV, barrier; then final norm, LM head, barrier.
+ * gate/up GEMV, barrier, quantize, down GEMV, barrier (the phase ends), then inside
+ * attention: RoPE, scores, head barrier, exponentials, V-sum, head barrier, and inside
+ * the first norm: inputs, post-norm sum, residual sum, apply; then final norm, LM head,
+ * barrier.
  * With cap >= that + 8192, the next 8192 words are CTA 0's first 4096 ring tiles as
  * (copy issued, found complete) time pairs. */
 int  spb_session_decode_trace(spb_session *s, int32_t token, uint64_t *out, int cap);

@@ -129,7 +129,7 @@ __device__ __forceinline__ bool aborted() { return *(volatile int *)&g_sh.abort 
 
 __device__ __noinline__ void set_abort(const DecodeArgs &a) {
   *(volatile int *)&g_sh.abort = 1;
-  atomicExch(a.sync + SYNC_ABORT, 1u);
+  if (a.sync) atomicExch(a.sync + SYNC_ABORT, 1u);
   raise_err(a.err, ERR_TIMEOUT);
 }
 
@@ -231,8 +231,7 @@ __device__ __forceinline__ AttnPart attn_part(int c, int nctas, int NKV, int p, 
 //   embedding row of the token;
 //   per layer: [norm weights] QKV | K slices | V slices | O | [norm weights] gate/up | down;
 //   [final norm weights] LM head.
-// The order is generated by a small state machine so that the producer can walk it twice:
-// once to fill the shared-memory ring, and LEAD tiles further ahead to prefetch into L2.
+// The order is generated by a small state machine whose per-tile step is plain arithmetic.
 struct Tile {
   const void *s0, *s1;
   uint32_t b0, b1;
@@ -364,47 +363,39 @@ struct TileGen {
   }
 };
 
-__device__ __forceinline__ void prefetch_l2(const void *p, uint32_t bytes) {
-  if (bytes) asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+// put tile T into its ring slot once the consumers have released the slot's previous tile;
+// false (and the step aborted) if that wait gives up
+__device__ bool ring_issue(const DecodeArgs &a, uint32_t T, const Tile &t) {
+  const int slot = (int)(T % NSLOT);
+  const uint32_t n = T / NSLOT;
+  if (n > 0) {
+    bool got = false;
+    const uint64_t t0 = now_ns();
+    for (;;) {
+      if (mbar_try_wait_sleep(&g_sh.empty[slot], (n - 1) & 1u, SLEEP_NS)) { got = true; break; }
+      if (aborted()) break;
+      if (now_ns() - t0 > WAIT_LIMIT_NS) break;
+    }
+    if (!got) {
+      if (!aborted()) set_abort(a);
+      return false;
+    }
+  }
+  if (a.trace && blockIdx.x == 0 && T < DEC_TRACE_TILES) a.trace[3 * decode_trace_points(a.NL) + 2 * T] = now_ns();
+  fence_proxy_async_smem();
+  mbar_arrive_expect_tx(&g_sh.full[slot], t.b0 + t.b1);
+  bulk_g2s(ring_slot(slot), t.s0, t.b0, &g_sh.full[slot]);
+  if (t.b1) bulk_g2s(ring_slot(slot) + t.b0, t.s1, t.b1, &g_sh.full[slot]);
+  return true;
 }
 
-constexpr int LEAD = 0;   // tiles prefetched into L2 beyond the ring
-
 __device__ uint32_t produce(const DecodeArgs &a, int p, int tok) {
-  TileGen gen, lead;
-  Tile t, u;
+  TileGen gen;
+  Tile t;
   uint32_t T = 0;
-  int ahead = 0;   // tiles the lead cursor has prefetched beyond T
   while (gen.next(a, p, tok, t)) {
-    while (ahead < NSLOT + LEAD && lead.next(a, p, tok, u)) {
-      if (ahead >= NSLOT) {   // the first NSLOT go straight into the ring
-        prefetch_l2(u.s0, u.b0);
-        prefetch_l2(u.s1, u.b1);
-      }
-      ahead++;
-    }
-    const int slot = (int)(T % NSLOT);
-    const uint32_t n = T / NSLOT;
-    if (n > 0) {
-      bool got = false;
-      const uint64_t t0 = now_ns();
-      for (;;) {
-        if (mbar_try_wait_sleep(&g_sh.empty[slot], (n - 1) & 1u, SLEEP_NS)) { got = true; break; }
-        if (aborted()) break;
-        if (now_ns() - t0 > WAIT_LIMIT_NS) break;
-      }
-      if (!got) {
-        if (!aborted()) set_abort(a);
-        return T;
-      }
-    }
-    if (a.trace && blockIdx.x == 0 && T < DEC_TRACE_TILES) a.trace[3 * decode_trace_points(a.NL) + 2 * T] = now_ns();
-    fence_proxy_async_smem();
-    mbar_arrive_expect_tx(&g_sh.full[slot], t.b0 + t.b1);
-    bulk_g2s(ring_slot(slot), t.s0, t.b0, &g_sh.full[slot]);
-    if (t.b1) bulk_g2s(ring_slot(slot) + t.b0, t.s1, t.b1, &g_sh.full[slot]);
+    if (!ring_issue(a, T, t)) return T;
     T++;
-    ahead--;
   }
   return T;
 }
@@ -446,7 +437,7 @@ __device__ __noinline__ void trace_point(const DecodeArgs &a, int k) {
   if (tid_() == 0) {
     const unsigned long long t = now_ns();
     unsigned long long *e = a.trace + 3 * k;
-    if (blockIdx.x == 0) e[0] = t;
+    if (blockIdx.x == 0) e[0] = (unsigned long long)clock64();   // CTA 0: SM cycles (exact)
     atomicMax(e + 1, t);
     atomicMin(e + 2, t);
   }
@@ -497,7 +488,7 @@ __device__ __forceinline__ void release_tile(int slot) {
 // sandwich, add goes through the post-norm island first. CTA c writes slice c of the new
 // residual to xout. The quantized row lands in the activation blocks; returns its scale.
 __device__ __noinline__ float norm_phase(const DecodeArgs &a, Cnt &c, bool embed, const float *xin,
-                                         const float *add, bool sandwich, float *xout) {
+                                         const float *add, bool sandwich, float *xout, int tr = -1) {
   const int E = a.E, tid = tid_();
   float *X = vb(0), *A = vb(1);
   if (tid == 0) {
@@ -527,6 +518,7 @@ __device__ __noinline__ float norm_phase(const DecodeArgs &a, Cnt &c, bool embed
   if (!embed) vok = wait_bar(a, &g_sh.vbar[0], (c.vp0++) & 1u) && vok;
   if (add) vok = wait_bar(a, &g_sh.vbar[1], (c.vp1++) & 1u) && vok;
   cbar();   // X complete (embedding written by all threads)
+  if (tr >= 0) trace_point(a, tr);
   bool bad = false;
   uint64_t inv = 0;
   if (add && sandwich) {
@@ -539,6 +531,7 @@ __device__ __noinline__ float norm_phase(const DecodeArgs &a, Cnt &c, bool embed
     }
     inv = rms_inv_dec(csum128(ss), E, tid == 0 ? a.err : nullptr);
   }
+  if (tr >= 0) trace_point(a, tr + 1);
   const int per = (E + (int)gridDim.x - 1) / (int)gridDim.x;
   const int lo = (int)blockIdx.x * per, hi = min(lo + per, E);
   acc128 ss{0ull, 0ll};
@@ -553,6 +546,7 @@ __device__ __noinline__ float norm_phase(const DecodeArgs &a, Cnt &c, bool embed
   }
   if (bad) raise_err(a.err, ERR_NORM_RANGE);
   inv = rms_inv_dec(csum128(ss), E, tid == 0 ? a.err : nullptr);
+  if (tr >= 0) trace_point(a, tr + 2);
   float m = 0.0f;
   for (int i = tid; i < E; i += CT) {
     const float y = rms_apply(X[i], ow[i], inv, a.err);
@@ -561,6 +555,7 @@ __device__ __noinline__ float norm_phase(const DecodeArgs &a, Cnt &c, bool embed
   }
   release_tile(slot);
   const float s = cmax_f(m);
+  if (tr >= 0) trace_point(a, tr + 3);
   if (vok) quant_smem(X, E, 0, s);
   return s;
 }
@@ -787,6 +782,7 @@ __device__ __noinline__ int64_t floordiv_dec(int64_t hi, uint64_t lo, uint64_t d
 // layer's max |ao| slot. Returns false on abort.
 template <int HD>
 __device__ __noinline__ bool attn_phase(const DecodeArgs &a, Cnt &c, int L, const DecLayer &ly, int p) {
+  const int tr = 1 + L * DEC_TRACE_PER_LAYER + 14;   // sub-phase trace points
   const int tid = tid_(), warp = warp_(), lane = lane_();
   const int G = a.NH / a.NKV, half = HD / 2;
   const int SCS = SCMAX / G;
@@ -878,6 +874,7 @@ __device__ __noinline__ bool attn_phase(const DecodeArgs &a, Cnt &c, int L, cons
     }
   }
   cbar();
+  trace_point(a, tr);
   // ---- exact scores -> the 2^14 grid; K slices through the ring
   const int sub = SLOT / (HD * 4);
   const int nsub = (ncached + sub - 1) / sub;
@@ -893,8 +890,10 @@ __device__ __noinline__ bool attn_phase(const DecodeArgs &a, Cnt &c, int L, cons
   }
   if (fits && has_new && warp == 0) score_row<HD>(a, kn(), G, ncached, SCS);
   cbar();
+  trace_point(a, tr + 1);
   if (tid < G) a.pmx[blockIdx.x * G + tid] = g_sh.mx[tid];
   if (!counter_sync(a, hctr, t1)) return false;
+  trace_point(a, tr + 2);
   // ---- head maximum (one warp per query head gathers the parts), integer exponentials,
   // their exact sum
   if (warp < G) {
@@ -917,6 +916,7 @@ __device__ __noinline__ bool attn_phase(const DecodeArgs &a, Cnt &c, int L, cons
     if (lane == 0 && part) atomicAdd(&g_sh.ssum[h], (unsigned long long)part);
   }
   cbar();
+  trace_point(a, tr + 3);
   // ---- exact V-sum: e * v split at bit 16 so both halves accumulate in int64
   const int GH = G * HD;
   int64_t vh0 = 0, vl0 = 0, vh1 = 0, vl1 = 0;   // outputs tid and tid + CT
@@ -964,7 +964,9 @@ __device__ __noinline__ bool attn_phase(const DecodeArgs &a, Cnt &c, int L, cons
     __stcg(dst + 1, (uint64_t)N.hi);
   }
   if (tid < G) __stcg(reinterpret_cast<unsigned long long *>(a.psum) + blockIdx.x * G + tid, g_sh.ssum[tid]);
+  trace_point(a, tr + 4);
   if (!counter_sync(a, hctr, t2)) return false;
+  trace_point(a, tr + 5);
   // ---- this part finalizes outputs [j*fo, (j+1)*fo) of the head group: one warp per
   // output, its lanes gather the parts' partial sums in parallel
   const int fo = (GH + ap.npart - 1) / ap.npart;
@@ -1023,7 +1025,8 @@ __device__ void consumer(const DecodeArgs &a, int p) {
     const DecLayer &ly = g_sh.ly[L % 3];
     const int tk = 1 + L * DEC_TRACE_PER_LAYER;
     // attention block
-    float s = norm_phase(a, c, L == 0, xb[cur], L ? a.dn : nullptr, L && a.gemma, xb[cur ^ 1]);
+    float s = norm_phase(a, c, L == 0, xb[cur], L ? a.dn : nullptr, L && a.gemma, xb[cur ^ 1],
+                         a.trace ? tk + 20 : -1);
     cur ^= 1;
     cbar();
     trace_point(a, tk + 0);
@@ -1134,7 +1137,121 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_decode(const __grid_constant__ 
   }
 }
 
+// ------------------------------------------------------------------------------ ring GEMV
+// The GEMV phase as a kernel of its own (batch-1 GEMVs of the multi-kernel schedule): the
+// producer warp streams this CTA's row tiles into the ring before the programmatic-dependent-
+// launch wait (the weights do not depend on the previous kernel), the consumers wait, stage
+// the quantized activation row and run gemv_phase.
+__global__ void __launch_bounds__(NTHREADS, 1) k_gemv_ring(const __grid_constant__ GemvRingArgs g) {
+  __shared__ DecodeArgs sa;
+  const int tid = threadIdx.x, warp = tid >> 5;
+  if (tid == 0) {
+    for (int s = 0; s < NSLOT; s++) {
+      mbar_init(&g_sh.full[s], 1);
+      mbar_init(&g_sh.empty[s], CW);
+    }
+    g_sh.abort = 0;
+    g_sh.issued = 0;
+    mbar_init_fence();
+    memset(&sa, 0, sizeof sa);
+    sa.err = g.err;
+    sa.amax = g.amax;
+  }
+  for (int i = tid; i < 2 * RACC; i += NTHREADS) racc()[i] = 0ull;
+  __syncthreads();
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  if (warp == CW) {
+    if ((tid & 31) == 0) {
+      const DevQ4B *w2 = g.mode == 1 || g.mode == 2 ? &g.w2 : nullptr;
+      int r, r1;
+      rows_of(g.w.rows, blockIdx.x, gridDim.x, r, r1);
+      const int K = g.w.cols, rt = tiling(K).rt;
+      uint32_t T = 0;
+      for (; r < r1; r += rt) {
+        const int rows = min(rt, r1 - r);
+        for (int m = 0; m < (w2 ? 2 : 1); m++) {
+          const DevQ4B &q = m ? *w2 : g.w;
+          Tile t{q.codes + (size_t)r * (K >> 1), reinterpret_cast<const uint8_t *>(q.scales) + (size_t)r * (K >> 4),
+                 (uint32_t)rows * (K >> 1), (uint32_t)rows * (K >> 4)};
+          if (!ring_issue(sa, T, t)) break;
+          T++;
+        }
+        if (aborted()) break;
+      }
+      g_sh.issued = T;
+    }
+    __syncwarp();
+  } else {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    // the activation row: per 32-column block, bytes 0-15 to plane 0 and 16-31 to plane 1
+    const int nblk = g.w.cols >> 5;
+    const int4 *q4 = reinterpret_cast<const int4 *>(g.act.q);
+    int4 *p0 = reinterpret_cast<int4 *>(xa()), *p1 = reinterpret_cast<int4 *>(xa() + PLANE);
+    for (int b = tid; b < nblk; b += CT) {
+      p0[b] = q4[2 * b];
+      p1[b] = q4[2 * b + 1];
+      xs()[b] = g.act.bsum[b];
+    }
+    const double dsc = act_dscale(g.act.scale[0]);
+    cbar();
+    Cnt c{0u, 0u, 0u, 0u, 0u};
+    switch (g.mode) {
+      case 0: gemv_phase<PH_STORE>(sa, c, g.w, g.w, dsc, g.y, g.ymax); break;
+      case 1: gemv_phase<PH_GELU>(sa, c, g.w, g.w2, dsc, g.y, g.ymax); break;
+      case 2: gemv_phase<PH_SILU>(sa, c, g.w, g.w2, dsc, g.y, g.ymax); break;
+      default: gemv_phase<PH_LM>(sa, c, g.w, g.w, dsc, g.y, nullptr); break;
+    }
+  }
+  __syncthreads();
+  if (tid == 0) {   // copies still in flight (only after an abort)
+    const uint32_t issued = g_sh.issued;
+    for (int s = 0; s < NSLOT; s++) {
+      if ((uint32_t)s >= issued) break;
+      const uint32_t last = issued - 1 - ((issued - 1 - (uint32_t)s) % NSLOT);
+      const uint64_t t0 = now_ns();
+      while (!mbar_try_wait(&g_sh.full[s], (last / NSLOT) & 1u))
+        if (now_ns() - t0 > WAIT_LIMIT_NS) break;
+    }
+  }
+}
+
 }  // namespace
+
+bool gemv_ring_covers(const DevQ4B &w, int mode) {
+  const int K = w.cols;
+  if (K > KMAX || (K & 255) || w.rows <= 0) return false;
+  int segs = 1;
+  while (segs * 128 < K / 32) segs <<= 1;
+  const int rt = std::min(16, SLOT / (K / 2 + K / 16));
+  if (rt * segs > 2 * CW) return false;
+  const int grid = decode_grid();
+  if (grid <= 0) return false;
+  if (mode != 3 && (((w.rows + 3) / 4 + grid - 1) / grid) * 4 > RACC) return false;
+  return (long long)((w.rows + 3) / 4) * grid <= 0x7fffffffLL;
+}
+
+cudaError_t launch_gemv_ring(const GemvRingArgs &g, cudaStream_t st, bool pdl) {
+  static int grid = 0;
+  if (grid == 0) grid = decode_grid();
+  if (grid <= 0) return cudaErrorInvalidConfiguration;
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(k_gemv_ring, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(NTHREADS);
+  cfg.dynamicSmemBytes = SMEM;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, k_gemv_ring, g);
+}
 
 const char *decode_unsupported(const DecodeArgs &a, int grid, int ctx) {
   if (grid <= 0) return "the persistent decode kernel cannot be resident on this device";

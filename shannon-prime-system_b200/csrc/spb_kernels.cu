@@ -47,6 +47,18 @@ namespace spb {
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
+// SPB_GEMV_RING=1 sends batch-1 GEMVs to the TMA-ring kernel of spb_decode.cu instead of
+// k_gemv (identical results; at the 12B shape k_gemv is faster for every matrix but the LM
+// head, where the two tie, because its ramp is shorter)
+static bool ring_gemv_enabled() {
+  static int on = -1;
+  if (on < 0) {
+    const char *e = getenv("SPB_GEMV_RING");
+    on = (e && e[0] == '1') ? 1 : 0;
+  }
+  return on != 0;
+}
+
 static int pdl_enabled() {
   static int on = -1;
   if (on < 0) {
@@ -345,6 +357,13 @@ cudaError_t launch_gemv(const DevQ4B &w, const DevQ4B *w2, const DevAct &act, in
                        amax ? amax + h : nullptr);
   }
   const DevQ4B ww2 = w2 ? *w2 : w;
+  if (ntok == 1 && grid_limit == 0 && ring_gemv_enabled()) {   // batch 1: the TMA-ring GEMV
+    const int mode = epi == EPI_GELU_MUL ? 1 : epi == EPI_SILU_MUL ? 2 : amax ? 3 : 0;
+    if (gemv_ring_covers(w, mode)) {
+      GemvRingArgs g{w, ww2, mode, act, y, ymax, amax, err};
+      return launch_gemv_ring(g, st, pdl_enabled() != 0);
+    }
+  }
   switch (epi) {
     case EPI_STORE: return gemv_nt<EPI_STORE>(w, ww2, act, ntok, y, ldy, err, ymax, amax, st, grid_limit);
     case EPI_GELU_MUL: return gemv_nt<EPI_GELU_MUL>(w, ww2, act, ntok, y, ldy, err, ymax, amax, st, grid_limit);

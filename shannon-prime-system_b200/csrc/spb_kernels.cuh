@@ -136,10 +136,12 @@ struct DecodeArgs {
   // [k][2] = the earliest CTA (host-initialised to 0 and ~0)
   unsigned long long *trace;
 };
-// trace points: DEC_TRACE_PER_LAYER per layer, then the final norm, LM head, last barrier;
-// after the points, CTA 0's per-tile record [DEC_TRACE_TILES][2]: the time the producer
-// issued the tile's copy and the time warp 0 found it complete
-constexpr int DEC_TRACE_PER_LAYER = 14;
+// trace points (column 0: CTA 0's SM clock cycles; 1, 2: %globaltimer ns of the latest and
+// the earliest CTA): DEC_TRACE_PER_LAYER per layer (14 phase ends, then 6 inside attention and 4
+// inside the first norm), then the final norm, LM head, last barrier; after the points, CTA
+// 0's per-tile record [DEC_TRACE_TILES][2]: the time the producer issued the tile's copy and
+// the time warp 0 found it complete
+constexpr int DEC_TRACE_PER_LAYER = 24;
 constexpr int DEC_TRACE_TILES = 4096;
 __host__ __device__ inline int decode_trace_points(int nl) { return 1 + nl * DEC_TRACE_PER_LAYER + 3; }
 __host__ __device__ inline int decode_trace_words(int nl) { return 3 * decode_trace_points(nl) + 2 * DEC_TRACE_TILES; }
@@ -155,6 +157,22 @@ const char *decode_unsupported(const DecodeArgs &a, int grid, int ctx);
 // CTAs the persistent kernel runs with on the current device (0 if it cannot be resident)
 int decode_grid();
 cudaError_t launch_decode(const DecodeArgs &a, int grid, cudaStream_t st);
+
+// ---- batch-1 GEMV through a TMA ring (spb_decode.cu): one CTA per SM, a producer warp
+// streaming the CTA's row tiles, 16 consumer warps. mode 0: y = W x; 1 / 2: y = gelu / silu
+// (W x) * (W2 x) with the per-row max |y| folded into ymax; 3: LM head, y = W x and the
+// greedy-argmax key folded into amax (zero on entry). act: one quantized row.
+struct GemvRingArgs {
+  DevQ4B w, w2;
+  int mode;
+  DevAct act;
+  float *y;
+  uint32_t *ymax;
+  unsigned long long *amax;
+  uint32_t *err;
+};
+bool gemv_ring_covers(const DevQ4B &w, int mode);
+cudaError_t launch_gemv_ring(const GemvRingArgs &g, cudaStream_t st, bool pdl);
 
 // store `msg` as this thread's spb_last_error() text and return `code` (host runtime)
 int record_error(int code, const char *msg);

@@ -464,10 +464,12 @@ extern "C" int spb_decode_mode(int mode) {
   return prev;
 }
 
-// the persistent kernel serves a step whose new token lands at position `pos`
-static bool use_decode_kernel(const spb_session *s, int pos) {
-  return g_decode_mode == 1 && s->dgrid > 0 && decode_unsupported(s->dargs, s->dgrid, pos + 1) == nullptr;
+// the persistent kernel can serve a step whose new token lands at position `pos`
+static bool decode_kernel_covers(const spb_session *s, int pos) {
+  return s->dgrid > 0 && decode_unsupported(s->dargs, s->dgrid, pos + 1) == nullptr;
 }
+// ... and is selected for it
+static bool use_decode_kernel(const spb_session *s, int pos) { return g_decode_mode == 1 && decode_kernel_covers(s, pos); }
 
 static size_t kv_layer_elems(const spb_model *m, int pmax) { return (size_t)m->NKV * pmax * m->HD; }
 
@@ -702,7 +704,7 @@ extern "C" int spb_session_decode_trace(spb_session *s, int32_t token, uint64_t 
   if (cap < 3 * np) return set_err(SPB_EBADARG, "spb_session_decode_trace: need %d words", 3 * np);
   if (s->pos >= s->pmax) return set_err(SPB_ECONTEXT_FULL, "spb_session_decode_trace: context full");
   CU(cudaSetDevice(s->m->device));
-  if (!use_decode_kernel(s, s->pos))
+  if (!decode_kernel_covers(s, s->pos))
     return set_err(SPB_EUNSUPPORTED, "spb_session_decode_trace: the persistent kernel does not serve this step");
   if (!s->trace_dev) CU(cudaMalloc(&s->trace_dev, (size_t)nw * 8));
   std::vector<uint64_t> init((size_t)nw, 0ull);

@@ -239,7 +239,7 @@ class Session:
     def decode_trace(self, token):
         """One decode step through the persistent kernel with its phase trace; returns an
         array [points][3] of %globaltimer ns (CTA 0, latest CTA, earliest CTA)."""
-        npts = 1 + self.model.cfg.n_layers * 14 + 3
+        npts = 1 + self.model.cfg.n_layers * 24 + 3
         out = np.zeros(3 * npts + 2 * 4096, np.uint64)
         check(load().spb_session_decode_trace(self.h, int(token), out.ctypes.data, out.size))
         return out[:3 * npts].reshape(npts, 3), out[3 * npts:].reshape(4096, 2)
