@@ -30,6 +30,7 @@
 #include "spb_exact.cuh"
 #include "spb_kernels.cuh"
 
+#include <algorithm>
 #include <cooperative_groups.h>
 #include <cuda_fp16.h>
 
@@ -341,11 +342,257 @@ static cudaError_t gemv_nt(const DevQ4B &w, const DevQ4B &w2, const DevAct &act,
   }
 }
 
+// ------------------------------------------------------------------------------ token-batch GEMM
+// 16..64 token rows at a time on the tensor cores (mma.sync m16n8k32, int8 x int8 -> int32):
+// one MMA per 32-column block gives the exact block sums of 16 tokens x 8 weight rows at once.
+// The weight operand is the code nibble shifted to the top of its byte (16 c, exact in int8),
+// so the block sum comes out times 16 and an exact arithmetic shift recovers it. Each block
+// sum is then scaled by its f16 block scale as integer mantissa and shift and accumulated in
+// int64 in registers, the same arithmetic as the GEMV, so the results are identical. The
+// activation rows are stored in the GEMV's permuted column order (per 8 columns: even, then
+// odd); the fragment layout of m16n8k32 maps k positions 0-3 of a thread to one 4-byte group,
+// which is exactly one word of low or high nibbles of the code block.
+constexpr int GEMM_THREADS = 128;   // 4 warps x 8 weight rows
+constexpr int GEMM_ROWS = 32;       // weight rows per CTA
+constexpr int GEMM_KC = 512;        // columns staged per step
+constexpr int GEMM_AP = GEMM_KC + 16;   // padded activation row (bank-conflict-free fragment loads)
+constexpr int GEMM_WP = GEMM_KC / 2 + 16;   // padded code row
+
+__device__ __forceinline__ void mma_s8(const uint32_t (&a)[4], uint32_t b0, uint32_t b1, int32_t (&c)[4]) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%12,%13};"
+      : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(0), "r"(0), "r"(0), "r"(0));
+}
+
+// f16 block scale as (signed mantissa, 2^shift), value = m * pw * 2^-24
+__device__ __forceinline__ void scale_parts(uint32_t h, int32_t &m, int32_t &pw) {
+  const uint32_t e = (h >> 10) & 31u;
+  m = (int32_t)(e ? ((h & 1023u) | 1024u) : (h & 1023u));
+  if (h & 0x8000u) m = -m;
+  pw = 1 << (e ? e - 1 : 0);
+}
+
+__device__ __forceinline__ void cp_async16(void *dst, const void *src, bool valid) {
+  // src-size 0 zero-fills the 16 destination bytes (rows past the matrix or the token count)
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)),
+               "l"(src), "r"(valid ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_prev() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+
+template <int MT, int NM>
+struct GemmSmem {
+  static constexpr int A = MT * 16 * GEMM_AP;                 // activation rows
+  static constexpr int W = NM * GEMM_ROWS * GEMM_WP;          // code rows
+  static constexpr int S = NM * GEMM_ROWS * (GEMM_KC / 32) * 2;   // block scales
+  static constexpr int STAGE = A + W + S;
+  static constexpr int TOTAL = 2 * STAGE;                     // double buffered
+};
+
+template <int MT, int EPI>
+__global__ void __launch_bounds__(GEMM_THREADS)
+k_gemm(DevQ4B w, DevQ4B w2, DevAct act, int ntok, float *__restrict__ y, int ldy, uint32_t *err, uint32_t *ymax,
+       unsigned long long *amax) {
+  constexpr int NM = (EPI == EPI_STORE) ? 1 : 2;
+  constexpr int M = MT * 16;
+  using SM = GemmSmem<MT, NM>;
+  extern __shared__ __align__(16) uint8_t gsm[];
+  __shared__ float tmax[M];
+  __shared__ unsigned long long tkey[M];
+  __shared__ double dsc[M];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, tig = lane & 3;
+  const int K = w.cols, rows = w.rows;
+  const int nch = (K + GEMM_KC - 1) / GEMM_KC;
+  pdl_trigger();
+  pdl_wait();
+  for (int t = tid; t < M; t += GEMM_THREADS) {
+    dsc[t] = t < ntok ? __dmul_rn(__ddiv_rn((double)act.scale[t], 127.0), 0x1p-24) : 0.0;
+    tmax[t] = 0.0f;
+    tkey[t] = 0ull;
+  }
+  // stage chunk ci of row block row0 into buffer `buf` (asynchronous copies, one commit group)
+  auto stage = [&](int buf, int row0, int ci) {
+    uint8_t *base = gsm + buf * SM::STAGE;
+    int8_t *A = reinterpret_cast<int8_t *>(base);
+    uint8_t *W = base + SM::A;
+    uint8_t *S = W + SM::W;
+    const int k0 = ci * GEMM_KC, kc = min(GEMM_KC, K - k0);
+    for (int i = tid; i < M * (kc >> 4); i += GEMM_THREADS) {
+      const int t = i / (kc >> 4), c = (i - t * (kc >> 4)) << 4;
+      const bool ok = t < ntok;
+      cp_async16(A + t * GEMM_AP + c, act.q + (size_t)(ok ? t : 0) * K + k0 + c, ok);
+    }
+#pragma unroll
+    for (int m = 0; m < NM; m++) {
+      const DevQ4B &q = m ? w2 : w;
+      for (int i = tid; i < GEMM_ROWS * (kc >> 5); i += GEMM_THREADS) {   // 16 code bytes per block
+        const int r = i / (kc >> 5), b = i - r * (kc >> 5);
+        const bool ok = row0 + r < rows;
+        cp_async16(W + (m * GEMM_ROWS + r) * GEMM_WP + b * 16,
+                   q.codes + (size_t)(ok ? row0 + r : 0) * (K >> 1) + (size_t)((k0 >> 5) + b) * 16, ok);
+      }
+      const uint8_t *sc = reinterpret_cast<const uint8_t *>(q.scales);
+      for (int i = tid; i < GEMM_ROWS * (kc >> 8); i += GEMM_THREADS) {   // 8 block scales per 16 bytes
+        const int r = i / (kc >> 8), j = i - r * (kc >> 8);
+        const bool ok = row0 + r < rows;
+        cp_async16(S + ((m * GEMM_ROWS + r) * (GEMM_KC / 32)) * 2 + j * 16,
+                   sc + (size_t)(ok ? row0 + r : 0) * (K >> 4) + (k0 >> 4) + j * 16, ok);
+      }
+    }
+    cp_async_commit();
+  };
+  for (int rb = blockIdx.x; rb * GEMM_ROWS < rows; rb += gridDim.x) {
+    const int row0 = rb * GEMM_ROWS;
+    int64_t acc[NM][MT][4];
+#pragma unroll
+    for (int m = 0; m < NM; m++)
+#pragma unroll
+      for (int mt = 0; mt < MT; mt++)
+#pragma unroll
+        for (int i = 0; i < 4; i++) acc[m][mt][i] = 0;
+    __syncthreads();   // both buffers are free
+    stage(0, row0, 0);
+    for (int ci = 0; ci < nch; ci++) {
+      if (ci + 1 < nch) stage((ci + 1) & 1, row0, ci + 1);
+      else cp_async_commit();   // an empty group keeps the wait count uniform
+      cp_async_wait_prev();
+      __syncthreads();
+      const uint8_t *base = gsm + (ci & 1) * SM::STAGE;
+      const int8_t *A = reinterpret_cast<const int8_t *>(base);
+      const uint8_t *W = base + SM::A;
+      const uint16_t *S = reinterpret_cast<const uint16_t *>(W + SM::W);
+      const int kc = min(GEMM_KC, K - ci * GEMM_KC);
+      for (int kb = 0; kb < (kc >> 5); kb++) {
+        uint32_t af[MT][4];
+#pragma unroll
+        for (int mt = 0; mt < MT; mt++) {
+          const int8_t *ab = A + (mt * 16 + g) * GEMM_AP + kb * 32 + tig * 4;
+          af[mt][0] = *reinterpret_cast<const uint32_t *>(ab);
+          af[mt][1] = *reinterpret_cast<const uint32_t *>(ab + 8 * GEMM_AP);
+          af[mt][2] = *reinterpret_cast<const uint32_t *>(ab + 16);
+          af[mt][3] = *reinterpret_cast<const uint32_t *>(ab + 8 * GEMM_AP + 16);
+        }
+#pragma unroll
+        for (int m = 0; m < NM; m++) {
+          const uint32_t *wr = reinterpret_cast<const uint32_t *>(W + (m * GEMM_ROWS + warp * 8 + g) * GEMM_WP + kb * 16);
+          const uint32_t w0 = wr[tig >> 1], w1 = wr[2 + (tig >> 1)];
+          const uint32_t b0 = (tig & 1) ? (w0 & 0xF0F0F0F0u) : ((w0 << 4) & 0xF0F0F0F0u);
+          const uint32_t b1 = (tig & 1) ? (w1 & 0xF0F0F0F0u) : ((w1 << 4) & 0xF0F0F0F0u);
+          const uint16_t *sr = S + (m * GEMM_ROWS + warp * 8 + tig * 2) * (GEMM_KC / 32) + kb;
+          int32_t m0, p0, m1, p1;
+          scale_parts(sr[0], m0, p0);
+          scale_parts(sr[GEMM_KC / 32], m1, p1);
+#pragma unroll
+          for (int mt = 0; mt < MT; mt++) {
+            int32_t c[4];
+            mma_s8(af[mt], b0, b1, c);
+            acc[m][mt][0] += (int64_t)((c[0] >> 4) * m0) * (int64_t)p0;   // token g,   row 2 tig
+            acc[m][mt][1] += (int64_t)((c[1] >> 4) * m1) * (int64_t)p1;   // token g,   row 2 tig + 1
+            acc[m][mt][2] += (int64_t)((c[2] >> 4) * m0) * (int64_t)p0;   // token g+8, row 2 tig
+            acc[m][mt][3] += (int64_t)((c[3] >> 4) * m1) * (int64_t)p1;   // token g+8, row 2 tig + 1
+          }
+        }
+      }
+      __syncthreads();   // buffer ci & 1 may be refilled by the next stage
+    }
+    // epilogue: (token, row) of each accumulator
+#pragma unroll
+    for (int mt = 0; mt < MT; mt++) {
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        const int t = mt * 16 + g + (i >= 2 ? 8 : 0);
+        const int row = row0 + warp * 8 + tig * 2 + (i & 1);
+        if (t >= ntok || row >= rows) continue;
+        float v = __double2float_rn(__dmul_rn(__ll2double_rn(acc[0][mt][i]), dsc[t]));
+        if (EPI != EPI_STORE) {
+          const float u = __double2float_rn(__dmul_rn(__ll2double_rn(acc[NM - 1][mt][i]), dsc[t]));
+          if (!(fabsf(v) < 2048.0f)) { raise_err(err, ERR_ACT_RANGE); v = 0.0f; }
+          v = __fmul_rn(EPI == EPI_GELU_MUL ? gelu_exact(v) : silu_exact(v), u);
+        }
+        y[(size_t)t * ldy + row] = v;
+        if (ymax) atomicMax(reinterpret_cast<unsigned int *>(&tmax[t]), __float_as_uint(fabsf(v)));
+        if (amax) atomicMax(&tkey[t], argmax_key(v, row));
+      }
+    }
+  }
+  __syncthreads();
+  for (int t = tid; t < ntok; t += GEMM_THREADS) {
+    if (ymax) {
+      const float m = tmax[t];
+      if (!(m <= 3.402823466e38f)) raise_err(err, ERR_ACT_RANGE);
+      else if (m > 0.0f) atomicMax(ymax + t, __float_as_uint(m));
+    }
+    if (amax && tkey[t]) atomicMax(amax + t, tkey[t]);
+  }
+}
+
+template <int MT, int EPI>
+static cudaError_t gemm_launch(const DevQ4B &w, const DevQ4B &w2, const DevAct &act, int ntok, float *y, int ldy,
+                               uint32_t *err, uint32_t *ymax, unsigned long long *amax, cudaStream_t st) {
+  constexpr int NM = (EPI == EPI_STORE) ? 1 : 2;
+  const size_t smem = GemmSmem<MT, NM>::TOTAL;
+  auto kern = k_gemm<MT, EPI>;
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  int dev = 0, nsm = 148, occ = 1;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, GEMM_THREADS, smem);
+  const int nrb = (w.rows + GEMM_ROWS - 1) / GEMM_ROWS;
+  const int grid = std::min(nrb, nsm * std::max(occ, 1));
+  return launch_k(kern, dim3(grid), dim3(GEMM_THREADS), smem, st, 1, w, w2, act, ntok, y, ldy, err, ymax, amax);
+}
+
+template <int EPI>
+static cudaError_t gemm_mt(const DevQ4B &w, const DevQ4B &w2, const DevAct &act, int ntok, float *y, int ldy,
+                           uint32_t *err, uint32_t *ymax, unsigned long long *amax, cudaStream_t st) {
+  switch ((ntok + 15) / 16) {
+    case 1: return gemm_launch<1, EPI>(w, w2, act, ntok, y, ldy, err, ymax, amax, st);
+    case 2: return gemm_launch<2, EPI>(w, w2, act, ntok, y, ldy, err, ymax, amax, st);
+    case 3: return gemm_launch<3, EPI>(w, w2, act, ntok, y, ldy, err, ymax, amax, st);
+    default: return gemm_launch<4, EPI>(w, w2, act, ntok, y, ldy, err, ymax, amax, st);
+  }
+}
+
+// SPB_GEMM=0 keeps token batches on the dp4a k_gemv (comparisons; results are identical)
+static bool gemm_enabled() {
+  static int on = -1;
+  if (on < 0) {
+    const char *e = getenv("SPB_GEMM");
+    on = (e && e[0] == '0') ? 0 : 1;
+  }
+  return on != 0;
+}
+
 cudaError_t launch_gemv(const DevQ4B &w, const DevQ4B *w2, const DevAct &act, int ntok, float *y, int ldy,
                         int epi, uint32_t *err, cudaStream_t st, int grid_limit, uint32_t *ymax,
                         unsigned long long *amax) {
   if ((w.cols & 31) || w.cols <= 0 || w.rows <= 0 || w.cols > 16384) return cudaErrorInvalidValue;
   if (epi != EPI_STORE && (!w2 || w2->rows != w.rows || w2->cols != w.cols)) return cudaErrorInvalidValue;
+  if (ntok >= 16 && grid_limit == 0 && (w.cols & 255) == 0 && gemm_enabled()) {   // token batches: tensor-core GEMM
+    const DevQ4B ww2 = w2 ? *w2 : w;
+    for (int t0 = 0; t0 < ntok; t0 += 64) {
+      const int n = std::min(64, ntok - t0);
+      const DevAct a2{act.q + (size_t)t0 * w.cols, act.bsum + (size_t)t0 * (w.cols >> 5), act.scale + t0};
+      float *y2 = y + (size_t)t0 * ldy;
+      uint32_t *ym = ymax ? ymax + t0 : nullptr;
+      unsigned long long *am = amax ? amax + t0 : nullptr;
+      cudaError_t e;
+      switch (epi) {
+        case EPI_STORE: e = gemm_mt<EPI_STORE>(w, ww2, a2, n, y2, ldy, err, ym, am, st); break;
+        case EPI_GELU_MUL: e = gemm_mt<EPI_GELU_MUL>(w, ww2, a2, n, y2, ldy, err, ym, am, st); break;
+        default: e = gemm_mt<EPI_SILU_MUL>(w, ww2, a2, n, y2, ldy, err, ym, am, st); break;
+      }
+      if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
+  }
   // the staged activations of all rows must fit shared memory: split the token rows
   const size_t per_tok = (size_t)w.cols + (size_t)(w.cols >> 5) * 4 + 8;
   if (ntok > 1 && per_tok * ntok > 160 * 1024) {

@@ -2,8 +2,8 @@
 // exact KV sessions, the per-token kernel schedule (captured once as a CUDA graph),
 // integer RoPE/CORDIC tables, and the C ABI declared in include/spb200.h.
 //
-// Schedule of one token row (decode; prefill runs the same schedule on chunks of
-// up to 16 rows through the multi-row GEMV):
+// Schedule of one token row (decode; prefill runs the same schedule on chunks of up to 64
+// rows, whose GEMVs become the tensor-core token-batch GEMM from 16 rows on):
 //   embed -> per layer { norm(+residual)+quant -> GEMV Q|K|V -> QK-norm+CORDIC-RoPE+KV
 //   store -> cluster attention -> quant -> GEMV O -> norm(+sandwich)+quant -> GEMV
 //   gate|up with the exact GELU/SiLU * up epilogue -> quant -> GEMV down }
@@ -431,7 +431,7 @@ extern "C" void spb_model_free(spb_model *m) {
 extern "C" int64_t spb_model_weight_bytes(const spb_model *m) { return m ? m->stream_bytes : 0; }
 
 // ------------------------------------------------------------------------------ session
-constexpr int NT_MAX = 16;
+constexpr int NT_MAX = 64;   // token rows per schedule pass (prefill chunk)
 
 struct spb_session {
   spb_model *m;
