@@ -61,6 +61,9 @@ def parse():
     # with either set is not the configs[2] measurement and says so in config.workload
     p.add_argument("--layers", type=int, default=0)
     p.add_argument("--vocab", type=int, default=0)
+    p.add_argument("--batch", type=int, default=64,
+                   help="sessions decoded together for the b64 figure (0: skip it)")
+    p.add_argument("--batch-steps", type=int, default=16)
     return p.parse_args()
 
 
@@ -251,6 +254,42 @@ def trace_report(tr, n_layers, sm_mhz=1965.0):
     return out
 
 
+def measure_batch(m, cfg, B, K, W, seed, max_over_ranks):
+    """B independent sessions (seeded ragged contexts, U[128, 512] tokens each) decoding
+    greedily together through spb_batch_decode_step: B*K tokens over the time of K steps
+    (each call puts the B tokens H2D and reads the B argmaxes D2H; max over ranks)."""
+    import torch
+    import spb200
+    import spmodel
+    rng = np.random.default_rng(seed + 999)
+    ctx = rng.integers(128, 513, size=B)
+    pmax = int(ctx.max()) + W + K + 8
+    sessions, toks = [], []
+    t0 = time.perf_counter()
+    for i in range(B):
+        s = m.session(pmax)
+        t = spmodel.gen_tokens(seed + 2000 + i, int(ctx[i]), cfg.n_vocab)
+        s.prefill(t, logits=False)
+        sessions.append(s)
+        toks.append(int(t[-1]))
+    prefill_s = time.perf_counter() - t0
+    for _ in range(W):
+        _, am = spb200.batch_decode(sessions, toks, logits=False)
+        toks = am
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(K):
+        _, am = spb200.batch_decode(sessions, toks, logits=False)
+        toks = am
+    dt = max_over_ranks((time.perf_counter() - t0) * 1e3) / 1e3
+    for s in sessions:
+        s.close()
+    return {"value": B * K / dt, "unit": "tokens/s", "sessions": B, "steps": K, "warmup": W,
+            "ms_per_step": round(dt / K * 1e3, 3), "ctx": "seeded U[128, 512] tokens per session",
+            "timing": "wall clock around K synchronous spb_batch_decode_step calls (B tokens H2D, "
+                      "B argmaxes D2H per step)", "prefill_s_untimed": round(prefill_s, 2)}
+
+
 def tile_report(tiles, pts):
     """CTA 0's ring tiles: copy latency (issue -> found complete) and the gap between
     consecutive issues, as percentiles, over the last 256 tiles of the step (the LM head)."""
@@ -358,6 +397,11 @@ def run_spb(args):
         print(json.dumps({"decode_phase_trace_us": trace_report(pts, cfg.n_layers, clk.get("sm_mhz") or 1965.0),
                           "tile_latency_us": tile_report(tiles, pts)}), file=sys.stderr)
 
+    b64 = None
+    if args.batch > 0:
+        b64 = measure_batch(m, cfg, args.batch, args.batch_steps, 3, args.seed + rank, max_over_ranks)
+        b64["value"] = round(world * b64["value"], 3)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         sys.path.insert(0, ORACLE)
@@ -386,6 +430,7 @@ def run_spb(args):
         "clocks": clk,
         "roofline": roof,
         "cpu_baseline": cpu,
+        "b64": b64,
     }
     s.close()
     m.free()

@@ -116,6 +116,13 @@ int  spb_decode_mode(int mode);
  * With cap >= that + 8192, the next 8192 words are CTA 0's first 4096 ring tiles as
  * (copy issued, found complete) time pairs. */
 int  spb_session_decode_trace(spb_session *s, int32_t token, uint64_t *out, int cap);
+/* One decode step for B (1..64) sessions of one model at once, each at its own position:
+ * tokens[B] in, full-vocab logits [B][n_vocab] (host, or NULL) and the greedy argmaxes [B]
+ * (host, or NULL) out, every position advanced by one. Same bytes as B separate
+ * spb_session_decode_step calls; the weights are streamed once for all B rows. ss[0] runs
+ * the step on its stream; the sessions must be distinct. */
+int  spb_batch_decode_step(spb_session *const *ss, int B, const int32_t *tokens, float *logits,
+                           int32_t *argmax);
 int  spb_session_rewind(spb_session *s, int n);          /* O(1): position -= n */
 int  spb_session_position(const spb_session *s);         /* -1 on NULL */
 int  spb_session_clone(const spb_session *s, spb_session **out);   /* deep KV copy */

@@ -575,7 +575,9 @@ cudaError_t launch_gemv(const DevQ4B &w, const DevQ4B *w2, const DevAct &act, in
                         unsigned long long *amax) {
   if ((w.cols & 31) || w.cols <= 0 || w.rows <= 0 || w.cols > 16384) return cudaErrorInvalidValue;
   if (epi != EPI_STORE && (!w2 || w2->rows != w.rows || w2->cols != w.cols)) return cudaErrorInvalidValue;
-  if (ntok >= 16 && grid_limit == 0 && (w.cols & 255) == 0 && gemm_enabled()) {   // token batches: tensor-core GEMM
+  // token batches (and row counts the k_gemv templates do not cover): the tensor-core GEMM
+  const bool odd = ntok > 1 && (ntok & (ntok - 1)) != 0;
+  if ((ntok >= 16 || odd) && grid_limit == 0 && (w.cols & 255) == 0 && (gemm_enabled() || odd)) {
     const DevQ4B ww2 = w2 ? *w2 : w;
     for (int t0 = 0; t0 < ntok; t0 += 64) {
       const int n = std::min(64, ntok - t0);
@@ -909,13 +911,27 @@ __global__ void k_rope_kv(RopeArgs a) {
   const int head = blockIdx.x, t = blockIdx.y;
   const int HD = a.HD, half = HD >> 1, QD = a.NH * HD, KVD = a.NKV * HD;
   const float *row = a.qkv + (size_t)t * (QD + 2 * KVD);
-  const int p = a.pos_dev[0] + t;
+  int p, P;
+  int32_t *kc, *vc;
+  if (a.rows) {   // row t of a multi-session batch: its own session's position and cache
+    const BatchRow br = a.rows[t];
+    p = br.pos;
+    P = br.P;
+    const size_t lo = (size_t)a.layer * a.NKV * P * HD;
+    kc = br.kc + lo;
+    vc = br.vc + lo;
+  } else {
+    p = a.pos_dev[0] + t;
+    P = a.P;
+    kc = a.kc;
+    vc = a.vc;
+  }
   const int i = threadIdx.x;   // pair index, blockDim.x == half
   if (a.zero_slot && head == 0 && i == 0) a.zero_slot[t] = 0u;
   if (head >= a.NH + a.NKV) {  // V head: quantize to the 2^16 grid
     const int g = head - a.NH - a.NKV;
     const float *src = row + QD + KVD + g * HD;
-    int32_t *dst = a.vc + ((size_t)g * a.P + p) * HD;
+    int32_t *dst = vc + ((size_t)g * P + p) * HD;
 #pragma unroll
     for (int r = 0; r < 2; r++) {
       const float v = src[i + r * half];
@@ -941,7 +957,7 @@ __global__ void k_rope_kv(RopeArgs a) {
   const uint64_t phase = (uint64_t)(int64_t)p * a.W[i];
   int32_t oa, ob;
   cordic_rotate(vals[i], vals[i + half], phase, a.T, a.gain, oa, ob, a.err);
-  int32_t *dst = is_q ? a.qi + (size_t)t * QD + hh * HD : a.kc + ((size_t)hh * a.P + p) * HD;
+  int32_t *dst = is_q ? a.qi + (size_t)t * QD + hh * HD : kc + ((size_t)hh * P + p) * HD;
   dst[i] = oa;
   dst[i + half] = ob;
 }
@@ -983,7 +999,21 @@ __global__ void __launch_bounds__(ATTN_THREADS) k_attn(AttnArgs a, int cmax) {
   const int rank = (int)cluster.block_rank();
   const int g = blockIdx.y, t = blockIdx.z;
   const int QD = a.NH * HD;
-  const int p = a.pos_dev[0] + t;
+  int p, P;
+  const int32_t *kcl, *vcl;
+  if (a.rows) {   // row t of a multi-session batch: its own session's position and cache
+    const BatchRow br = a.rows[t];
+    p = br.pos;
+    P = br.P;
+    const size_t lo = (size_t)a.layer * a.NKV * P * HD;
+    kcl = br.kc + lo;
+    vcl = br.vc + lo;
+  } else {
+    p = a.pos_dev[0] + t;
+    P = a.P;
+    kcl = a.kc;
+    vcl = a.vc;
+  }
   const int s0 = (a.win >= 0 && p - a.win + 1 > 0) ? p - a.win + 1 : 0;
   const int n = p - s0 + 1;
   const int c = (n + CL - 1) / CL;
@@ -992,8 +1022,8 @@ __global__ void __launch_bounds__(ATTN_THREADS) k_attn(AttnArgs a, int cmax) {
   const int cn = max(c1 - c0, 0);
   const int nsub = (cn + SUB - 1) / SUB;
   const int total = 2 * nsub;                 // K slices, then V slices
-  const int32_t *kbase = a.kc + (size_t)g * a.P * HD;
-  const int32_t *vbase = a.vc + (size_t)g * a.P * HD;
+  const int32_t *kbase = kcl + (size_t)g * P * HD;
+  const int32_t *vbase = vcl + (size_t)g * P * HD;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 
   auto issue = [&](int i) {                   // one bulk copy: slice i -> ring stage i % STAGES
@@ -1008,7 +1038,7 @@ __global__ void __launch_bounds__(ATTN_THREADS) k_attn(AttnArgs a, int cmax) {
 
   // K/V rows before this launch's first new position were written by earlier steps, so a
   // CTA whose slice ends before it can start its copies before the predecessor finishes
-  const bool early = c1 <= a.pos_dev[0];
+  const bool early = c1 <= (a.rows ? p : a.pos_dev[0]);
   pdl_trigger();
   if (threadIdx.x == 0) {
     for (int s = 0; s < ATTN_STAGES; s++) mbar_init(&full[s], 1);
@@ -1238,8 +1268,7 @@ cudaError_t launch_embed(const DevQ4B &emb, const int32_t *tok_dev, int ntok, fl
 __global__ void k_argmax_take(unsigned long long *keys, int ntok, int32_t *out) {
   pdl_trigger();
   pdl_wait();
-  const int t = threadIdx.x;
-  if (t < ntok) {
+  for (int t = threadIdx.x; t < ntok; t += blockDim.x) {
     const unsigned long long k = keys[t];
     out[t] = (int32_t)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull));
     keys[t] = 0ull;
@@ -1247,7 +1276,7 @@ __global__ void k_argmax_take(unsigned long long *keys, int ntok, int32_t *out) 
 }
 
 cudaError_t launch_argmax_take(unsigned long long *keys, int ntok, int32_t *out, cudaStream_t st) {
-  return launch_k(k_argmax_take, dim3(1), dim3(32), 0, st, 1, keys, ntok, out);
+  return launch_k(k_argmax_take, dim3(1), dim3(128), 0, st, 1, keys, ntok, out);
 }
 
 __global__ void k_advance(int32_t *pos_dev, int n, const int32_t *src_tok, int32_t *dst_tok) {

@@ -60,6 +60,13 @@ cudaError_t launch_norm(float *x, const float *add, const float *add_w, const fl
                         int ntok, const DevAct &act, float *nx_out, uint32_t *err, cudaStream_t st,
                         uint32_t *zero_slot = nullptr);
 
+// One token row of a multi-session batch: its session's K/V cache base (layer 0,
+// [NL][NKV][P][HD]), the row's position and the session's capacity P.
+struct BatchRow {
+  int32_t *kc, *vc;
+  int32_t pos, P;
+};
+
 struct RopeArgs {
   const float *qkv;        // [ntok][QD + 2*KVD] projections
   int32_t *qi;             // [ntok][QD] rotated q on the 2^16 grid
@@ -72,6 +79,8 @@ struct RopeArgs {
   int NH, NKV, HD, P, ntok;
   uint32_t *err;
   uint32_t *zero_slot;     // nullable: per-row max slots cleared for the attention output
+  const BatchRow *rows;    // nullable: rows of different sessions (kc, vc, P, pos_dev unused)
+  int layer;               // with rows: the layer whose cache rows are written
 };
 cudaError_t launch_rope_kv(const RopeArgs &a, cudaStream_t st);
 
@@ -84,6 +93,9 @@ struct AttnArgs {
   float ascale;
   uint32_t *err;
   uint32_t *ao_max;        // nullable: per-row atomicMax of the f32 bits of max |ao|
+  const BatchRow *rows;    // nullable: rows of different sessions (kc, vc, pos_dev unused;
+                           // P = the largest capacity, sizes the shared memory)
+  int layer;               // with rows: the layer whose cache rows are read
 };
 cudaError_t launch_attn(const AttnArgs &a, cudaStream_t st);
 

@@ -448,6 +448,9 @@ struct spb_session {
   uint32_t *ao_max, *gg_max;      // [NT_MAX] per-row max |y| slots (f32 bits) of the producers
   unsigned long long *amax_keys;  // [NT_MAX] greedy-argmax keys of the LM head (zero between steps)
   int32_t *h_pinned = nullptr;    // pinned staging: [0..NT_MAX) tokens, [NT_MAX] err, [NT_MAX+1] argmax
+  BatchRow *rows_dev = nullptr;   // [NT_MAX] rows of a multi-session batch led by this session
+  BatchRow *h_rows = nullptr;     // pinned staging for rows_dev
+  int32_t *h_argmax = nullptr;    // pinned [NT_MAX] batch argmaxes
   cudaGraphExec_t step_graph = nullptr;
   int dgrid = 0;                  // CTAs of the persistent decode kernel (0: not available)
   DecodeArgs dargs{};             // its arguments (fixed for the session's lifetime)
@@ -494,6 +497,7 @@ extern "C" int spb_session_open(spb_model *m, int pmax, spb_session **out) {
   const size_t o_as = take(NT_MAX * 4), o_pos = take(4), o_tok = take(NT_MAX * 4), o_am = take(NT_MAX * 4);
   const size_t o_hist = take((size_t)pmax * 4), o_err = take(4), o_slots = take(2 * NT_MAX * 4);
   const size_t o_keys = take(NT_MAX * 8);
+  const size_t o_rows = take(NT_MAX * sizeof(BatchRow));
   const int G = m->NH / m->NKV;
   s->dgrid = decode_grid();
   (void)cudaGetLastError();
@@ -513,6 +517,7 @@ extern "C" int spb_session_open(spb_model *m, int pmax, spb_session **out) {
   s->hist_dev = (int32_t *)(B + o_hist); s->err_dev = (uint32_t *)(B + o_err);
   s->ao_max = (uint32_t *)(B + o_slots); s->gg_max = s->ao_max + NT_MAX;
   s->amax_keys = (unsigned long long *)(B + o_keys);
+  s->rows_dev = (BatchRow *)(B + o_rows);
   {
     DecodeArgs &a = s->dargs;
     a.layers = m->dec_layers; a.embd = m->embd; a.out = m->out; a.out_norm = m->out_norm;
@@ -529,6 +534,8 @@ extern "C" int spb_session_open(spb_model *m, int pmax, spb_session **out) {
   }
   e = cudaStreamCreateWithFlags(&s->st, cudaStreamNonBlocking);
   if (e == cudaSuccess) e = cudaMallocHost(&s->h_pinned, (NT_MAX + 4) * 4);
+  if (e == cudaSuccess) e = cudaMallocHost(&s->h_rows, NT_MAX * sizeof(BatchRow));
+  if (e == cudaSuccess) e = cudaMallocHost(&s->h_argmax, NT_MAX * 4);
   if (e == cudaSuccess) e = cudaMemsetAsync(s->buf, 0, off, s->st);
   if (e == cudaSuccess) e = cudaStreamSynchronize(s->st);
   if (e != cudaSuccess) { spb_session_close(s); return set_err(SPB_ECUDA, "spb_session_open: %s", cudaGetErrorString(e)); }
@@ -544,6 +551,8 @@ extern "C" void spb_session_close(spb_session *s) {
   cudaFree(s->trace_dev);
   if (s->st) cudaStreamDestroy(s->st);
   cudaFreeHost(s->h_pinned);
+  cudaFreeHost(s->h_rows);
+  cudaFreeHost(s->h_argmax);
   cudaFree(s->buf);
   delete s;
 }
@@ -551,8 +560,11 @@ extern "C" void spb_session_close(spb_session *s) {
 extern "C" void *spb_session_stream(spb_session *s) { return s ? (void *)s->st : nullptr; }
 extern "C" int spb_session_position(const spb_session *s) { return s ? s->pos : -1; }
 
-// Enqueue the schedule for nt rows (tokens already in tok_dev, positions at pos_dev).
-static cudaError_t enqueue_rows(spb_session *s, int nt, bool want_logits) {
+// Enqueue the schedule for nt rows (tokens already in tok_dev, positions at pos_dev). With
+// rows (device, [nt]), row t belongs to its own session: RoPE/KV store and attention use that
+// session's cache and position; Pmax is the largest of their capacities.
+static cudaError_t enqueue_rows(spb_session *s, int nt, bool want_logits, const BatchRow *rows = nullptr,
+                                int Pmax = 0) {
   spb_model *m = s->m;
   cudaStream_t st = s->st;
   const int E = m->E, QKV = m->QD + 2 * m->KVD;
@@ -574,7 +586,8 @@ static cudaError_t enqueue_rows(spb_session *s, int nt, bool want_logits) {
       K(launch_norm(s->x, s->dn, m->gemma ? p.post_ffw : nullptr, d.attn_norm, E, nt, s->act, nullptr, s->err_dev, st));
     }
     K(launch_gemv(d.qkv, nullptr, s->act, nt, s->qkv, QKV, EPI_STORE, s->err_dev, st));
-    RopeArgs ra;
+    RopeArgs ra{};
+    ra.rows = rows; ra.layer = L;
     ra.qkv = s->qkv; ra.qi = s->qi; ra.kc = s->kc + (size_t)L * kvl; ra.vc = s->vc + (size_t)L * kvl;
     ra.q_norm = d.q_norm; ra.k_norm = d.k_norm;
     ra.W = m->tabs + 32 + (d.global ? 0 : m->HD / 2);
@@ -582,9 +595,10 @@ static cudaError_t enqueue_rows(spb_session *s, int nt, bool want_logits) {
     ra.NH = m->NH; ra.NKV = m->NKV; ra.HD = m->HD; ra.P = s->pmax; ra.ntok = nt; ra.err = s->err_dev;
     ra.zero_slot = s->ao_max;
     K(launch_rope_kv(ra, st));
-    AttnArgs aa;
+    AttnArgs aa{};
+    aa.rows = rows; aa.layer = L;
     aa.qi = s->qi; aa.kc = ra.kc; aa.vc = ra.vc; aa.ao = s->ao; aa.pos_dev = s->pos_dev;
-    aa.NH = m->NH; aa.NKV = m->NKV; aa.HD = m->HD; aa.P = s->pmax; aa.win = d.win; aa.ntok = nt;
+    aa.NH = m->NH; aa.NKV = m->NKV; aa.HD = m->HD; aa.P = rows ? Pmax : s->pmax; aa.win = d.win; aa.ntok = nt;
     aa.ascale = ascale; aa.err = s->err_dev; aa.ao_max = s->ao_max;
     K(launch_attn(aa, st));
     K(launch_quant(s->ao, m->QD, m->QD, nt, s->act, s->ao_max, s->err_dev, st));
@@ -724,6 +738,47 @@ extern "C" int spb_session_decode_trace(spb_session *s, int32_t token, uint64_t 
 
 extern "C" int spb_session_decode_step(spb_session *s, int32_t token, float *logits) {
   return spb_session_decode_step_argmax(s, token, logits, nullptr);
+}
+
+// One decode step for B sessions at once (each at its own position): one pass of the schedule
+// over B token rows, so every weight matrix is streamed once for all of them and the GEMVs
+// become the token-batch GEMM. ss[0] leads: its stream and scratch rows run the step.
+extern "C" int spb_batch_decode_step(spb_session *const *ss, int B, const int32_t *tokens, float *logits,
+                                     int32_t *argmax) {
+  if (!ss || !tokens || B <= 0 || B > NT_MAX) return set_err(SPB_EBADARG, "spb_batch_decode_step: B in [1, %d]", NT_MAX);
+  spb_session *lead = ss[0];
+  if (!lead) return set_err(SPB_EBADARG, "spb_batch_decode_step: null session");
+  int Pmax = 0;
+  for (int i = 0; i < B; i++) {
+    spb_session *s = ss[i];
+    if (!s || s->m != lead->m) return set_err(SPB_EBADARG, "spb_batch_decode_step: sessions must share one model");
+    if (s->pos >= s->pmax) return set_err(SPB_ECONTEXT_FULL, "spb_batch_decode_step: session %d context full", i);
+    for (int j = 0; j < i; j++)
+      if (ss[j] == s) return set_err(SPB_EBADARG, "spb_batch_decode_step: session %d repeated", i);
+    Pmax = std::max(Pmax, s->pmax);
+  }
+  CU(cudaSetDevice(lead->m->device));
+  for (int i = 1; i < B; i++) CU(cudaStreamSynchronize(ss[i]->st));   // their caches are settled
+  for (int i = 0; i < B; i++) {
+    lead->h_pinned[i] = tokens[i];
+    lead->h_rows[i] = BatchRow{ss[i]->kc, ss[i]->vc, ss[i]->pos, ss[i]->pmax};
+  }
+  CU(cudaMemcpyAsync(lead->tok_dev, lead->h_pinned, (size_t)B * 4, cudaMemcpyHostToDevice, lead->st));
+  CU(cudaMemcpyAsync(lead->rows_dev, lead->h_rows, (size_t)B * sizeof(BatchRow), cudaMemcpyHostToDevice, lead->st));
+  CU(enqueue_rows(lead, B, true, lead->rows_dev, Pmax));
+  if (logits)
+    CU(cudaMemcpyAsync(logits, lead->logits, (size_t)B * lead->m->V * 4, cudaMemcpyDeviceToHost, lead->st));
+  CU(cudaMemcpyAsync(lead->h_argmax, lead->argmax_dev, (size_t)B * 4, cudaMemcpyDeviceToHost, lead->st));
+  int rc = collect_errors(lead);
+  if (rc) return rc;   // no position moved
+  if (argmax) memcpy(argmax, lead->h_argmax, (size_t)B * 4);
+  for (int i = 0; i < B; i++) {
+    ss[i]->pos += 1;
+    rc = sync_pos(ss[i]);
+    if (rc) return rc;
+  }
+  for (int i = 0; i < B; i++) CU(cudaStreamSynchronize(ss[i]->st));
+  return SPB_OK;
 }
 
 extern "C" int spb_session_decode_greedy(spb_session *s, int32_t token, int n_steps, int32_t *tokens_out) {

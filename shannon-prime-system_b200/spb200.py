@@ -29,7 +29,7 @@ CORE_SYMBOLS = [
     "spb_gemv_q4b_gated_q", "spb_rmsnorm_exact_dev", "spb_gelu_exact_dev",
     "spb_silu_exact_dev", "spb_rope_cordic_dev", "spb_take_device_errors", "spb_rope_freq_table",
     "spb_cordic_tables", "spb_graph_begin", "spb_graph_end", "spb_graph_launch", "spb_graph_free",
-    "spb_decode_mode", "spb_session_decode_trace",
+    "spb_decode_mode", "spb_session_decode_trace", "spb_batch_decode_step",
 ]
 L1_SYMBOLS = ["spb_l1_forward", "spb_l1_backend", "spb_l1_kvdecode_table", "spb_l1_kvdecode_clone",
               "spb_l1_set_device", "spb_l1_release_model"]
@@ -124,6 +124,7 @@ def load(path: str = CORE_SO):
         "spb_session_decode_step_argmax": ([vp, i32, vp, vp], C.c_int),
         "spb_session_decode_greedy": ([vp, i32, C.c_int, vp], C.c_int),
         "spb_decode_mode": ([C.c_int], C.c_int),
+        "spb_batch_decode_step": ([vp, C.c_int, vp, vp, vp], C.c_int),
         "spb_session_decode_trace": ([vp, i32, vp, C.c_int], C.c_int),
         "spb_session_rewind": ([vp, C.c_int], C.c_int), "spb_session_position": ([vp], C.c_int),
         "spb_session_clone": ([vp, C.POINTER(vp)], C.c_int), "spb_session_close": ([vp], None),
@@ -273,6 +274,20 @@ class Session:
         if self.h:
             load().spb_session_close(self.h)
             self.h = None
+
+
+def batch_decode(sessions, tokens, logits=True):
+    """One decode step for several sessions at once (spb_batch_decode_step): returns
+    (logits [B][V] or None, argmax [B])."""
+    B = len(sessions)
+    hs = (C.c_void_p * B)(*[s.h for s in sessions])
+    tok = np.ascontiguousarray(np.asarray(tokens, np.int32))
+    V = sessions[0].V
+    lg = np.empty((B, V), np.float32) if logits else None
+    am = np.empty(B, np.int32)
+    check(load().spb_batch_decode_step(hs, B, tok.ctypes.data, lg.ctypes.data if logits else None,
+                                       am.ctypes.data))
+    return lg, am
 
 
 def load_l1(path: str = L1_SO):
