@@ -352,7 +352,7 @@ static cudaError_t gemv_nt(const DevQ4B &w, const DevQ4B &w2, const DevAct &act,
 // activation rows are stored in the GEMV's permuted column order (per 8 columns: even, then
 // odd); the fragment layout of m16n8k32 maps k positions 0-3 of a thread to one 4-byte group,
 // which is exactly one word of low or high nibbles of the code block.
-constexpr int GEMM_THREADS = 128;   // 4 warps x 8 weight rows
+constexpr int GEMM_THREADS = 128;   // per token group: 4 warps x 8 weight rows
 constexpr int GEMM_ROWS = 32;       // weight rows per CTA
 constexpr int GEMM_KC = 512;        // columns staged per step
 constexpr int GEMM_AP = GEMM_KC + 16;   // padded activation row (bank-conflict-free fragment loads)
@@ -388,26 +388,46 @@ struct GemmSmem {
   static constexpr int W = NM * GEMM_ROWS * GEMM_WP;          // code rows
   static constexpr int S = NM * GEMM_ROWS * (GEMM_KC / 32) * 2;   // block scales
   static constexpr int STAGE = A + W + S;
-  static constexpr int TOTAL = 2 * STAGE;                     // double buffered
+  static constexpr int KS = NM * (GEMM_KC / 32) * GEMM_ROWS * 4;   // decoded scales [m][block][row]
+  static constexpr int TOTAL = 2 * STAGE + KS;                // double buffered staging, one table
 };
 
-template <int MT, int EPI>
-__global__ void __launch_bounds__(GEMM_THREADS)
+// One block scale decoded for the GEMM's inner loop: SMALL, the integer k = value * 2^24
+// (|k| < 2^31); otherwise the signed mantissa in the low 16 bits and the exponent shift above.
+template <bool SMALL>
+__device__ __forceinline__ int32_t scale_word(uint32_t h) {
+  int32_t m, pw;
+  scale_parts(h, m, pw);
+  if (SMALL) return m * pw;
+  const uint32_t e = (h >> 10) & 31u;
+  return (int32_t)(((e ? e - 1 : 0) << 16) | ((uint32_t)m & 0xFFFFu));
+}
+
+// SMALL: every block scale of w (and w2) is below 128, so k = scale * 2^24 fits in int32 and
+// the 16x block sums accumulate as sum(16 isum * k) < 2^59 with one widening multiply-add per
+// value; the exact shift by 4 comes once at the end.
+// TH token groups of MT 16-token tiles: warp w takes weight rows 8 (w % 4) .. + 8 of the CTA's
+// 32 and token tiles MT (w / 4) .. + MT, so the CTA's 128 TH threads cover MT TH tiles.
+template <int MT, int TH, int EPI, bool SMALL>
+__global__ void __launch_bounds__(GEMM_THREADS * TH, 2)
 k_gemm(DevQ4B w, DevQ4B w2, DevAct act, int ntok, float *__restrict__ y, int ldy, uint32_t *err, uint32_t *ymax,
        unsigned long long *amax) {
   constexpr int NM = (EPI == EPI_STORE) ? 1 : 2;
-  constexpr int M = MT * 16;
-  using SM = GemmSmem<MT, NM>;
+  constexpr int M = MT * TH * 16;
+  constexpr int NTHR = GEMM_THREADS * TH;
+  using SM = GemmSmem<MT * TH, NM>;
   extern __shared__ __align__(16) uint8_t gsm[];
   __shared__ float tmax[M];
   __shared__ unsigned long long tkey[M];
   __shared__ double dsc[M];
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, tig = lane & 3;
+  const int tid = threadIdx.x, lane = tid & 31, g = lane >> 2, tig = lane & 3;
+  const int warp = (tid >> 5) & 3, mt0 = (tid >> 7) * MT;   // weight-row group, first token tile
   const int K = w.cols, rows = w.rows;
   const int nch = (K + GEMM_KC - 1) / GEMM_KC;
+  int32_t *KS = reinterpret_cast<int32_t *>(gsm + 2 * SM::STAGE);
   pdl_trigger();
   pdl_wait();
-  for (int t = tid; t < M; t += GEMM_THREADS) {
+  for (int t = tid; t < M; t += NTHR) {
     dsc[t] = t < ntok ? __dmul_rn(__ddiv_rn((double)act.scale[t], 127.0), 0x1p-24) : 0.0;
     tmax[t] = 0.0f;
     tkey[t] = 0ull;
@@ -418,24 +438,27 @@ k_gemm(DevQ4B w, DevQ4B w2, DevAct act, int ntok, float *__restrict__ y, int ldy
     int8_t *A = reinterpret_cast<int8_t *>(base);
     uint8_t *W = base + SM::A;
     uint8_t *S = W + SM::W;
+    // chunk widths are powers of two of at least 256 columns (K % 256 == 0), so every split
+    // below is a shift
     const int k0 = ci * GEMM_KC, kc = min(GEMM_KC, K - k0);
-    for (int i = tid; i < M * (kc >> 4); i += GEMM_THREADS) {
-      const int t = i / (kc >> 4), c = (i - t * (kc >> 4)) << 4;
+    const int l16 = 31 - __clz(kc >> 4);   // log2(kc / 16)
+    for (int i = tid; i < (M << l16); i += NTHR) {
+      const int t = i >> l16, c = (i & ((1 << l16) - 1)) << 4;
       const bool ok = t < ntok;
       cp_async16(A + t * GEMM_AP + c, act.q + (size_t)(ok ? t : 0) * K + k0 + c, ok);
     }
 #pragma unroll
     for (int m = 0; m < NM; m++) {
       const DevQ4B &q = m ? w2 : w;
-      for (int i = tid; i < GEMM_ROWS * (kc >> 5); i += GEMM_THREADS) {   // 16 code bytes per block
-        const int r = i / (kc >> 5), b = i - r * (kc >> 5);
+      for (int i = tid; i < (GEMM_ROWS << (l16 - 1)); i += NTHR) {   // 16 code bytes per block
+        const int r = i >> (l16 - 1), b = i & ((1 << (l16 - 1)) - 1);
         const bool ok = row0 + r < rows;
         cp_async16(W + (m * GEMM_ROWS + r) * GEMM_WP + b * 16,
                    q.codes + (size_t)(ok ? row0 + r : 0) * (K >> 1) + (size_t)((k0 >> 5) + b) * 16, ok);
       }
       const uint8_t *sc = reinterpret_cast<const uint8_t *>(q.scales);
-      for (int i = tid; i < GEMM_ROWS * (kc >> 8); i += GEMM_THREADS) {   // 8 block scales per 16 bytes
-        const int r = i / (kc >> 8), j = i - r * (kc >> 8);
+      for (int i = tid; i < (GEMM_ROWS << (l16 - 4)); i += NTHR) {   // 8 block scales per 16 bytes
+        const int r = i >> (l16 - 4), j = i & ((1 << (l16 - 4)) - 1);
         const bool ok = row0 + r < rows;
         cp_async16(S + ((m * GEMM_ROWS + r) * (GEMM_KC / 32)) * 2 + j * 16,
                    sc + (size_t)(ok ? row0 + r : 0) * (K >> 4) + (k0 >> 4) + j * 16, ok);
@@ -462,17 +485,26 @@ k_gemm(DevQ4B w, DevQ4B w2, DevAct act, int ntok, float *__restrict__ y, int ldy
       const uint8_t *base = gsm + (ci & 1) * SM::STAGE;
       const int8_t *A = reinterpret_cast<const int8_t *>(base);
       const uint8_t *W = base + SM::A;
-      const uint16_t *S = reinterpret_cast<const uint16_t *>(W + SM::W);
       const int kc = min(GEMM_KC, K - ci * GEMM_KC);
+      {   // decode the chunk's block scales once: KS[m][block][row]
+        const uint16_t *S = reinterpret_cast<const uint16_t *>(W + SM::W);
+        for (int i = tid; i < NM * GEMM_ROWS * (GEMM_KC / 32); i += NTHR) {
+          const int r = i & (GEMM_ROWS - 1), kb = (i / GEMM_ROWS) % (GEMM_KC / 32), m = i / (GEMM_ROWS * (GEMM_KC / 32));
+          KS[i] = scale_word<SMALL>(S[(m * GEMM_ROWS + r) * (GEMM_KC / 32) + kb]);
+        }
+        __syncthreads();
+      }
+#pragma unroll 4
       for (int kb = 0; kb < (kc >> 5); kb++) {
+        // A fragments: one ldmatrix.x4 per 16-token tile; lane l addresses row l % 8 of
+        // matrix l / 8 (rows +8 for matrices 1 and 3, columns +16 for matrices 2 and 3)
         uint32_t af[MT][4];
 #pragma unroll
         for (int mt = 0; mt < MT; mt++) {
-          const int8_t *ab = A + (mt * 16 + g) * GEMM_AP + kb * 32 + tig * 4;
-          af[mt][0] = *reinterpret_cast<const uint32_t *>(ab);
-          af[mt][1] = *reinterpret_cast<const uint32_t *>(ab + 8 * GEMM_AP);
-          af[mt][2] = *reinterpret_cast<const uint32_t *>(ab + 16);
-          af[mt][3] = *reinterpret_cast<const uint32_t *>(ab + 8 * GEMM_AP + 16);
+          const int8_t *ab = A + ((mt0 + mt) * 16 + (lane & 7) + ((lane >> 3) & 1) * 8) * GEMM_AP + kb * 32 + (lane >> 4) * 16;
+          asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                       : "=r"(af[mt][0]), "=r"(af[mt][1]), "=r"(af[mt][2]), "=r"(af[mt][3])
+                       : "r"((uint32_t)__cvta_generic_to_shared(ab)));
         }
 #pragma unroll
         for (int m = 0; m < NM; m++) {
@@ -480,29 +512,49 @@ k_gemm(DevQ4B w, DevQ4B w2, DevAct act, int ntok, float *__restrict__ y, int ldy
           const uint32_t w0 = wr[tig >> 1], w1 = wr[2 + (tig >> 1)];
           const uint32_t b0 = (tig & 1) ? (w0 & 0xF0F0F0F0u) : ((w0 << 4) & 0xF0F0F0F0u);
           const uint32_t b1 = (tig & 1) ? (w1 & 0xF0F0F0F0u) : ((w1 << 4) & 0xF0F0F0F0u);
-          const uint16_t *sr = S + (m * GEMM_ROWS + warp * 8 + tig * 2) * (GEMM_KC / 32) + kb;
-          int32_t m0, p0, m1, p1;
-          scale_parts(sr[0], m0, p0);
-          scale_parts(sr[GEMM_KC / 32], m1, p1);
+          const int2 kw = *reinterpret_cast<const int2 *>(KS + (m * (GEMM_KC / 32) + kb) * GEMM_ROWS + warp * 8 + tig * 2);
+          if (SMALL) {
+            const int32_t k0 = kw.x, k1 = kw.y;   // |k| < 2^31
 #pragma unroll
-          for (int mt = 0; mt < MT; mt++) {
-            int32_t c[4];
-            mma_s8(af[mt], b0, b1, c);
-            acc[m][mt][0] += (int64_t)((c[0] >> 4) * m0) * (int64_t)p0;   // token g,   row 2 tig
-            acc[m][mt][1] += (int64_t)((c[1] >> 4) * m1) * (int64_t)p1;   // token g,   row 2 tig + 1
-            acc[m][mt][2] += (int64_t)((c[2] >> 4) * m0) * (int64_t)p0;   // token g+8, row 2 tig
-            acc[m][mt][3] += (int64_t)((c[3] >> 4) * m1) * (int64_t)p1;   // token g+8, row 2 tig + 1
+            for (int mt = 0; mt < MT; mt++) {
+              int32_t c[4];
+              mma_s8(af[mt], b0, b1, c);
+              acc[m][mt][0] += (int64_t)c[0] * (int64_t)k0;   // 16 x (token g,   row 2 tig)
+              acc[m][mt][1] += (int64_t)c[1] * (int64_t)k1;   // 16 x (token g,   row 2 tig + 1)
+              acc[m][mt][2] += (int64_t)c[2] * (int64_t)k0;   // 16 x (token g+8, row 2 tig)
+              acc[m][mt][3] += (int64_t)c[3] * (int64_t)k1;   // 16 x (token g+8, row 2 tig + 1)
+            }
+          } else {
+            const int32_t m0 = (int16_t)kw.x, p0 = 1 << (kw.x >> 16);
+            const int32_t m1 = (int16_t)kw.y, p1 = 1 << (kw.y >> 16);
+#pragma unroll
+            for (int mt = 0; mt < MT; mt++) {
+              int32_t c[4];
+              mma_s8(af[mt], b0, b1, c);
+              acc[m][mt][0] += (int64_t)((c[0] >> 4) * m0) * (int64_t)p0;   // token g,   row 2 tig
+              acc[m][mt][1] += (int64_t)((c[1] >> 4) * m1) * (int64_t)p1;   // token g,   row 2 tig + 1
+              acc[m][mt][2] += (int64_t)((c[2] >> 4) * m0) * (int64_t)p0;   // token g+8, row 2 tig
+              acc[m][mt][3] += (int64_t)((c[3] >> 4) * m1) * (int64_t)p1;   // token g+8, row 2 tig + 1
+            }
           }
         }
       }
       __syncthreads();   // buffer ci & 1 may be refilled by the next stage
+    }
+    if (SMALL) {   // the sums were accumulated 16x: every term is a multiple of 16
+#pragma unroll
+      for (int m = 0; m < NM; m++)
+#pragma unroll
+        for (int mt = 0; mt < MT; mt++)
+#pragma unroll
+          for (int i = 0; i < 4; i++) acc[m][mt][i] >>= 4;
     }
     // epilogue: (token, row) of each accumulator
 #pragma unroll
     for (int mt = 0; mt < MT; mt++) {
 #pragma unroll
       for (int i = 0; i < 4; i++) {
-        const int t = mt * 16 + g + (i >= 2 ? 8 : 0);
+        const int t = (mt0 + mt) * 16 + g + (i >= 2 ? 8 : 0);
         const int row = row0 + warp * 8 + tig * 2 + (i & 1);
         if (t >= ntok || row >= rows) continue;
         float v = __double2float_rn(__dmul_rn(__ll2double_rn(acc[0][mt][i]), dsc[t]));
@@ -518,7 +570,7 @@ k_gemm(DevQ4B w, DevQ4B w2, DevAct act, int ntok, float *__restrict__ y, int ldy
     }
   }
   __syncthreads();
-  for (int t = tid; t < ntok; t += GEMM_THREADS) {
+  for (int t = tid; t < ntok; t += NTHR) {
     if (ymax) {
       const float m = tmax[t];
       if (!(m <= 3.402823466e38f)) raise_err(err, ERR_ACT_RANGE);
@@ -528,12 +580,12 @@ k_gemm(DevQ4B w, DevQ4B w2, DevAct act, int ntok, float *__restrict__ y, int ldy
   }
 }
 
-template <int MT, int EPI>
+template <int MT, int TH, int EPI, bool SMALL>
 static cudaError_t gemm_launch(const DevQ4B &w, const DevQ4B &w2, const DevAct &act, int ntok, float *y, int ldy,
                                uint32_t *err, uint32_t *ymax, unsigned long long *amax, cudaStream_t st) {
   constexpr int NM = (EPI == EPI_STORE) ? 1 : 2;
-  const size_t smem = GemmSmem<MT, NM>::TOTAL;
-  auto kern = k_gemm<MT, EPI>;
+  const size_t smem = GemmSmem<MT * TH, NM>::TOTAL;
+  auto kern = k_gemm<MT, TH, EPI, SMALL>;
   static bool configured = false;
   if (!configured) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -543,21 +595,40 @@ static cudaError_t gemm_launch(const DevQ4B &w, const DevQ4B &w2, const DevAct &
   int dev = 0, nsm = 148, occ = 1;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
-  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, GEMM_THREADS, smem);
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, GEMM_THREADS * TH, smem);
   const int nrb = (w.rows + GEMM_ROWS - 1) / GEMM_ROWS;
   const int grid = std::min(nrb, nsm * std::max(occ, 1));
-  return launch_k(kern, dim3(grid), dim3(GEMM_THREADS), smem, st, 1, w, w2, act, ntok, y, ldy, err, ymax, amax);
+  return launch_k(kern, dim3(grid), dim3(GEMM_THREADS * TH), smem, st, 1, w, w2, act, ntok, y, ldy, err, ymax,
+                  amax);
+}
+
+// 16-token tiles per warp for full 64-token pieces: 2 (two token groups, 8 warps; the default)
+// or 4 (one group of 4 warps, SPB_GEMM_SPLIT=0)
+static bool gemm_split() {
+  static int on = -1;
+  if (on < 0) {
+    const char *e = getenv("SPB_GEMM_SPLIT");
+    on = (e && e[0] == '0') ? 0 : 1;
+  }
+  return on != 0;
 }
 
 template <int EPI>
 static cudaError_t gemm_mt(const DevQ4B &w, const DevQ4B &w2, const DevAct &act, int ntok, float *y, int ldy,
                            uint32_t *err, uint32_t *ymax, unsigned long long *amax, cudaStream_t st) {
-  switch ((ntok + 15) / 16) {
-    case 1: return gemm_launch<1, EPI>(w, w2, act, ntok, y, ldy, err, ymax, amax, st);
-    case 2: return gemm_launch<2, EPI>(w, w2, act, ntok, y, ldy, err, ymax, amax, st);
-    case 3: return gemm_launch<3, EPI>(w, w2, act, ntok, y, ldy, err, ymax, amax, st);
-    default: return gemm_launch<4, EPI>(w, w2, act, ntok, y, ldy, err, ymax, amax, st);
+  const bool small = w.small && (EPI == EPI_STORE || w2.small);
+#define SPB_GEMM_MT(MTV, THV)                                                                        \
+  return small ? gemm_launch<MTV, THV, EPI, true>(w, w2, act, ntok, y, ldy, err, ymax, amax, st) \
+               : gemm_launch<MTV, THV, EPI, false>(w, w2, act, ntok, y, ldy, err, ymax, amax, st)
+  switch ((ntok + 15) / 16) {   // 16-token tiles: split across two warp groups when even
+    case 1: SPB_GEMM_MT(1, 1);
+    case 2: SPB_GEMM_MT(1, 2);
+    case 3: SPB_GEMM_MT(3, 1);
+    default:
+      if (gemm_split()) SPB_GEMM_MT(2, 2);
+      SPB_GEMM_MT(4, 1);
   }
+#undef SPB_GEMM_MT
 }
 
 // SPB_GEMM=0 keeps token batches on the dp4a k_gemv (comparisons; results are identical)
@@ -971,6 +1042,7 @@ cudaError_t launch_rope_kv(const RopeArgs &a, cudaStream_t st) {
 // ------------------------------------------------------------------------------ attention
 constexpr int ATTN_THREADS = 256;
 constexpr int ATTN_STAGES = 3;
+constexpr int ATTN_SPAN = 1024;   // positions one CTA takes before the row is split further
 
 // positions per ring stage (32 KB of int32 K or V per stage)
 template <int HD>
@@ -978,13 +1050,15 @@ struct AttnSub {
   static constexpr int SUB = 8192 / HD;
 };
 
-template <int HD, int G, int CL>
-__global__ void __launch_bounds__(ATTN_THREADS) k_attn(AttnArgs a, int cmax) {
+// CL CTAs (a cluster when CL > 1) split the positions of one (token row, KV head): CL = 16 for
+// one long context, 1 when the rows and heads alone fill the GPU.
+template <int HD, int G>
+__global__ void __launch_bounds__(ATTN_THREADS) k_attn(AttnArgs a, int cmax, int CL) {
   cg::cluster_group cluster = cg::this_cluster();
   constexpr int SUB = AttnSub<HD>::SUB;
   constexpr int EPL = HD / 32;                 // q/k elements per lane in the score dot
   constexpr int GROUPS = ATTN_THREADS / HD;    // position groups in the V-sum
-  constexpr int DPR = HD / CL;                 // head dims each rank finalizes
+  const int DPR = HD / CL;                     // head dims each rank finalizes
   extern __shared__ __align__(128) uint8_t asm_raw[];
   int32_t *ring = reinterpret_cast<int32_t *>(asm_raw);            // [STAGES][SUB*HD]
   int32_t *qs = ring + ATTN_STAGES * SUB * HD;                       // [G][HD]
@@ -996,7 +1070,7 @@ __global__ void __launch_bounds__(ATTN_THREADS) k_attn(AttnArgs a, int cmax) {
   __shared__ int32_t mx_all[G];
   __shared__ float fred[33];
 
-  const int rank = (int)cluster.block_rank();
+  const int rank = CL > 1 ? (int)cluster.block_rank() : 0;
   const int g = blockIdx.y, t = blockIdx.z;
   const int QD = a.NH * HD;
   int p, P;
@@ -1090,10 +1164,11 @@ __global__ void __launch_bounds__(ATTN_THREADS) k_attn(AttnArgs a, int cmax) {
       issue(i + ATTN_STAGES);
     }
   }
-  cluster.sync();
+  if (CL > 1) cluster.sync();
   if (threadIdx.x < G) {
-    int32_t m = INT32_MIN;
-    for (int r = 0; r < CL; r++) m = max(m, *cluster.map_shared_rank(&mx_loc[threadIdx.x], r));
+    int32_t m = mx_loc[threadIdx.x];
+    for (int r = 0; r < CL; r++)
+      if (r != rank) m = max(m, *cluster.map_shared_rank(&mx_loc[threadIdx.x], r));
     mx_all[threadIdx.x] = m;
   }
   __syncthreads();
@@ -1144,14 +1219,16 @@ __global__ void __launch_bounds__(ATTN_THREADS) k_attn(AttnArgs a, int cmax) {
       nacc[i] = s;
     }
   }
-  cluster.sync();
+  if (CL > 1) cluster.sync();
+  else __syncthreads();
   // ---- phase 4: combine the cluster's partials; rank r finalizes HD/CL dims per head
   float omax = 0.0f;
   for (int i = threadIdx.x; i < G * DPR; i += ATTN_THREADS) {
     const int h = i / DPR, dd = rank * DPR + (i % DPR);
-    acc128 N{0ull, 0ll};
-    int64_t S = 0;
+    acc128 N = nacc[h * HD + dd];
+    int64_t S = s_loc[h];
     for (int r = 0; r < CL; r++) {
+      if (r == rank) continue;
       acc128_add(N, *cluster.map_shared_rank(&nacc[h * HD + dd], r));
       S += *cluster.map_shared_rank(&s_loc[h], r);
     }
@@ -1166,24 +1243,9 @@ __global__ void __launch_bounds__(ATTN_THREADS) k_attn(AttnArgs a, int cmax) {
     omax = block_max(omax, fred);
     if (threadIdx.x == 0) atomicMax(a.ao_max + t, __float_as_uint(omax));
   }
-  cluster.sync();
+  if (CL > 1) cluster.sync();   // peers' shared memory stays live until every rank has read it
 }
 
-template <int HD, int G, int CL>
-static cudaError_t attn_launch(const AttnArgs &a, int cmax, size_t smem, cudaStream_t st) {
-  auto kern = k_attn<HD, G, CL>;
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    if (e != cudaSuccess) return e;
-    if (CL > 8) {
-      e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-      if (e != cudaSuccess) return e;
-    }
-    configured = true;
-  }
-  return launch_k(kern, dim3(CL, a.NKV, a.ntok), dim3(ATTN_THREADS), smem, st, CL, a, cmax);
-}
 
 template <int HD, int G>
 static size_t attn_smem(int cmax) {
@@ -1194,14 +1256,22 @@ static size_t attn_smem(int cmax) {
 
 template <int HD, int G>
 static cudaError_t attn_cl(const AttnArgs &a, cudaStream_t st) {
-  // 16-CTA clusters where the device can co-schedule them (asked once, before any launch,
-  // so a graph capture never sees a failed launch), else the portable 8
-  static int cl = 0;
-  if (cl == 0) {
-    cl = 8;
-    auto k16 = k_attn<HD, G, 16>;
-    if (cudaFuncSetAttribute(k16, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess &&
-        cudaFuncSetAttribute(k16, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) == cudaSuccess) {
+  // Largest cluster: 16 CTAs where the device can co-schedule them (asked once, before any
+  // launch, so a graph capture never sees a failed launch), else the portable 8.
+  static int clmax = 0, nsm = 148;
+  auto kern = k_attn<HD, G>;
+  if (clmax == 0) {
+    clmax = 8;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    if (e != cudaSuccess) {
+      clmax = 0;
+      return e;
+    }
+    auto k16 = kern;
+    if (cudaFuncSetAttribute(k16, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess) {
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3(16, 1, 1);
       cfg.blockDim = dim3(ATTN_THREADS);
@@ -1214,14 +1284,20 @@ static cudaError_t attn_cl(const AttnArgs &a, cudaStream_t st) {
       cfg.attrs = attr;
       cfg.numAttrs = 1;
       int nclusters = 0;
-      if (cudaOccupancyMaxActiveClusters(&nclusters, k16, &cfg) == cudaSuccess && nclusters >= 4) cl = 16;
+      if (cudaOccupancyMaxActiveClusters(&nclusters, k16, &cfg) == cudaSuccess && nclusters >= 4) clmax = 16;
     }
     (void)cudaGetLastError();
   }
+  // Split a row's positions over more CTAs only while (rows x KV heads) CTAs leave SMs idle or
+  // a CTA would cover more than ATTN_SPAN positions; the score buffer bounds it from below.
+  const int span = a.win >= 0 ? std::min(a.P, a.win) : a.P;
+  int cl = 1;
+  while (cl < clmax && ((long)a.ntok * a.NKV * cl < 2L * nsm || span > cl * ATTN_SPAN)) cl *= 2;
+  while (cl < clmax && attn_smem<HD, G>((a.P + cl - 1) / cl) > 200 * 1024) cl *= 2;
   const int cmax = (a.P + cl - 1) / cl;
   const size_t smem = attn_smem<HD, G>(cmax);
   if (smem > 200 * 1024) return cudaErrorInvalidValue;
-  return cl == 16 ? attn_launch<HD, G, 16>(a, cmax, smem, st) : attn_launch<HD, G, 8>(a, cmax, smem, st);
+  return launch_k(kern, dim3(cl, a.NKV, a.ntok), dim3(ATTN_THREADS), smem, st, cl, a, cmax, cl);
 }
 
 cudaError_t launch_attn(const AttnArgs &a, cudaStream_t st) {
@@ -1265,6 +1341,19 @@ cudaError_t launch_embed(const DevQ4B &emb, const int32_t *tok_dev, int ntok, fl
 }
 
 // decode the keys left by the LM-head GEMV into token ids and clear them for the next step
+__global__ void k_scale_emax(const uint16_t *s, size_t n, int *out) {
+  int e = 0;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+    e = max(e, (int)((s[i] >> 10) & 31u));
+  e = warp_max_i32(e);
+  if ((threadIdx.x & 31) == 0) atomicMax(out, e);
+}
+
+cudaError_t launch_scale_emax(const uint16_t *scales, size_t n, int *out, cudaStream_t st) {
+  k_scale_emax<<<296, 256, 0, st>>>(scales, n, out);
+  return cudaGetLastError();
+}
+
 __global__ void k_argmax_take(unsigned long long *keys, int ntok, int32_t *out) {
   pdl_trigger();
   pdl_wait();

@@ -23,7 +23,12 @@ struct DevQ4B {
   const uint8_t *codes;
   const uint16_t *scales;
   int rows, cols;
+  int small;   // 1 when every block scale is below 128 in magnitude (f16 exponent field <= 21),
+               // so each scale as the integer k = value * 2^24 fits in int32 (set after upload)
 };
+
+// largest f16 exponent field among n block scales (device reduction, for DevQ4B::small)
+cudaError_t launch_scale_emax(const uint16_t *scales, size_t n, int *out, cudaStream_t st);
 
 // A quantized activation set: NTOK rows of K int8 codes in the GEMV's interleaved
 // order (per 8-column group: even columns then odd columns), the per-32-block code

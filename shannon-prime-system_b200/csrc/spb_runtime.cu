@@ -179,6 +179,8 @@ struct spb_model {
   DecLayer *dec_layers = nullptr;   // device [NL]: the persistent decode kernel's view of the layers
 };
 
+static int mark_small_scales(spb_model *m);
+
 static size_t q4b_bytes(int rows, int cols) { return (size_t)rows * (cols / 2) + (size_t)rows * (cols / 32) * 2; }
 
 static int check_cfg(const spb_config &c) {
@@ -358,8 +360,32 @@ extern "C" int spb_model_upload(const spb_model_desc *desc, int device, spb_mode
   PUT(put_q4b(desc->token_embd, m->V, m->E, m->embd, 0, "token_embd"));
   if (!m->gemma) PUT(put_q4b(desc->output, m->V, m->E, m->out, 0, "output"));
   PUT(put_f32(desc->output_norm, m->out_norm, m->E, "output_norm"));
+  PUT(mark_small_scales(m));
 #undef PUT
   *out = m;
+  return SPB_OK;
+}
+
+// Mark the matrices whose block scales are all below 128 (DevQ4B::small): the token-batch
+// GEMM then accumulates each block with one widening multiply-add.
+static int mark_small_scales(spb_model *m) {
+  std::vector<DevQ4B *> ws;
+  for (DevLayer &d : m->layers) {
+    ws.push_back(&d.qkv); ws.push_back(&d.o); ws.push_back(&d.g); ws.push_back(&d.u); ws.push_back(&d.d);
+  }
+  ws.push_back(&m->embd);
+  if (!m->gemma) ws.push_back(&m->out);
+  int *dev = nullptr;
+  CU(cudaMalloc(&dev, ws.size() * sizeof(int)));
+  cudaError_t e = cudaMemset(dev, 0, ws.size() * sizeof(int));
+  for (size_t i = 0; i < ws.size() && e == cudaSuccess; i++)
+    e = launch_scale_emax(ws[i]->scales, (size_t)ws[i]->rows * (ws[i]->cols / 32), dev + i, 0);
+  std::vector<int> emax(ws.size(), 31);
+  if (e == cudaSuccess) e = cudaMemcpy(emax.data(), dev, ws.size() * sizeof(int), cudaMemcpyDeviceToHost);
+  cudaFree(dev);
+  if (e != cudaSuccess) return set_err(SPB_ECUDA, "spb_model: scale check: %s", cudaGetErrorString(e));
+  for (size_t i = 0; i < ws.size(); i++) ws[i]->small = emax[i] <= 21 ? 1 : 0;
+  if (m->gemma) m->out = m->embd;
   return SPB_OK;
 }
 
@@ -415,6 +441,7 @@ extern "C" int spb_model_synthetic(const spb_config *cfg, uint64_t seed, int dev
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
     if (e != cudaSuccess) rc = set_err(SPB_ECUDA, "synth: %s", cudaGetErrorString(e));
   }
+  if (!rc) rc = mark_small_scales(m);
   if (rc) { spb_model_free(m); return rc; }
   *out = m;
   return SPB_OK;
