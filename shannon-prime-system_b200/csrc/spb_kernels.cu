@@ -1053,10 +1053,11 @@ struct AttnSub {
 // CL CTAs (a cluster when CL > 1) split the positions of one (token row, KV head): CL = 16 for
 // one long context, 1 when the rows and heads alone fill the GPU.
 template <int HD, int G>
-__global__ void __launch_bounds__(ATTN_THREADS) k_attn(AttnArgs a, int cmax, int CL) {
+__global__ void __launch_bounds__(ATTN_THREADS, 2) k_attn(AttnArgs a, int cmax, int CL) {
   cg::cluster_group cluster = cg::this_cluster();
   constexpr int SUB = AttnSub<HD>::SUB;
-  constexpr int EPL = HD / 32;                 // q/k elements per lane in the score dot
+  constexpr int V4 = HD / 32;                  // int4 columns per lane in the score dot
+  constexpr bool QREG = G * V4 <= 16;          // q slices held in registers (<= 64 words)
   constexpr int GROUPS = ATTN_THREADS / HD;    // position groups in the V-sum
   const int DPR = HD / CL;                     // head dims each rank finalizes
   extern __shared__ __align__(128) uint8_t asm_raw[];
@@ -1127,35 +1128,54 @@ __global__ void __launch_bounds__(ATTN_THREADS) k_attn(AttnArgs a, int cmax, int
   if (threadIdx.x == 0 && !early)
     for (int i = 0; i < min(ATTN_STAGES, total); i++) issue(i);
 
-  // ---- phase 1: exact scores of this CTA's positions -> the 2^14 grid
+  // ---- phase 1: exact scores of this CTA's positions -> the 2^14 grid. Eight lanes share a
+  // position (lane j takes the int4 columns 4j + 32v), so a warp scores four positions per pass
+  // with a three-level butterfly, and lane h of each group finishes head h. |q|, |k| < 2^24
+  // keep every partial sum below 2^56.
+  const int gq = lane >> 3, gj = lane & 7;
+  int4 qr[QREG ? G * V4 : 1];
+  if (QREG) {
+#pragma unroll
+    for (int h = 0; h < G; h++)
+#pragma unroll
+      for (int v = 0; v < V4; v++) qr[h * V4 + v] = *reinterpret_cast<const int4 *>(qs + h * HD + 32 * v + 4 * gj);
+  }
+  int32_t lmax = INT32_MIN;   // lanes gj < G: running maximum of head gj
   for (int i = 0; i < nsub; i++) {
     const int stage = i % ATTN_STAGES;
     mbar_wait(&full[stage], (uint32_t)(i / ATTN_STAGES) & 1u, a.err);
     const int32_t *buf = ring + stage * SUB * HD;
     const int len = min(SUB, cn - i * SUB);
-    for (int pp = warp; pp < len; pp += ATTN_THREADS / 32) {
-      const int32_t *kr = buf + pp * HD + lane * EPL;
-      int32_t kv[EPL];
+    for (int p4 = warp * 4; p4 < len; p4 += ATTN_THREADS / 8) {   // warp-uniform bound
+      const int pp = p4 + gq;
+      const bool ok = pp < len;
+      const int32_t *kr = buf + (ok ? pp : p4) * HD + 4 * gj;
+      int4 kv[V4];
 #pragma unroll
-      for (int e = 0; e < EPL; e += 2) {
-        const int2 u = *reinterpret_cast<const int2 *>(kr + e);
-        kv[e] = u.x;
-        kv[e + 1] = u.y;
-      }
+      for (int v = 0; v < V4; v++) kv[v] = *reinterpret_cast<const int4 *>(kr + 32 * v);
+      int64_t sv = 0;
 #pragma unroll
       for (int h = 0; h < G; h++) {
-        const int32_t *qh = qs + h * HD + lane * EPL;
-        int64_t s = 0;
+        int64_t acc = 0;
 #pragma unroll
-        for (int e = 0; e < EPL; e++) s += (int64_t)qh[e] * (int64_t)kv[e];
-        s = warp_sum_i64(s);
-        if (lane == 0) {
-          float z = __fmul_rn(__double2float_rn(__dmul_rn(__ll2double_rn(s), 0x1p-32)), a.ascale);
-          if (!(fabsf(z) < 131072.0f)) { raise_err(a.err, ERR_SCORE_RANGE); z = 0.0f; }
-          const int32_t zi = (int32_t)llround_d((double)z * 16384.0);
-          sc[h * cmax + i * SUB + pp] = zi;
-          atomicMax(&mx_loc[h], zi);
+        for (int v = 0; v < V4; v++) {
+          const int4 q = QREG ? qr[h * V4 + v] : *reinterpret_cast<const int4 *>(qs + h * HD + 32 * v + 4 * gj);
+          acc += (int64_t)q.x * kv[v].x;
+          acc += (int64_t)q.y * kv[v].y;
+          acc += (int64_t)q.z * kv[v].z;
+          acc += (int64_t)q.w * kv[v].w;
         }
+        acc += __shfl_xor_sync(0xffffffffu, acc, 4);
+        acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+        acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+        if (gj == h) sv = acc;
+      }
+      if (ok && gj < G) {
+        float z = __fmul_rn(__double2float_rn(__dmul_rn(__ll2double_rn(sv), 0x1p-32)), a.ascale);
+        if (!(fabsf(z) < 131072.0f)) { raise_err(a.err, ERR_SCORE_RANGE); z = 0.0f; }
+        const int32_t zi = (int32_t)llround_d((double)z * 16384.0);
+        sc[gj * cmax + i * SUB + pp] = zi;
+        lmax = max(lmax, zi);
       }
     }
     __syncthreads();
@@ -1164,7 +1184,11 @@ __global__ void __launch_bounds__(ATTN_THREADS) k_attn(AttnArgs a, int cmax, int
       issue(i + ATTN_STAGES);
     }
   }
+  lmax = max(lmax, __shfl_xor_sync(0xffffffffu, lmax, 8));
+  lmax = max(lmax, __shfl_xor_sync(0xffffffffu, lmax, 16));
+  if (lane < G && lmax != INT32_MIN) atomicMax(&mx_loc[lane], lmax);
   if (CL > 1) cluster.sync();
+  else __syncthreads();
   if (threadIdx.x < G) {
     int32_t m = mx_loc[threadIdx.x];
     for (int r = 0; r < CL; r++)
@@ -1197,11 +1221,22 @@ __global__ void __launch_bounds__(ATTN_THREADS) k_attn(AttnArgs a, int cmax, int
     const int32_t *buf = ring + stage * SUB * HD;
     const int j0 = (i - nsub) * SUB;
     const int len = min(SUB, cn - j0);
-#pragma unroll 4
-    for (int pp = grp; pp < len; pp += GROUPS) {
-      const int64_t v = buf[pp * HD + d];
+    // eight positions per fold into 128 bits: e <= 2^30 and |v| < 2^30, so 8 |e v| < 2^63
+    // (positions pp < SUB always stay inside the stage; those past len weigh 0)
+    for (int p8 = grp; p8 < len; p8 += 8 * GROUPS) {
+      int64_t part[G];
 #pragma unroll
-      for (int h = 0; h < G; h++) acc128_add(acc[h], (int64_t)sc[h * cmax + j0 + pp] * v);
+      for (int h = 0; h < G; h++) part[h] = 0;
+#pragma unroll
+      for (int u = 0; u < 8; u++) {
+        const int pp = p8 + u * GROUPS;
+        const bool ok = pp < len;
+        const int64_t v = buf[pp * HD + d];
+#pragma unroll
+        for (int h = 0; h < G; h++) part[h] += (int64_t)(ok ? sc[h * cmax + j0 + pp] : 0) * v;
+      }
+#pragma unroll
+      for (int h = 0; h < G; h++) acc128_add(acc[h], part[h]);
     }
     __syncthreads();
     if (threadIdx.x == 0 && i + ATTN_STAGES < total) {

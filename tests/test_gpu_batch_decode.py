@@ -4,6 +4,8 @@ B sessions with ragged contexts step together: every row's logits, argmax and ne
 must be the bytes the same session produces with its own spb_session_decode_step (which the
 other GPU tests tie to XREF). Row counts cover the dp4a GEMV (1, 2, 8), the tensor-core GEMM
 with a partial 16-row tile (3, 20) and full tiles (16, 64)."""
+import dataclasses
+
 import numpy as np
 import pytest
 
@@ -30,9 +32,13 @@ def sessions_with_history(m, cfg, B, seed, pmax):
 
 
 @pytest.mark.parametrize("name,B", [("micro_gemma", 3), ("micro_gemma", 20), ("micro_qwen", 16),
-                                    ("micro_qwen", 1), ("tiny", 8), ("tiny", 2), ("micro_gemma", 64)])
+                                    ("micro_qwen", 1), ("tiny", 8), ("tiny", 2), ("micro_gemma", 64),
+                                    ("kv8", 64)])
 def test_batch_matches_single_sessions(cuda_ok, name, B):
-    cfg = spmodel.CONFIGS[name]
+    if name == "kv8":   # 64 rows x 8 KV heads: one attention CTA per (row, KV head)
+        cfg = dataclasses.replace(spmodel.CONFIGS["micro_qwen"], name="kv8", n_head=8, n_head_kv=8)
+    else:
+        cfg = spmodel.CONFIGS[name]
     m = spb200.Model.synthetic(cfg, seed=7)
     pmax = 96
     batch = sessions_with_history(m, cfg, B, 40 + B, pmax)

@@ -137,3 +137,26 @@ def test_sliding_window_long_context(xr, cuda_ok):
     want = xr.session(xref.build_desc(cfg, T), 128).prefill(toks)
     m.free()
     assert np.array_equal(u32(got), u32(want))
+
+
+@pytest.mark.parametrize("hd,nh,nkv", [(256, 8, 2), (128, 8, 8), (128, 16, 2), (256, 4, 2)])
+def test_attention_head_shapes(xr, cuda_ok, hd, nh, nkv):
+    """Head widths 128 / 256 and GQA groups 1-8: q held in registers (G * hd <= 512) or read
+    from shared memory, one CTA per (row, KV head) when rows x KV heads fill the GPU (the
+    64-row chunk with 8 KV heads) and clusters otherwise; a 70-token prefill spans several
+    K/V stages."""
+    cfg = dataclasses.replace(spmodel.CONFIGS["micro_gemma"], n_layers=2, head_dim=hd, n_head=nh,
+                              n_head_kv=nkv)
+    T = spmodel.gen_model(cfg, seed=11)
+    m = spb200.Model.upload(cfg, T)
+    toks = spmodel.gen_tokens(31, 70, cfg.n_vocab)
+    s = m.session(cfg.max_context)
+    got = s.prefill(toks)
+    want_s = xr.session(xref.build_desc(cfg, T), cfg.max_context)
+    want = want_s.prefill(toks)
+    assert np.array_equal(u32(got), u32(want))
+    for t in spmodel.gen_tokens(32, 3, cfg.n_vocab):
+        assert np.array_equal(u32(s.step(int(t))), u32(want_s.step(int(t))))
+    s.close()
+    want_s.close()
+    m.free()
