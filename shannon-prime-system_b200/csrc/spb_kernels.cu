@@ -837,90 +837,167 @@ __device__ void block_rmsnorm(const float *src, const float *w, int n, float *ds
   __syncthreads();
 }
 
-// ---- norm block as one 8-CTA cluster per token row: each CTA owns E/8 columns, the
-// exact sums of squares and the quantizer's max are exchanged through DSMEM.
-constexpr int NORM_CL = 8;
-constexpr int NORM_CL_THREADS = 256;
+// ---- norm block as one NORM_CL-CTA cluster of 1024 threads per token row: rank r owns
+// columns [r E/NCL, (r+1) E/NCL), one or two per thread. Each reduction (sums of squares, the
+// quantizer's max) is finished by warp 0 and pushed into every rank's shared memory, so one
+// cluster barrier per reduction and no remote loads.
+constexpr int NORM_CL = 4;
+constexpr int NORM_CL_THREADS = 1024;
+constexpr int NORM_REG_THREADS = 1024;   // the one-CTA form below
 
+// per-thread sum of q16(v)^2 over the thread's columns j * 1024 + tid < E (1024-thread blocks)
+template <int EPT>
+__device__ __forceinline__ acc128 sq_partial(const float (&v)[EPT], int E, uint32_t *err) {
+  acc128 ss{0ull, 0ll};
+  bool bad = false;
+#pragma unroll
+  for (int j = 0; j < EPT; j++) {
+    if (j * 1024 + (int)threadIdx.x >= E) continue;
+    if (!(fabsf(v[j]) < 32768.0f)) { bad = true; continue; }
+    const int64_t xi = q16_round(v[j]);
+    acc128_add(ss, xi * xi);
+  }
+  if (bad) raise_err(err, ERR_NORM_RANGE);
+  return ss;
+}
+
+__device__ __forceinline__ void cluster_wait_started() {
+  asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
+}
+
+// this CTA's 128-bit partial (warp 0, lane 0 holds it on return; the others hold garbage)
+__device__ __forceinline__ acc128 block_partial128(acc128 v, acc128 *red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    acc128 r;
+    r.lo = __shfl_xor_sync(0xffffffffu, v.lo, o);
+    r.hi = __shfl_xor_sync(0xffffffffu, v.hi, o);
+    acc128_add(v, r);
+  }
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  acc128 s{0ull, 0ll};
+  if (warp == 0) {
+    s = lane < nw ? red[lane] : acc128{0ull, 0ll};
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      acc128 r;
+      r.lo = __shfl_xor_sync(0xffffffffu, s.lo, o);
+      r.hi = __shfl_xor_sync(0xffffffffu, s.hi, o);
+      acc128_add(s, r);
+    }
+  }
+  return s;
+}
+
+template <int EPT>
 __global__ void __launch_bounds__(NORM_CL_THREADS)
 k_norm_cl(float *x, const float *add, const float *add_w, const float *out_w, int E, DevAct act, float *nx_out,
           uint32_t *err, uint32_t *zero_slot) {
   cg::cluster_group cluster = cg::this_cluster();
-  extern __shared__ __align__(16) float csm[];
-  const int ns = E / NORM_CL;
-  float *xb = csm;        // [ns] residual slice after the add
-  float *nb = csm + ns;   // [ns] normed slice
-  __shared__ acc128 red[33];
-  __shared__ acc128 part[2];
+  __shared__ acc128 red[32];
+  __shared__ acc128 sq_in[2][NORM_CL];   // [reduction][source rank]
+  __shared__ float mx_in[NORM_CL];
   __shared__ float fred[33];
-  __shared__ float mx_loc;
-  __shared__ float s_all;
-  __shared__ uint64_t inv_sh;
+  __shared__ uint64_t inv_sh[2];
   const int rank = (int)cluster.block_rank();
-  const int t = blockIdx.y;
-  const int off = rank * ns;
+  const int t = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int ns = E / NORM_CL, off = rank * ns;
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");   // waited on before the first push
+  float aw[EPT], ow[EPT];
+#pragma unroll
+  for (int j = 0; j < EPT; j++) {
+    const int c = j * NORM_CL_THREADS + tid;
+    aw[j] = (add_w && c < ns) ? add_w[off + c] : 0.0f;
+    ow[j] = c < ns ? out_w[off + c] : 0.0f;
+  }
   pdl_trigger();
   pdl_wait();
-  if (zero_slot && rank == 0 && threadIdx.x == 0) zero_slot[t] = 0u;
+  if (zero_slot && rank == 0 && tid == 0) zero_slot[t] = 0u;
   float *xr = x + (size_t)t * E + off;
+  float v[EPT];
+#pragma unroll
+  for (int j = 0; j < EPT; j++) {
+    const int c = j * NORM_CL_THREADS + tid;
+    v[j] = c < ns ? xr[c] : 0.0f;
+  }
+  bool started = false;
+  // the cluster-wide inverse rms of the sum of squares over this rank's values
+  auto cluster_inv = [&](const float(&vals)[EPT], int k) -> uint64_t {
+    const acc128 p = block_partial128(sq_partial<EPT>(vals, ns, err), red);
+    if (!started) { cluster_wait_started(); started = true; }
+    if (warp == 0) {   // lane r pushes the partial into rank r
+      acc128 b;
+      b.lo = __shfl_sync(0xffffffffu, p.lo, 0);
+      b.hi = __shfl_sync(0xffffffffu, p.hi, 0);
+      if (lane < NORM_CL) *cluster.map_shared_rank(&sq_in[k][rank], lane) = b;
+    }
+    cluster.sync();
+    if (warp == 0 && lane == 0) {
+      acc128 tot = sq_in[k][0];
+      for (int r = 1; r < NORM_CL; r++) acc128_add(tot, sq_in[k][r]);
+      inv_sh[k] = rms_inv(tot, E, err);
+    }
+    __syncthreads();
+    return inv_sh[k];
+  };
   if (add) {
     const float *ar = add + (size_t)t * E + off;
-    if (add_w) {   // sandwich post-norm of `add`, then the residual add
-      const acc128 p = block_sum128(rms_partial(ar, ns, err), red);
-      if (threadIdx.x == 0) part[0] = p;
-      cluster.sync();
-      if (threadIdx.x == 0) {
-        acc128 tot{0ull, 0ll};
-        for (int r = 0; r < NORM_CL; r++) acc128_add(tot, *cluster.map_shared_rank(&part[0], r));
-        inv_sh = rms_inv(tot, E, err);
-      }
-      __syncthreads();
-      const uint64_t inv = inv_sh;
-      for (int i = threadIdx.x; i < ns; i += blockDim.x)
-        xb[i] = __fadd_rn(xr[i], rms_apply(ar[i], add_w[off + i], inv, err));
-    } else {
-      for (int i = threadIdx.x; i < ns; i += blockDim.x) xb[i] = __fadd_rn(xr[i], ar[i]);
+    float u[EPT];
+#pragma unroll
+    for (int j = 0; j < EPT; j++) {
+      const int c = j * NORM_CL_THREADS + tid;
+      u[j] = c < ns ? ar[c] : 0.0f;
     }
-    for (int i = threadIdx.x; i < ns; i += blockDim.x) xr[i] = xb[i];
-  } else {
-    for (int i = threadIdx.x; i < ns; i += blockDim.x) xb[i] = xr[i];
+    if (add_w) {   // sandwich post-norm of `add`, then the residual add
+      const uint64_t inv = cluster_inv(u, 0);
+#pragma unroll
+      for (int j = 0; j < EPT; j++)
+        if (j * NORM_CL_THREADS + tid < ns) u[j] = rms_apply(u[j], aw[j], inv, err);
+    }
+#pragma unroll
+    for (int j = 0; j < EPT; j++) {
+      const int c = j * NORM_CL_THREADS + tid;
+      if (c < ns) {
+        v[j] = __fadd_rn(v[j], u[j]);
+        xr[c] = v[j];
+      }
+    }
   }
-  __syncthreads();
-  {
-    const acc128 p = block_sum128(rms_partial(xb, ns, err), red);
-    if (threadIdx.x == 0) part[1] = p;
-  }
-  cluster.sync();
-  if (threadIdx.x == 0) {
-    acc128 tot{0ull, 0ll};
-    for (int r = 0; r < NORM_CL; r++) acc128_add(tot, *cluster.map_shared_rank(&part[1], r));
-    inv_sh = rms_inv(tot, E, err);
-  }
-  __syncthreads();
-  const uint64_t inv = inv_sh;
+  const uint64_t inv = cluster_inv(v, 1);
   float m = 0.0f;
-  for (int i = threadIdx.x; i < ns; i += blockDim.x) {
-    const float v = rms_apply(xb[i], out_w[off + i], inv, err);
-    nb[i] = v;
-    m = fmaxf(m, fabsf(v));
-    if (nx_out) nx_out[(size_t)t * E + off + i] = v;
+#pragma unroll
+  for (int j = 0; j < EPT; j++) {
+    const int c = j * NORM_CL_THREADS + tid;
+    if (c < ns) {
+      v[j] = rms_apply(v[j], ow[j], inv, err);
+      m = fmaxf(m, fabsf(v[j]));
+      if (nx_out) nx_out[(size_t)t * E + off + c] = v[j];
+    }
   }
-  m = block_max(m, fred);
-  if (threadIdx.x == 0) mx_loc = m;
-  cluster.sync();
-  if (threadIdx.x == 0) {
-    float s = 0.0f;
-    for (int r = 0; r < NORM_CL; r++) s = fmaxf(s, *cluster.map_shared_rank(&mx_loc, r));
-    s_all = s;
-    if (rank == 0) act.scale[t] = s;
+  m = block_max(m, fred);   // every thread holds this CTA's max
+  if (tid < NORM_CL) *cluster.map_shared_rank(&mx_in[rank], tid) = m;
+  cluster.sync();   // the last cluster access: no rank touches another's memory after it
+  float s = mx_in[0];
+#pragma unroll
+  for (int r = 1; r < NORM_CL; r++) s = fmaxf(s, mx_in[r]);
+  if (rank == 0 && tid == 0) act.scale[t] = s;
+  int8_t *q = act.q + (size_t)t * E + off;
+  int32_t *bs = act.bsum + (size_t)t * (E >> 5) + (off >> 5);
+#pragma unroll
+  for (int j = 0; j < EPT; j++) {
+    const int c = j * NORM_CL_THREADS + tid;
+    if (c < ns) {   // ns % 32 == 0: a warp's 32 columns are all in or all out
+      const int32_t qv = quant1(v[j], s);
+      q[(c & ~31) + perm_pos(lane)] = (int8_t)qv;
+      const int32_t sum = warp_sum_i32(qv);
+      if (lane == 0) bs[c >> 5] = sum;
+    }
   }
-  __syncthreads();
-  quant_blocks(nb, ns, s_all, act.q + (size_t)t * E + off, act.bsum + (size_t)t * (E >> 5) + (off >> 5),
-               threadIdx.x >> 5, blockDim.x >> 5);
-  cluster.sync();   // remote CTAs may still be reading this CTA's shared memory
 }
 
-// single-CTA fallback for widths that do not split into 8 slices of 32-column blocks
+// single-CTA fallback for any width (rows past the register-resident forms)
 constexpr int NORM_THREADS = 1024;
 
 __global__ void __launch_bounds__(NORM_THREADS)
@@ -953,13 +1030,143 @@ k_norm(float *x, const float *add, const float *add_w, const float *out_w, int E
   quant_row(nbuf, E, act.q + (size_t)t * E, act.bsum + (size_t)t * (E >> 5), act.scale + t, fred, err);
 }
 
+// ---- norm block as one CTA per token row with the row in registers (E <= 1024 EPT): thread i
+// owns columns i + 1024 j, so warp w's 32 columns of slot j are quantizer block 32 j + w. Every
+// thread takes the inverse rms from the broadcast 128-bit total itself; the norm weights are
+// read before the dependency wait.
+
+// inverse rms of a block's 128-bit sum of squares: warp 0 finishes the sum and lane 0
+// computes the island's quotient and square root once, broadcast through shared memory
+__device__ __forceinline__ uint64_t block_rms_inv(acc128 v, int n, acc128 *red, uint64_t *inv_sh, uint32_t *err) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    acc128 r;
+    r.lo = __shfl_xor_sync(0xffffffffu, v.lo, o);
+    r.hi = __shfl_xor_sync(0xffffffffu, v.hi, o);
+    acc128_add(v, r);
+  }
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  if (warp == 0) {
+    acc128 s = lane < nw ? red[lane] : acc128{0ull, 0ll};
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      acc128 r;
+      r.lo = __shfl_xor_sync(0xffffffffu, s.lo, o);
+      r.hi = __shfl_xor_sync(0xffffffffu, s.hi, o);
+      acc128_add(s, r);
+    }
+    if (lane == 0) *inv_sh = rms_inv(s, n, err);
+  }
+  __syncthreads();
+  return *inv_sh;
+}
+
+template <int EPT>
+__global__ void __launch_bounds__(NORM_REG_THREADS)
+k_norm_reg(float *x, const float *add, const float *add_w, const float *out_w, int E, DevAct act, float *nx_out,
+           uint32_t *err, uint32_t *zero_slot) {
+  __shared__ acc128 red[32];
+  __shared__ float fred[33];
+  __shared__ uint64_t inv_sh[2];
+  const int t = blockIdx.x, tid = threadIdx.x, lane = tid & 31;
+  float aw[EPT], ow[EPT];
+#pragma unroll
+  for (int j = 0; j < EPT; j++) {
+    const int c = j * NORM_REG_THREADS + tid;
+    aw[j] = (add_w && c < E) ? add_w[c] : 0.0f;
+    ow[j] = c < E ? out_w[c] : 0.0f;
+  }
+  pdl_trigger();
+  pdl_wait();
+  if (zero_slot && tid == 0) zero_slot[t] = 0u;
+  float *xr = x + (size_t)t * E;
+  float v[EPT];
+#pragma unroll
+  for (int j = 0; j < EPT; j++) {
+    const int c = j * NORM_REG_THREADS + tid;
+    v[j] = c < E ? xr[c] : 0.0f;
+  }
+  if (add) {
+    const float *ar = add + (size_t)t * E;
+    float u[EPT];
+#pragma unroll
+    for (int j = 0; j < EPT; j++) {
+      const int c = j * NORM_REG_THREADS + tid;
+      u[j] = c < E ? ar[c] : 0.0f;
+    }
+    if (add_w) {   // sandwich post-norm of `add`, then the residual add
+      const uint64_t inv = block_rms_inv(sq_partial<EPT>(u, E, err), E, red, &inv_sh[0], err);
+#pragma unroll
+      for (int j = 0; j < EPT; j++)
+        if (j * NORM_REG_THREADS + tid < E) u[j] = rms_apply(u[j], aw[j], inv, err);
+    }
+#pragma unroll
+    for (int j = 0; j < EPT; j++) {
+      const int c = j * NORM_REG_THREADS + tid;
+      if (c < E) {
+        v[j] = __fadd_rn(v[j], u[j]);
+        xr[c] = v[j];
+      }
+    }
+  }
+  const uint64_t inv = block_rms_inv(sq_partial<EPT>(v, E, err), E, red, &inv_sh[1], err);
+  float m = 0.0f;
+#pragma unroll
+  for (int j = 0; j < EPT; j++) {
+    const int c = j * NORM_REG_THREADS + tid;
+    if (c < E) {
+      v[j] = rms_apply(v[j], ow[j], inv, err);
+      m = fmaxf(m, fabsf(v[j]));
+      if (nx_out) nx_out[(size_t)t * E + c] = v[j];
+    }
+  }
+  const float s = block_max(m, fred);
+  if (tid == 0) act.scale[t] = s;
+  int8_t *q = act.q + (size_t)t * E;
+  int32_t *bs = act.bsum + (size_t)t * (E >> 5);
+#pragma unroll
+  for (int j = 0; j < EPT; j++) {
+    const int c = j * NORM_REG_THREADS + tid;
+    if (c < E) {   // E % 32 == 0: a warp's 32 columns are all in or all out
+      const int32_t qv = quant1(v[j], s);
+      q[(c & ~31) + perm_pos(lane)] = (int8_t)qv;
+      const int32_t sum = warp_sum_i32(qv);
+      if (lane == 0) bs[c >> 5] = sum;
+    }
+  }
+}
+
+// SPB_NORM_1CTA=1 keeps every row on one CTA (k_norm_reg) instead of a 4-CTA cluster
+static bool norm_one_cta() {
+  static int on = -1;
+  if (on < 0) {
+    const char *e = getenv("SPB_NORM_1CTA");
+    on = (e && e[0] == '1') ? 1 : 0;
+  }
+  return on != 0;
+}
+
 cudaError_t launch_norm(float *x, const float *add, const float *add_w, const float *out_w, int E, int ntok,
                         const DevAct &act, float *nx_out, uint32_t *err, cudaStream_t st, uint32_t *zero_slot) {
   if (E & 31) return cudaErrorInvalidValue;
-  if (E % (NORM_CL * 32) == 0) {
-    const size_t smem = (size_t)2 * (E / NORM_CL) * sizeof(float);
-    return launch_k(k_norm_cl, dim3(NORM_CL, ntok), dim3(NORM_CL_THREADS), smem, st, NORM_CL, x, add, add_w, out_w,
+  if (E % (NORM_CL * 32) == 0 && E <= NORM_CL * 2 * NORM_CL_THREADS && !norm_one_cta()) {
+    if (E <= NORM_CL * NORM_CL_THREADS)
+      return launch_k(k_norm_cl<1>, dim3(NORM_CL, ntok), dim3(NORM_CL_THREADS), 0, st, NORM_CL, x, add, add_w,
+                      out_w, E, act, nx_out, err, zero_slot);
+    return launch_k(k_norm_cl<2>, dim3(NORM_CL, ntok), dim3(NORM_CL_THREADS), 0, st, NORM_CL, x, add, add_w, out_w,
                     E, act, nx_out, err, zero_slot);
+  }
+  if (E <= 8 * NORM_REG_THREADS) {
+#define SPB_NORM_REG(EPTV)                                                                                     \
+  return launch_k(k_norm_reg<EPTV>, dim3(ntok), dim3(NORM_REG_THREADS), 0, st, 1, x, add, add_w, out_w, E, act, \
+                  nx_out, err, zero_slot)
+    if (E <= NORM_REG_THREADS) SPB_NORM_REG(1);
+    if (E <= 2 * NORM_REG_THREADS) SPB_NORM_REG(2);
+    if (E <= 4 * NORM_REG_THREADS) SPB_NORM_REG(4);
+    SPB_NORM_REG(8);
+#undef SPB_NORM_REG
   }
   const size_t smem = (size_t)2 * E * sizeof(float);
   if (smem > 48 * 1024) {
@@ -1064,14 +1271,23 @@ __global__ void __launch_bounds__(ATTN_THREADS, 2) k_attn(AttnArgs a, int cmax, 
   int32_t *ring = reinterpret_cast<int32_t *>(asm_raw);            // [STAGES][SUB*HD]
   int32_t *qs = ring + ATTN_STAGES * SUB * HD;                       // [G][HD]
   int32_t *sc = qs + G * HD;                                         // [G][cmax] scores, then e
-  acc128 *nacc = reinterpret_cast<acc128 *>(sc + ((G * cmax + 3) & ~3));  // [GROUPS][G][HD]
+  // [GROUPS][G][HD] this CTA's V-sums (absent when one thread per head dim pushes them
+  // straight from registers), then with CL > 1 the [CL][G][HD/CL] V-sums pushed by each rank
+  const bool direct = GROUPS == 1 && CL > 1;
+  acc128 *nacc = reinterpret_cast<acc128 *>(sc + ((G * cmax + 3) & ~3));
+  acc128 *gat = nacc + (direct ? 0 : GROUPS * G * HD);
   __shared__ __align__(8) uint64_t full[ATTN_STAGES];
   __shared__ int32_t mx_loc[G];
   __shared__ int64_t s_loc[G];
   __shared__ int32_t mx_all[G];
+  __shared__ int32_t mx_in[16][G];        // CL > 1: each rank's score maximum, pushed by that rank
+  __shared__ int64_t s_in[16][G];         // CL > 1: each rank's exponential sum
   __shared__ float fred[33];
 
   const int rank = CL > 1 ? (int)cluster.block_rank() : 0;
+  // the partials are pushed into the owning rank's shared memory (no remote loads): this
+  // arrival, waited on before the first push, guarantees every rank of the cluster has started
+  if (CL > 1) asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
   const int g = blockIdx.y, t = blockIdx.z;
   const int QD = a.NH * HD;
   int p, P;
@@ -1187,27 +1403,38 @@ __global__ void __launch_bounds__(ATTN_THREADS, 2) k_attn(AttnArgs a, int cmax, 
   lmax = max(lmax, __shfl_xor_sync(0xffffffffu, lmax, 8));
   lmax = max(lmax, __shfl_xor_sync(0xffffffffu, lmax, 16));
   if (lane < G && lmax != INT32_MIN) atomicMax(&mx_loc[lane], lmax);
-  if (CL > 1) cluster.sync();
-  else __syncthreads();
+  __syncthreads();
+  if (CL > 1) {
+    asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
+    if (threadIdx.x < CL * G) {
+      const int r = threadIdx.x / G, h = threadIdx.x % G;
+      *cluster.map_shared_rank(&mx_in[rank][h], r) = mx_loc[h];
+    }
+    cluster.sync();
+  }
   if (threadIdx.x < G) {
     int32_t m = mx_loc[threadIdx.x];
-    for (int r = 0; r < CL; r++)
-      if (r != rank) m = max(m, *cluster.map_shared_rank(&mx_loc[threadIdx.x], r));
+    for (int r = 0; r < (CL > 1 ? CL : 0); r++) m = max(m, mx_in[r][threadIdx.x]);
     mx_all[threadIdx.x] = m;
   }
   __syncthreads();
-  // ---- phase 2: integer exponentials and their exact sum
-#pragma unroll
-  for (int h = 0; h < G; h++) {
-    int64_t part = 0;
-    for (int j = threadIdx.x; j < cn; j += ATTN_THREADS) {
-      const int64_t d = (((int64_t)sc[h * cmax + j] - (int64_t)mx_all[h]) * ONE) >> 14;
-      const int32_t e = (int32_t)exp_fixed(d);
-      sc[h * cmax + j] = e;
-      part += e;
+  // ---- phase 2: integer exponentials and their exact sum, one (head, position) per thread
+  // (a warp's items may span several heads: one warp sum per head it covers)
+  for (int i0 = 0; i0 < G * cn; i0 += ATTN_THREADS) {
+    const int i = i0 + threadIdx.x;
+    const int h = i < G * cn ? i / cn : G - 1, j = i - h * cn;
+    int64_t e = 0;
+    if (i < G * cn) {
+      const int64_t dz = (((int64_t)sc[h * cmax + j] - (int64_t)mx_all[h]) * ONE) >> 14;
+      e = exp_fixed(dz);
+      sc[h * cmax + j] = (int32_t)e;
     }
-    part = warp_sum_i64(part);
-    if (lane == 0 && part) atomicAdd(reinterpret_cast<unsigned long long *>(&s_loc[h]), (unsigned long long)part);
+    const int h0 = __shfl_sync(0xffffffffu, h, 0);
+#pragma unroll 1
+    for (int hh = h0; hh <= __shfl_sync(0xffffffffu, h, 31); hh++) {
+      const int64_t part = warp_sum_i64(h == hh ? e : 0);
+      if (lane == 0 && part) atomicAdd(reinterpret_cast<unsigned long long *>(&s_loc[hh]), (unsigned long long)part);
+    }
   }
   __syncthreads();
   // ---- phase 3: exact 128-bit V-sum, V slices streamed through the same ring
@@ -1244,28 +1471,52 @@ __global__ void __launch_bounds__(ATTN_THREADS, 2) k_attn(AttnArgs a, int cmax, 
       issue(i + ATTN_STAGES);
     }
   }
+  // push: head dim dd goes to rank dd / DPR, slot [this rank][h][dd % DPR]
+  if (direct) {
+    const int o = d / DPR;
 #pragma unroll
-  for (int h = 0; h < G; h++) nacc[(grp * G + h) * HD + d] = acc[h];
-  __syncthreads();
-  if (GROUPS > 1) {
-    for (int i = threadIdx.x; i < G * HD; i += ATTN_THREADS) {
-      acc128 s = nacc[i];
-      for (int r = 1; r < GROUPS; r++) acc128_add(s, nacc[r * G * HD + i]);
-      nacc[i] = s;
+    for (int h = 0; h < G; h++) *cluster.map_shared_rank(&gat[(rank * G + h) * DPR + (d - o * DPR)], o) = acc[h];
+  } else {
+#pragma unroll
+    for (int h = 0; h < G; h++) nacc[(grp * G + h) * HD + d] = acc[h];
+    __syncthreads();
+    if (GROUPS > 1) {
+      for (int i = threadIdx.x; i < G * HD; i += ATTN_THREADS) {
+        acc128 s = nacc[i];
+        for (int r = 1; r < GROUPS; r++) acc128_add(s, nacc[r * G * HD + i]);
+        nacc[i] = s;
+      }
     }
+    __syncthreads();
+    if (CL > 1)
+      for (int i = threadIdx.x; i < G * HD; i += ATTN_THREADS) {
+        const int h = i / HD, dd = i % HD, o = dd / DPR;
+        *cluster.map_shared_rank(&gat[(rank * G + h) * DPR + (dd - o * DPR)], o) = nacc[i];
+      }
   }
-  if (CL > 1) cluster.sync();
-  else __syncthreads();
+  if (CL > 1) {
+    if (threadIdx.x < CL * G) {
+      const int r = threadIdx.x / G, h = threadIdx.x % G;
+      *cluster.map_shared_rank(&s_in[rank][h], r) = s_loc[h];
+    }
+    cluster.sync();   // the last cluster access: after it no rank touches another's memory
+  }
   // ---- phase 4: combine the cluster's partials; rank r finalizes HD/CL dims per head
   float omax = 0.0f;
   for (int i = threadIdx.x; i < G * DPR; i += ATTN_THREADS) {
-    const int h = i / DPR, dd = rank * DPR + (i % DPR);
-    acc128 N = nacc[h * HD + dd];
-    int64_t S = s_loc[h];
-    for (int r = 0; r < CL; r++) {
-      if (r == rank) continue;
-      acc128_add(N, *cluster.map_shared_rank(&nacc[h * HD + dd], r));
-      S += *cluster.map_shared_rank(&s_loc[h], r);
+    const int h = i / DPR, j = i % DPR, dd = rank * DPR + j;
+    acc128 N;
+    int64_t S;
+    if (CL > 1) {
+      N = gat[h * DPR + j];
+      S = s_in[0][h];
+      for (int r = 1; r < CL; r++) {
+        acc128_add(N, gat[(r * G + h) * DPR + j]);
+        S += s_in[r][h];
+      }
+    } else {
+      N = nacc[h * HD + dd];
+      S = s_loc[h];
     }
     const int64_t hi = (int64_t)(((uint64_t)N.hi << 16) | (N.lo >> 48));   // N * 2^16, |N| < 2^78
     const uint64_t lo = N.lo << 16;
@@ -1278,15 +1529,15 @@ __global__ void __launch_bounds__(ATTN_THREADS, 2) k_attn(AttnArgs a, int cmax, 
     omax = block_max(omax, fred);
     if (threadIdx.x == 0) atomicMax(a.ao_max + t, __float_as_uint(omax));
   }
-  if (CL > 1) cluster.sync();   // peers' shared memory stays live until every rank has read it
 }
 
 
 template <int HD, int G>
-static size_t attn_smem(int cmax) {
-  constexpr int SUB = AttnSub<HD>::SUB;
+static size_t attn_smem(int cmax, int cl) {
+  constexpr int SUB = AttnSub<HD>::SUB, GROUPS = ATTN_THREADS / HD;
+  const bool direct = GROUPS == 1 && cl > 1;
   return (size_t)ATTN_STAGES * SUB * HD * 4 + (size_t)G * HD * 4 + (size_t)((G * cmax + 3) & ~3) * 4 +
-         (size_t)(ATTN_THREADS / HD) * G * HD * sizeof(acc128);
+         (direct ? 0 : (size_t)GROUPS * G * HD * sizeof(acc128)) + (cl > 1 ? (size_t)G * HD * sizeof(acc128) : 0);
 }
 
 template <int HD, int G>
@@ -1310,7 +1561,7 @@ static cudaError_t attn_cl(const AttnArgs &a, cudaStream_t st) {
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3(16, 1, 1);
       cfg.blockDim = dim3(ATTN_THREADS);
-      cfg.dynamicSmemBytes = attn_smem<HD, G>((a.P + 15) / 16);
+      cfg.dynamicSmemBytes = attn_smem<HD, G>((a.P + 15) / 16, 16);
       cudaLaunchAttribute attr[1];
       attr[0].id = cudaLaunchAttributeClusterDimension;
       attr[0].val.clusterDim.x = 16;
@@ -1328,9 +1579,9 @@ static cudaError_t attn_cl(const AttnArgs &a, cudaStream_t st) {
   const int span = a.win >= 0 ? std::min(a.P, a.win) : a.P;
   int cl = 1;
   while (cl < clmax && ((long)a.ntok * a.NKV * cl < 2L * nsm || span > cl * ATTN_SPAN)) cl *= 2;
-  while (cl < clmax && attn_smem<HD, G>((a.P + cl - 1) / cl) > 200 * 1024) cl *= 2;
+  while (cl < clmax && attn_smem<HD, G>((a.P + cl - 1) / cl, cl) > 200 * 1024) cl *= 2;
   const int cmax = (a.P + cl - 1) / cl;
-  const size_t smem = attn_smem<HD, G>(cmax);
+  const size_t smem = attn_smem<HD, G>(cmax, cl);
   if (smem > 200 * 1024) return cudaErrorInvalidValue;
   return launch_k(kern, dim3(cl, a.NKV, a.ntok), dim3(ATTN_THREADS), smem, st, cl, a, cmax, cl);
 }
