@@ -64,6 +64,9 @@ def parse():
     p.add_argument("--batch", type=int, default=64,
                    help="sessions decoded together for the b64 figure (0: skip it)")
     p.add_argument("--batch-steps", type=int, default=16)
+    p.add_argument("--tp", action="store_true",
+                   help="N>1: also time one session tensor-parallel over all N GPUs (strong scaling), "
+                        "reported as the line's 'tp' object")
     return p.parse_args()
 
 
@@ -290,6 +293,44 @@ def measure_batch(m, cfg, B, K, W, seed, max_over_ranks):
                       "B argmaxes D2H per step)", "prefill_s_untimed": round(prefill_s, 2)}
 
 
+def measure_tp(cfg, args, rank, local, world, max_over_ranks, barrier, p2p=True):
+    """One session of the model split over the group (spb_model_synthetic_tp): K greedy steps
+    timed with CUDA events on the session stream, max over ranks; every rank produces the
+    whole model's tokens."""
+    import torch
+    import spb200
+    import spmodel
+    uid = spb200.tp_uid_from_dist()
+    tp = spb200.TensorParallel(uid, rank, world, device=local)
+    if p2p:
+        tp.enable_p2p(16 * cfg.n_embd)
+    K, W = args.steps, args.warmup
+    m = spb200.Model.synthetic_tp(cfg, tp, seed=args.seed)
+    s = m.session(args.prefill + W + K + 8)
+    stream = torch.cuda.ExternalStream(s.stream(), device=torch.device("cuda", local))
+    toks = spmodel.gen_tokens(args.seed + 100, args.prefill, cfg.n_vocab)
+    s.prefill(toks, logits=False)
+    tok = int(toks[-1])
+    tok = int(s.greedy(tok, W)[-1])
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    s.greedy(tok, K)
+    e1.record(stream)
+    e1.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1))
+    barrier()
+    s.close()
+    m.free()
+    tp.close()
+    return {"value": round(K / (ms / 1e3), 3), "unit": "tokens/s", "n_gpus": world, "steps": K,
+            "ms_per_step": round(ms / K, 4), "scaling": "strong",
+            "parallelism": f"tp{world}: heads, FFN columns and LM-head rows split; int64 all-reduce after "
+                           f"the attention output and FFN down projections, quantizer-max and argmax-key "
+                           f"max-reduces ({'one-shot kernel over peer memory' if p2p else 'NCCL'}); "
+                           f"logits all-gathered by NCCL"}
+
+
 def tile_report(tiles, pts):
     """CTA 0's ring tiles: copy latency (issue -> found complete) and the gap between
     consecutive issues, as percentiles, over the last 256 tiles of the step (the LM head)."""
@@ -402,6 +443,11 @@ def run_spb(args):
         b64 = measure_batch(m, cfg, args.batch, args.batch_steps, 3, args.seed + rank, max_over_ranks)
         b64["value"] = round(world * b64["value"], 3)
 
+    tpr = None
+    if args.tp and world > 1:
+        tpr = measure_tp(cfg, args, rank, local, world, max_over_ranks, barrier, p2p=True)
+        tpr["nccl_only"] = measure_tp(cfg, args, rank, local, world, max_over_ranks, barrier, p2p=False)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         sys.path.insert(0, ORACLE)
@@ -432,6 +478,8 @@ def run_spb(args):
         "cpu_baseline": cpu,
         "b64": b64,
     }
+    if tpr:
+        line["tp"] = tpr
     s.close()
     m.free()
     if world > 1:

@@ -183,6 +183,42 @@ int  spb_graph_end(void *stream, void **graph_exec);
 int  spb_graph_launch(void *graph_exec, void *stream);
 void spb_graph_free(void *graph_exec);
 
+/* ---- tensor parallel: one process per GPU ----------------------------------
+ * Sharding of the per-layer orchestration (gemma3_forward, gemma3.c:39-148; qwen3_forward_ex2,
+ * forward.c:87-291) over a group of GPUs. Rank r holds query heads [h0, h0+nh) and their KV
+ * heads (Q/K/V rows), the FFN columns [f0, f0+nff) (gate/up rows, down columns), the attention
+ * output projection's columns of its heads and the LM-head rows [v0, v0+nv); norms, tables
+ * and the embedding are whole on every rank. The two K-split matrices per layer end in an
+ * all-reduce of their int64 partial sums (exact in any order); the quantizer's row max of a
+ * split producer is all-reduced first; the LM head all-reduces its greedy-argmax keys and
+ * all-gathers its logits, so every rank returns the full-vocabulary logits and the argmax of
+ * the unsplit model, byte for byte. Exchanges run on NCCL (loaded at run time). */
+typedef struct spb_tp spb_tp;
+#define SPB_TP_ID_BYTES 128
+/* out = {h0, nh, kv0, nkv, f0, nff, v0, nv} of `rank`; no device needed. Requires n_head_kv,
+ * n_vocab divisible by world and n_ff by 32 * world. */
+int  spb_tp_shard(const spb_config *cfg, int rank, int world, int32_t out[8]);
+int  spb_tp_unique_id(uint8_t id[SPB_TP_ID_BYTES]);   /* on one rank; every rank opens with it */
+int  spb_tp_open(const uint8_t id[SPB_TP_ID_BYTES], int rank, int world, int device, spb_tp **out);
+void spb_tp_close(spb_tp *tp);
+int  spb_tp_rank(const spb_tp *tp);
+int  spb_tp_world(const spb_tp *tp);
+/* Optional, collective: a mailbox of `cap` 8-byte values per rank and exchange parity in this
+ * rank's HBM, mapped into every rank through CUDA IPC; afterwards every exchange of at most cap
+ * values (the decode step's) runs as one kernel over peer memory (stores over NVLink, a system
+ * fence, a flag per rank, a wait bounded at 2 s that reports SPB_ERANGE "timeout" when a rank
+ * does not arrive) instead of NCCL. init returns this rank's blob; connect takes all ranks'
+ * blobs in rank order (SPB_TP_P2P_BLOB_BYTES each) and refuses two ranks on one GPU. */
+#define SPB_TP_P2P_BLOB_BYTES 80
+int  spb_tp_p2p_init(spb_tp *tp, int cap, uint8_t blob[SPB_TP_P2P_BLOB_BYTES]);
+int  spb_tp_p2p_connect(spb_tp *tp, const uint8_t *blobs);
+/* The rank's shard of the counter-generated model of spb_model_synthetic (same bytes as the
+ * corresponding slices of the unsplit model), on the group's device. */
+int  spb_model_synthetic_tp(const spb_config *cfg, uint64_t seed, spb_tp *tp, spb_model **out);
+/* The rank's shard of a whole host model (the same descriptor spb_model_upload takes): only
+ * the rank's rows and columns are copied to its device. */
+int  spb_model_upload_tp(const spb_model_desc *desc, spb_tp *tp, spb_model **out);
+
 /* ---- host-side tables (no device needed) ------------------------------------ */
 int      spb_rope_freq_table(float base, int d, uint64_t *W);      /* [d/2] turns Q64 */
 void     spb_cordic_tables(uint64_t T[30], uint64_t *gain_q62);

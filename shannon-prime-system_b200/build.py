@@ -26,8 +26,8 @@ REF_INCLUDE = os.environ.get("SPB_REF_INCLUDE", "/root/reference/include")
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVFLAGS = ["-std=c++17", "-O3", "-lineinfo", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr"] + ARCH
-CU_SRCS = ["spb_kernels.cu", "spb_decode.cu", "spb_runtime.cu", "spb_noalloc.cu"]
-HDRS = ["spb_exact.cuh", "spb_kernels.cuh", "spb_async.cuh", "spb_device.cuh"]
+CU_SRCS = ["spb_kernels.cu", "spb_decode.cu", "spb_runtime.cu", "spb_noalloc.cu", "spb_tp.cu"]
+HDRS = ["spb_exact.cuh", "spb_kernels.cuh", "spb_async.cuh", "spb_device.cuh", "spb_tp.cuh"]
 
 
 def _newer(out, deps):
@@ -60,7 +60,7 @@ def build(force: bool = False, verbose: bool = False) -> dict:
     with cf.ThreadPoolExecutor(max_workers=4) as ex:
         list(ex.map(lambda c: _run(c, verbose), jobs))
     if force or jobs or _newer(CORE_SO, objs):
-        _run([NVCC] + ARCH + ["-shared", "-o", CORE_SO] + objs + ["-lcudart"], verbose)
+        _run([NVCC] + ARCH + ["-shared", "-o", CORE_SO] + objs + ["-lcudart", "-ldl"], verbose)
     out = {"core": CORE_SO, "l1": None}
     l1_src = os.path.join(CSRC, "spb_l1.c")
     if os.path.exists(os.path.join(REF_INCLUDE, "sp", "sp_l1.h")):

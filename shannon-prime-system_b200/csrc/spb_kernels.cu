@@ -114,7 +114,7 @@ template <int NT, int EPI, int NCH, int RPW>
 __global__ void __launch_bounds__(GEMV_THREADS)
 k_gemv(DevQ4B w, DevQ4B w2, DevAct act, float *__restrict__ y, int ldy, uint32_t *err, uint32_t *ymax,
        unsigned long long *amax) {
-  constexpr int NM = (EPI == EPI_STORE) ? 1 : 2;
+  constexpr int NM = epi_pair(EPI) ? 2 : 1;
   extern __shared__ __align__(16) uint8_t smem_raw[];
   __shared__ float wmax[GEMV_WARPS][NT];
   const int K = w.cols, nblk = K >> 5, kw = K >> 2;
@@ -175,10 +175,12 @@ k_gemv(DevQ4B w, DevQ4B w2, DevAct act, float *__restrict__ y, int ldy, uint32_t
   int64_t pa = 0, pa2 = 0;
   int prow = -1, ptok = 0, npend = 0;
   auto flush = [&]() {
-    if (prow >= 0) {
+    if (EPI == EPI_I64) {
+      if (prow >= 0) reinterpret_cast<int64_t *>(y)[(size_t)ptok * ldy + prow] = pa;
+    } else if (prow >= 0) {
       const double d = dsc[ptok];
       float v = __double2float_rn(__dmul_rn(__ll2double_rn(pa), d));
-      if (EPI != EPI_STORE) {
+      if (epi_pair(EPI)) {
         const float u = __double2float_rn(__dmul_rn(__ll2double_rn(pa2), d));
         if (!(fabsf(v) < 2048.0f)) { raise_err(err, ERR_ACT_RANGE); v = 0.0f; }
         const float gv = (EPI == EPI_GELU_MUL) ? gelu_exact(v) : silu_exact(v);
@@ -311,7 +313,7 @@ template <int NT, int EPI, int NCH>
 static cudaError_t gemv_rpw(const DevQ4B &w, const DevQ4B &w2, const DevAct &act, float *y, int ldy,
                             uint32_t *err, uint32_t *ymax, unsigned long long *amax, cudaStream_t st,
                             int grid_limit) {
-  constexpr int NM = (EPI == EPI_STORE) ? 1 : 2;
+  constexpr int NM = epi_pair(EPI) ? 2 : 1;
   constexpr int R0 = 16 / (NCH * NM);
   constexpr int RPW = NT > 1 ? 1 : (R0 < 1 ? 1 : (R0 > 4 ? 4 : R0));
   return gemv_launch<NT, EPI, NCH, RPW>(w, w2, act, y, ldy, err, ymax, amax, st, grid_limit);
@@ -412,7 +414,7 @@ template <int MT, int TH, int EPI, bool SMALL>
 __global__ void __launch_bounds__(GEMM_THREADS * TH, 2)
 k_gemm(DevQ4B w, DevQ4B w2, DevAct act, int ntok, float *__restrict__ y, int ldy, uint32_t *err, uint32_t *ymax,
        unsigned long long *amax) {
-  constexpr int NM = (EPI == EPI_STORE) ? 1 : 2;
+  constexpr int NM = epi_pair(EPI) ? 2 : 1;
   constexpr int M = MT * TH * 16;
   constexpr int NTHR = GEMM_THREADS * TH;
   using SM = GemmSmem<MT * TH, NM>;
@@ -557,8 +559,12 @@ k_gemm(DevQ4B w, DevQ4B w2, DevAct act, int ntok, float *__restrict__ y, int ldy
         const int t = (mt0 + mt) * 16 + g + (i >= 2 ? 8 : 0);
         const int row = row0 + warp * 8 + tig * 2 + (i & 1);
         if (t >= ntok || row >= rows) continue;
+        if (EPI == EPI_I64) {
+          reinterpret_cast<int64_t *>(y)[(size_t)t * ldy + row] = acc[0][mt][i];
+          continue;
+        }
         float v = __double2float_rn(__dmul_rn(__ll2double_rn(acc[0][mt][i]), dsc[t]));
-        if (EPI != EPI_STORE) {
+        if (epi_pair(EPI)) {
           const float u = __double2float_rn(__dmul_rn(__ll2double_rn(acc[NM - 1][mt][i]), dsc[t]));
           if (!(fabsf(v) < 2048.0f)) { raise_err(err, ERR_ACT_RANGE); v = 0.0f; }
           v = __fmul_rn(EPI == EPI_GELU_MUL ? gelu_exact(v) : silu_exact(v), u);
@@ -583,7 +589,7 @@ k_gemm(DevQ4B w, DevQ4B w2, DevAct act, int ntok, float *__restrict__ y, int ldy
 template <int MT, int TH, int EPI, bool SMALL>
 static cudaError_t gemm_launch(const DevQ4B &w, const DevQ4B &w2, const DevAct &act, int ntok, float *y, int ldy,
                                uint32_t *err, uint32_t *ymax, unsigned long long *amax, cudaStream_t st) {
-  constexpr int NM = (EPI == EPI_STORE) ? 1 : 2;
+  constexpr int NM = epi_pair(EPI) ? 2 : 1;
   const size_t smem = GemmSmem<MT * TH, NM>::TOTAL;
   auto kern = k_gemm<MT, TH, EPI, SMALL>;
   static bool configured = false;
@@ -616,7 +622,7 @@ static bool gemm_split() {
 template <int EPI>
 static cudaError_t gemm_mt(const DevQ4B &w, const DevQ4B &w2, const DevAct &act, int ntok, float *y, int ldy,
                            uint32_t *err, uint32_t *ymax, unsigned long long *amax, cudaStream_t st) {
-  const bool small = w.small && (EPI == EPI_STORE || w2.small);
+  const bool small = w.small && (!epi_pair(EPI) || w2.small);
 #define SPB_GEMM_MT(MTV, THV)                                                                        \
   return small ? gemm_launch<MTV, THV, EPI, true>(w, w2, act, ntok, y, ldy, err, ymax, amax, st) \
                : gemm_launch<MTV, THV, EPI, false>(w, w2, act, ntok, y, ldy, err, ymax, amax, st)
@@ -645,7 +651,10 @@ cudaError_t launch_gemv(const DevQ4B &w, const DevQ4B *w2, const DevAct &act, in
                         int epi, uint32_t *err, cudaStream_t st, int grid_limit, uint32_t *ymax,
                         unsigned long long *amax) {
   if ((w.cols & 31) || w.cols <= 0 || w.rows <= 0 || w.cols > 16384) return cudaErrorInvalidValue;
-  if (epi != EPI_STORE && (!w2 || w2->rows != w.rows || w2->cols != w.cols)) return cudaErrorInvalidValue;
+  if (epi < EPI_STORE || epi > EPI_I64) return cudaErrorInvalidValue;
+  if (epi_pair(epi) && (!w2 || w2->rows != w.rows || w2->cols != w.cols)) return cudaErrorInvalidValue;
+  if (epi == EPI_I64 && (ymax || amax)) return cudaErrorInvalidValue;
+  const size_t yb = (size_t)epi_bytes(epi);   // y row offsets below are in elements of this size
   // token batches (and row counts the k_gemv templates do not cover): the tensor-core GEMM
   const bool odd = ntok > 1 && (ntok & (ntok - 1)) != 0;
   if ((ntok >= 16 || odd) && grid_limit == 0 && (w.cols & 255) == 0 && (gemm_enabled() || odd)) {
@@ -653,14 +662,15 @@ cudaError_t launch_gemv(const DevQ4B &w, const DevQ4B *w2, const DevAct &act, in
     for (int t0 = 0; t0 < ntok; t0 += 64) {
       const int n = std::min(64, ntok - t0);
       const DevAct a2{act.q + (size_t)t0 * w.cols, act.bsum + (size_t)t0 * (w.cols >> 5), act.scale + t0};
-      float *y2 = y + (size_t)t0 * ldy;
+      float *y2 = reinterpret_cast<float *>(reinterpret_cast<char *>(y) + (size_t)t0 * ldy * yb);
       uint32_t *ym = ymax ? ymax + t0 : nullptr;
       unsigned long long *am = amax ? amax + t0 : nullptr;
       cudaError_t e;
       switch (epi) {
         case EPI_STORE: e = gemm_mt<EPI_STORE>(w, ww2, a2, n, y2, ldy, err, ym, am, st); break;
         case EPI_GELU_MUL: e = gemm_mt<EPI_GELU_MUL>(w, ww2, a2, n, y2, ldy, err, ym, am, st); break;
-        default: e = gemm_mt<EPI_SILU_MUL>(w, ww2, a2, n, y2, ldy, err, ym, am, st); break;
+        case EPI_SILU_MUL: e = gemm_mt<EPI_SILU_MUL>(w, ww2, a2, n, y2, ldy, err, ym, am, st); break;
+        default: e = gemm_mt<EPI_I64>(w, ww2, a2, n, y2, ldy, err, ym, am, st); break;
       }
       if (e != cudaSuccess) return e;
     }
@@ -673,11 +683,11 @@ cudaError_t launch_gemv(const DevQ4B &w, const DevQ4B *w2, const DevAct &act, in
     const DevAct a2{act.q + (size_t)h * w.cols, act.bsum + (size_t)h * (w.cols >> 5), act.scale + h};
     cudaError_t e = launch_gemv(w, w2, act, h, y, ldy, epi, err, st, grid_limit, ymax, amax);
     if (e != cudaSuccess) return e;
-    return launch_gemv(w, w2, a2, h, y + (size_t)h * ldy, ldy, epi, err, st, grid_limit, ymax ? ymax + h : nullptr,
-                       amax ? amax + h : nullptr);
+    return launch_gemv(w, w2, a2, h, reinterpret_cast<float *>(reinterpret_cast<char *>(y) + (size_t)h * ldy * yb),
+                       ldy, epi, err, st, grid_limit, ymax ? ymax + h : nullptr, amax ? amax + h : nullptr);
   }
   const DevQ4B ww2 = w2 ? *w2 : w;
-  if (ntok == 1 && grid_limit == 0 && ring_gemv_enabled()) {   // batch 1: the TMA-ring GEMV
+  if (ntok == 1 && grid_limit == 0 && epi != EPI_I64 && ring_gemv_enabled()) {   // batch 1: the TMA-ring GEMV
     const int mode = epi == EPI_GELU_MUL ? 1 : epi == EPI_SILU_MUL ? 2 : amax ? 3 : 0;
     if (gemv_ring_covers(w, mode)) {
       GemvRingArgs g{w, ww2, mode, act, y, ymax, amax, err};
@@ -688,6 +698,7 @@ cudaError_t launch_gemv(const DevQ4B &w, const DevQ4B *w2, const DevAct &act, in
     case EPI_STORE: return gemv_nt<EPI_STORE>(w, ww2, act, ntok, y, ldy, err, ymax, amax, st, grid_limit);
     case EPI_GELU_MUL: return gemv_nt<EPI_GELU_MUL>(w, ww2, act, ntok, y, ldy, err, ymax, amax, st, grid_limit);
     case EPI_SILU_MUL: return gemv_nt<EPI_SILU_MUL>(w, ww2, act, ntok, y, ldy, err, ymax, amax, st, grid_limit);
+    case EPI_I64: return gemv_nt<EPI_I64>(w, ww2, act, ntok, y, ldy, err, ymax, amax, st, grid_limit);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -1654,6 +1665,32 @@ cudaError_t launch_argmax_take(unsigned long long *keys, int ntok, int32_t *out,
   return launch_k(k_argmax_take, dim3(1), dim3(128), 0, st, 1, keys, ntok, out);
 }
 
+__global__ void k_scale_i64(const int64_t *acc, const float *scale, int n, float *y, int ldy) {
+  pdl_trigger();
+  pdl_wait();
+  const int t = blockIdx.y;
+  const double d = __dmul_rn(__ddiv_rn((double)scale[t], 127.0), 0x1p-24);
+  for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < n; j += gridDim.x * blockDim.x)
+    y[(size_t)t * ldy + j] = __double2float_rn(__dmul_rn(__ll2double_rn(acc[(size_t)t * n + j]), d));
+}
+
+cudaError_t launch_scale_i64(const int64_t *acc, const float *scale, int ntok, int n, float *y, int ldy,
+                             cudaStream_t st) {
+  return launch_k(k_scale_i64, dim3((n + 255) / 256, ntok), dim3(256), 0, st, 1, acc, scale, n, y, ldy);
+}
+
+// the key's low word is 0xFFFFFFFF - row: a row offset subtracts from it
+__global__ void k_keys_rebase(unsigned long long *keys, int ntok, int base) {
+  pdl_trigger();
+  pdl_wait();
+  for (int t = threadIdx.x; t < ntok; t += blockDim.x)
+    if (keys[t]) keys[t] -= (unsigned long long)(uint32_t)base;
+}
+
+cudaError_t launch_keys_rebase(unsigned long long *keys, int ntok, int base, cudaStream_t st) {
+  return launch_k(k_keys_rebase, dim3(1), dim3(128), 0, st, 1, keys, ntok, base);
+}
+
 __global__ void k_advance(int32_t *pos_dev, int n, const int32_t *src_tok, int32_t *dst_tok) {
   pdl_trigger();
   pdl_wait();
@@ -1702,6 +1739,39 @@ cudaError_t launch_synth_scales(uint16_t *dst, int rows, int nblk_src, int nblk_
                                 cudaStream_t st) {
   if (nblk_src != nblk_dst) return cudaErrorInvalidValue;
   k_synth_scales<<<148 * 8, 256, 0, st>>>(dst, rows, nblk_src, exp_field, key);
+  return cudaGetLastError();
+}
+
+__global__ void k_synth_codes_cols(uint64_t *dst, int rows, size_t dst_words, size_t src_words, size_t off_words,
+                                   uint64_t key) {
+  const size_t n = (size_t)rows * dst_words;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+    const size_t r = i / dst_words, j = i - r * dst_words;
+    dst[i] = splitmix64(r * src_words + off_words + j + key);
+  }
+}
+
+__global__ void k_synth_scales_cols(uint16_t *dst, int rows, int nblk_dst, int nblk_src, int blk_off, int exp_field,
+                                    uint64_t key) {
+  const size_t n = (size_t)rows * nblk_dst;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+    const size_t r = i / nblk_dst, j = i - r * nblk_dst;
+    const uint64_t w = splitmix64(r * (size_t)nblk_src + (size_t)blk_off + j + key);
+    dst[i] = (uint16_t)(((uint32_t)exp_field << 10) | (uint32_t)(w & 0x3FFull));
+  }
+}
+
+cudaError_t launch_synth_codes_cols(uint8_t *dst, int rows, size_t dst_row_bytes, size_t src_row_bytes,
+                                   size_t src_off, uint64_t key, cudaStream_t st) {
+  if ((dst_row_bytes | src_row_bytes | src_off) % 8 || ((uintptr_t)dst & 7)) return cudaErrorInvalidValue;
+  k_synth_codes_cols<<<148 * 8, 256, 0, st>>>(reinterpret_cast<uint64_t *>(dst), rows, dst_row_bytes / 8,
+                                              src_row_bytes / 8, src_off / 8, key);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_synth_scales_cols(uint16_t *dst, int rows, int nblk_dst, int nblk_src, int blk_off,
+                                    int exp_field, uint64_t key, cudaStream_t st) {
+  k_synth_scales_cols<<<148 * 8, 256, 0, st>>>(dst, rows, nblk_dst, nblk_src, blk_off, exp_field, key);
   return cudaGetLastError();
 }
 

@@ -43,7 +43,12 @@ enum GemvEpi : int {
   EPI_STORE = 0,      // y[t][j] = acc -> f32
   EPI_GELU_MUL = 1,   // y[t][j] = gelu_exact(gate_j) * up_j   (two matrices)
   EPI_SILU_MUL = 2,   // y[t][j] = silu_exact(gate_j) * up_j
+  EPI_I64 = 3,        // y viewed as int64: y[t][j] = the exact accumulator, unscaled (the partial
+                      // sums of a K-split matrix, all-reduced before launch_scale_i64)
 };
+__host__ __device__ constexpr bool epi_pair(int epi) { return epi == EPI_GELU_MUL || epi == EPI_SILU_MUL; }
+// bytes of one y element
+__host__ __device__ constexpr int epi_bytes(int epi) { return epi == EPI_I64 ? 8 : 4; }
 
 // y[t][j] for t < ntok over `w` (and `w2` for the gated epilogues). ymax (nullable):
 // per-token slots receiving atomicMax of the f32 bits of max |y| (the next quantizer's scale).
@@ -51,6 +56,13 @@ enum GemvEpi : int {
 cudaError_t launch_gemv(const DevQ4B &w, const DevQ4B *w2, const DevAct &act, int ntok, float *y,
                         int ldy, int epi, uint32_t *err, cudaStream_t st, int grid_limit = 0,
                         uint32_t *ymax = nullptr, unsigned long long *amax = nullptr);
+
+// y[t][j] = (float)(acc[t][j] * (scale[t] / 127 * 2^-24)), the GEMV epilogue's rounding, for
+// n outputs of ntok rows (acc row stride n, y row stride ldy)
+cudaError_t launch_scale_i64(const int64_t *acc, const float *scale, int ntok, int n, float *y, int ldy,
+                             cudaStream_t st);
+// greedy-argmax keys of a row slice starting at global row `base` -> keys over global rows
+cudaError_t launch_keys_rebase(unsigned long long *keys, int ntok, int base, cudaStream_t st);
 
 // Quantize ntok rows of K floats (row stride ldu) into `act`. maxslot: per-row max |u| as
 // f32 bits already produced upstream; NULL computes it first.
@@ -115,6 +127,12 @@ cudaError_t launch_advance(int32_t *pos_dev, int n, const int32_t *src_tok, int3
 cudaError_t launch_synth_codes(uint8_t *dst, size_t nbytes, uint64_t key, cudaStream_t st);
 cudaError_t launch_synth_scales(uint16_t *dst, int rows, int nblk_src, int nblk_dst, int exp_field,
                                 uint64_t key, cudaStream_t st);
+// column slices of a generated matrix: rows of dst_row_bytes (scales: nblk_dst) taken at byte
+// (block) offset src_off of source rows src_row_bytes (nblk_src) long; keys as above
+cudaError_t launch_synth_codes_cols(uint8_t *dst, int rows, size_t dst_row_bytes, size_t src_row_bytes,
+                                   size_t src_off, uint64_t key, cudaStream_t st);
+cudaError_t launch_synth_scales_cols(uint16_t *dst, int rows, int nblk_dst, int nblk_src, int blk_off,
+                                    int exp_field, uint64_t key, cudaStream_t st);
 cudaError_t launch_synth_norm(float *dst, int n, uint64_t key, cudaStream_t st);
 
 // ---- the decode step as one persistent kernel (spb_decode.cu) ----

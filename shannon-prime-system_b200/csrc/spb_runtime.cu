@@ -11,6 +11,7 @@
 // This mirrors kv_step_gemma3 (sp_session.c:380-464) and kv_step (sp_session.c:274-363).
 #include "../../include/spb200.h"
 #include "spb_kernels.cuh"
+#include "spb_tp.cuh"
 
 #include <cuda_runtime.h>
 
@@ -177,6 +178,11 @@ struct spb_model {
   float es = 1.0f;
   int64_t stream_bytes = 0;
   DecLayer *dec_layers = nullptr;   // device [NL]: the persistent decode kernel's view of the layers
+  // tensor parallel: this rank's shard (NH, NKV, FF local; V = its LM-head rows [vbase, vbase+V)
+  // of Vfull); without a group Vfull == V and vbase == 0
+  spb_tp *tp = nullptr;
+  int Vfull = 0, vbase = 0;
+  bool out_sep = false;   // the LM head has its own storage (untied, or a vocabulary slice)
 };
 
 static int mark_small_scales(spb_model *m);
@@ -197,7 +203,9 @@ static int check_cfg(const spb_config &c) {
   return SPB_OK;
 }
 
-static int model_alloc(const spb_config &c, int device, spb_model **out) {
+// nv_out > 0: a vocabulary slice of nv_out LM-head rows (tensor parallel), stored apart from
+// the whole embedding table
+static int model_alloc(const spb_config &c, int device, spb_model **out, int nv_out = 0) {
   int rc = check_cfg(c);
   if (rc) return rc;
   CU(cudaSetDevice(device));
@@ -205,8 +213,11 @@ static int model_alloc(const spb_config &c, int device, spb_model **out) {
   m->device = device;
   m->cfg = c;
   m->E = c.n_embd; m->FF = c.n_ff; m->NH = c.n_head; m->NKV = c.n_head_kv; m->HD = c.head_dim;
-  m->QD = c.n_head * c.head_dim; m->KVD = c.n_head_kv * c.head_dim; m->V = c.n_vocab; m->NL = c.n_layers;
+  m->QD = c.n_head * c.head_dim; m->KVD = c.n_head_kv * c.head_dim; m->NL = c.n_layers;
+  m->Vfull = c.n_vocab;
+  m->V = nv_out > 0 ? nv_out : c.n_vocab;
   m->gemma = c.arch == SPB_ARCH_GEMMA3;
+  m->out_sep = !m->gemma || nv_out > 0;
   m->es = sqrtf((float)m->E);
   // layout: per layer qkv, o, gate, up, down, then norms; embedding; LM head (if untied)
   size_t off = 0;
@@ -224,8 +235,8 @@ static int model_alloc(const spb_config &c, int device, spb_model **out) {
     o.d_c = take((size_t)m->E * m->FF / 2); o.d_s = take((size_t)m->E * (m->FF / 32) * 2);
     o.norms = take((size_t)nnorm * 4);
   }
-  const size_t emb_c = take((size_t)m->V * m->E / 2), emb_s = take((size_t)m->V * (m->E / 32) * 2);
-  const bool untied = !m->gemma;
+  const size_t emb_c = take((size_t)m->Vfull * m->E / 2), emb_s = take((size_t)m->Vfull * (m->E / 32) * 2);
+  const bool untied = m->out_sep;
   size_t out_c = 0, out_s = 0;
   if (untied) { out_c = take((size_t)m->V * m->E / 2); out_s = take((size_t)m->V * (m->E / 32) * 2); }
   const size_t onorm = take((size_t)m->E * 4);
@@ -254,7 +265,7 @@ static int model_alloc(const spb_config &c, int device, spb_model **out) {
     d.global = !m->gemma || (L % period) == period - 1;
     d.win = (m->gemma && !d.global && c.sliding_window > 0) ? c.sliding_window : -1;
   }
-  m->embd = {B + emb_c, (const uint16_t *)(B + emb_s), m->V, m->E};
+  m->embd = {B + emb_c, (const uint16_t *)(B + emb_s), m->Vfull, m->E};
   m->out = untied ? DevQ4B{B + out_c, (const uint16_t *)(B + out_s), m->V, m->E} : m->embd;
   m->out_norm = (const float *)(B + onorm);
   m->tabs = (uint64_t *)(B + tabs);
@@ -306,17 +317,26 @@ static bool q4b_bound_ok(const spb_q4b &w) {
   return true;
 }
 
-static int put_q4b(const spb_q4b &w, int rows, int cols, const DevQ4B &dst, int row0, const char *what) {
+// rows [r0, r0 + nr) x columns [c0, c0 + nc) of a host matrix of rows x cols into rows
+// [row0, row0 + nr) of dst (nc columns wide); c0 and nc are multiples of 32
+static int put_q4b_part(const spb_q4b &w, int rows, int cols, int r0, int nr, int c0, int nc, const DevQ4B &dst,
+                        int row0, const char *what) {
   if (!w.codes || !w.bscale || w.rows != rows || w.cols != cols)
     return set_err(SPB_EBADARG, "spb_model_upload: %s shape [%d x %d], expected [%d x %d]", what, w.rows, w.cols,
                    rows, cols);
   if (!q4b_bound_ok(w))
     return set_err(SPB_ERANGE, "spb_model_upload: %s block scales exceed the exact int64 accumulation bound", what);
-  CU(cudaMemcpy((void *)(dst.codes + (size_t)row0 * (cols / 2)), w.codes, (size_t)rows * (cols / 2),
-                cudaMemcpyHostToDevice));
-  CU(cudaMemcpy((void *)(dst.scales + (size_t)row0 * (cols / 32)), w.bscale, (size_t)rows * (cols / 32) * 2,
-                cudaMemcpyHostToDevice));
+  CU(cudaMemcpy2D((void *)(dst.codes + (size_t)row0 * (nc / 2)), (size_t)nc / 2,
+                  w.codes + (size_t)r0 * (cols / 2) + c0 / 2, (size_t)cols / 2, (size_t)nc / 2, nr,
+                  cudaMemcpyHostToDevice));
+  CU(cudaMemcpy2D((void *)(dst.scales + (size_t)row0 * (nc / 32)), (size_t)nc / 32 * 2,
+                  w.bscale + (size_t)r0 * (cols / 32) + c0 / 32, (size_t)cols / 32 * 2, (size_t)nc / 32 * 2, nr,
+                  cudaMemcpyHostToDevice));
   return SPB_OK;
+}
+
+static int put_q4b(const spb_q4b &w, int rows, int cols, const DevQ4B &dst, int row0, const char *what) {
+  return put_q4b_part(w, rows, cols, 0, rows, 0, cols, dst, row0, what);
 }
 
 static int put_f32(const float *src, const float *dst, int n, const char *what) {
@@ -325,27 +345,27 @@ static int put_f32(const float *src, const float *dst, int n, const char *what) 
   return SPB_OK;
 }
 
-extern "C" int spb_model_upload(const spb_model_desc *desc, int device, spb_model **out) {
-  if (!desc || !out || !desc->layers) return set_err(SPB_EBADARG, "spb_model_upload: null arg");
-  *out = nullptr;
-  spb_model *m = nullptr;
-  int rc = model_alloc(desc->cfg, device, &m);
-  if (rc) return rc;
-#define PUT(x)                        \
-  do {                                \
-    rc = (x);                         \
-    if (rc) { spb_model_free(m); return rc; } \
+// Copy a whole host model, or with sh (spb_tp_shard's ranges) the rank's slices of it, into m.
+static int upload_fill(spb_model *m, const spb_model_desc *desc, const int32_t *sh) {
+  const spb_config &full = desc->cfg;
+  const int E = m->E, HD = m->HD, QDf = full.n_head * HD, KVDf = full.n_head_kv * HD, FFf = full.n_ff;
+  const int q0 = sh ? sh[0] * HD : 0, kv0 = sh ? sh[2] * HD : 0, f0 = sh ? sh[4] : 0, v0 = sh ? sh[6] : 0;
+  int rc = SPB_OK;
+#define PUT(x)          \
+  do {                  \
+    rc = (x);           \
+    if (rc) return rc;  \
   } while (0)
   for (int L = 0; L < m->NL; L++) {
     const spb_layer_desc &s = desc->layers[L];
     DevLayer &d = m->layers[L];
-    PUT(put_q4b(s.wq, m->QD, m->E, d.qkv, 0, "attn_q"));
-    PUT(put_q4b(s.wk, m->KVD, m->E, d.qkv, m->QD, "attn_k"));
-    PUT(put_q4b(s.wv, m->KVD, m->E, d.qkv, m->QD + m->KVD, "attn_v"));
-    PUT(put_q4b(s.wo, m->E, m->QD, d.o, 0, "attn_output"));
-    PUT(put_q4b(s.wg, m->FF, m->E, d.g, 0, "ffn_gate"));
-    PUT(put_q4b(s.wu, m->FF, m->E, d.u, 0, "ffn_up"));
-    PUT(put_q4b(s.wd, m->E, m->FF, d.d, 0, "ffn_down"));
+    PUT(put_q4b_part(s.wq, QDf, E, q0, m->QD, 0, E, d.qkv, 0, "attn_q"));
+    PUT(put_q4b_part(s.wk, KVDf, E, kv0, m->KVD, 0, E, d.qkv, m->QD, "attn_k"));
+    PUT(put_q4b_part(s.wv, KVDf, E, kv0, m->KVD, 0, E, d.qkv, m->QD + m->KVD, "attn_v"));
+    PUT(put_q4b_part(s.wo, E, QDf, 0, E, q0, m->QD, d.o, 0, "attn_output"));
+    PUT(put_q4b_part(s.wg, FFf, E, f0, m->FF, 0, E, d.g, 0, "ffn_gate"));
+    PUT(put_q4b_part(s.wu, FFf, E, f0, m->FF, 0, E, d.u, 0, "ffn_up"));
+    PUT(put_q4b_part(s.wd, E, FFf, 0, E, f0, m->FF, d.d, 0, "ffn_down"));
     PUT(put_f32(s.attn_norm, d.attn_norm, m->E, "attn_norm"));
     PUT(put_f32(s.ffn_norm, d.ffn_norm, m->E, "ffn_norm"));
     if (m->gemma) {
@@ -357,11 +377,48 @@ extern "C" int spb_model_upload(const spb_model_desc *desc, int device, spb_mode
       PUT(put_f32(s.k_norm, d.k_norm, m->HD, "attn_k_norm"));
     }
   }
-  PUT(put_q4b(desc->token_embd, m->V, m->E, m->embd, 0, "token_embd"));
-  if (!m->gemma) PUT(put_q4b(desc->output, m->V, m->E, m->out, 0, "output"));
+  PUT(put_q4b(desc->token_embd, m->Vfull, m->E, m->embd, 0, "token_embd"));
+  if (m->out_sep)
+    PUT(put_q4b_part(m->gemma ? desc->token_embd : desc->output, m->Vfull, E, v0, m->V, 0, E, m->out, 0, "output"));
   PUT(put_f32(desc->output_norm, m->out_norm, m->E, "output_norm"));
   PUT(mark_small_scales(m));
 #undef PUT
+  return SPB_OK;
+}
+
+extern "C" int spb_model_upload(const spb_model_desc *desc, int device, spb_model **out) {
+  if (!desc || !out || !desc->layers) return set_err(SPB_EBADARG, "spb_model_upload: null arg");
+  *out = nullptr;
+  spb_model *m = nullptr;
+  int rc = model_alloc(desc->cfg, device, &m);
+  if (!rc) rc = upload_fill(m, desc, nullptr);
+  if (rc) { spb_model_free(m); return rc; }
+  *out = m;
+  return SPB_OK;
+}
+
+// the rank's local geometry: its heads and FFN columns, the whole vocabulary for the embedding
+static spb_config local_cfg(const spb_config &full, const int32_t sh[8]) {
+  spb_config c = full;
+  c.n_head = sh[1];
+  c.n_head_kv = sh[3];
+  c.n_ff = sh[5];
+  return c;
+}
+
+extern "C" int spb_model_upload_tp(const spb_model_desc *desc, spb_tp *tp, spb_model **out) {
+  if (!desc || !out || !desc->layers || !tp) return set_err(SPB_EBADARG, "spb_model_upload_tp: null arg");
+  *out = nullptr;
+  int32_t sh[8];
+  int rc = spb_tp_shard(&desc->cfg, spb_tp_rank(tp), spb_tp_world(tp), sh);
+  if (rc) return rc;
+  spb_model *m = nullptr;
+  rc = model_alloc(local_cfg(desc->cfg, sh), tp_device(tp), &m, sh[7]);
+  if (rc) return rc;
+  m->tp = tp;
+  m->vbase = sh[6];
+  rc = upload_fill(m, desc, sh);
+  if (rc) { spb_model_free(m); return rc; }
   *out = m;
   return SPB_OK;
 }
@@ -374,7 +431,7 @@ static int mark_small_scales(spb_model *m) {
     ws.push_back(&d.qkv); ws.push_back(&d.o); ws.push_back(&d.g); ws.push_back(&d.u); ws.push_back(&d.d);
   }
   ws.push_back(&m->embd);
-  if (!m->gemma) ws.push_back(&m->out);
+  if (m->out_sep) ws.push_back(&m->out);
   int *dev = nullptr;
   CU(cudaMalloc(&dev, ws.size() * sizeof(int)));
   cudaError_t e = cudaMemset(dev, 0, ws.size() * sizeof(int));
@@ -385,7 +442,7 @@ static int mark_small_scales(spb_model *m) {
   cudaFree(dev);
   if (e != cudaSuccess) return set_err(SPB_ECUDA, "spb_model: scale check: %s", cudaGetErrorString(e));
   for (size_t i = 0; i < ws.size(); i++) ws[i]->small = emax[i] <= 21 ? 1 : 0;
-  if (m->gemma) m->out = m->embd;
+  if (!m->out_sep) m->out = m->embd;
   return SPB_OK;
 }
 
@@ -399,32 +456,45 @@ static uint64_t splitmix64_h(uint64_t z) {
 static uint64_t stream_key(uint64_t seed, uint64_t stream) { return splitmix64_h(seed * 0x10001ull + stream); }
 static int scale_exp_field(int cols) { return (int)std::floor(std::log2(1.0 / (8.0 * std::sqrt((double)cols)))) + 15; }
 
-static int synth_matrix(const DevQ4B &d, int row0, int rows, int cols, int tid, uint64_t seed) {
+// rows [src_row0, src_row0 + rows) of generator stream `tid` (a cols-wide matrix) into rows
+// [row0, row0 + rows) of d: the generators count words (codes) and blocks (scales) from the
+// matrix start, so a row offset is a key offset
+static int synth_matrix(const DevQ4B &d, int row0, int rows, int cols, int tid, uint64_t seed, int src_row0 = 0) {
   CU(launch_synth_codes((uint8_t *)d.codes + (size_t)row0 * (cols / 2), (size_t)rows * (cols / 2),
-                        stream_key(seed, 2ull * tid), 0));
+                        stream_key(seed, 2ull * tid) + (uint64_t)src_row0 * (cols / 16), 0));
   CU(launch_synth_scales((uint16_t *)d.scales + (size_t)row0 * (cols / 32), rows, cols / 32, cols / 32,
-                         scale_exp_field(cols), stream_key(seed, 2ull * tid + 1), 0));
+                         scale_exp_field(cols), stream_key(seed, 2ull * tid + 1) + (uint64_t)src_row0 * (cols / 32),
+                         0));
   return SPB_OK;
 }
 
-extern "C" int spb_model_synthetic(const spb_config *cfg, uint64_t seed, int device, spb_model **out) {
-  if (!cfg || !out) return set_err(SPB_EBADARG, "spb_model_synthetic: null arg");
-  *out = nullptr;
-  spb_model *m = nullptr;
-  int rc = model_alloc(*cfg, device, &m);
-  if (rc) return rc;
+// columns [c0, c0 + d.cols) of generator stream `tid` (a rows x cols_full matrix) into d
+static int synth_matrix_cols(const DevQ4B &d, int cols_full, int c0, int tid, uint64_t seed) {
+  CU(launch_synth_codes_cols((uint8_t *)d.codes, d.rows, (size_t)d.cols / 2, (size_t)cols_full / 2, (size_t)c0 / 2,
+                             stream_key(seed, 2ull * tid), 0));
+  CU(launch_synth_scales_cols((uint16_t *)d.scales, d.rows, d.cols / 32, cols_full / 32, c0 / 32,
+                              scale_exp_field(cols_full), stream_key(seed, 2ull * tid + 1), 0));
+  return SPB_OK;
+}
+
+// Generate the whole model, or with sh (spb_tp_shard's ranges) the rank's slices of the model
+// `full` describes, into m.
+static int synth_fill(spb_model *m, const spb_config &full, uint64_t seed, const int32_t *sh) {
+  const int HD = m->HD, QDf = full.n_head * HD, FFf = full.n_ff;
+  const int q0 = sh ? sh[0] * HD : 0, kv0 = sh ? sh[2] * HD : 0, f0 = sh ? sh[4] : 0, v0 = sh ? sh[6] : 0;
+  int rc = SPB_OK;
   // stream ids: globals 1..3, layer L field f -> 64 + 64 L + f (spmodel.LAYER_FIELDS order)
   enum { F_ATTN_NORM, F_Q, F_K, F_V, F_O, F_QN, F_KN, F_POST_ATTN, F_FFN_NORM, F_GATE, F_UP, F_DOWN, F_POST_FFW };
   auto lid = [](int L, int f) { return 64 + 64 * L + f; };
   for (int L = 0; L < m->NL && !rc; L++) {
     DevLayer &d = m->layers[L];
-    rc = synth_matrix(d.qkv, 0, m->QD, m->E, lid(L, F_Q), seed);
-    if (!rc) rc = synth_matrix(d.qkv, m->QD, m->KVD, m->E, lid(L, F_K), seed);
-    if (!rc) rc = synth_matrix(d.qkv, m->QD + m->KVD, m->KVD, m->E, lid(L, F_V), seed);
-    if (!rc) rc = synth_matrix(d.o, 0, m->E, m->QD, lid(L, F_O), seed);
-    if (!rc) rc = synth_matrix(d.g, 0, m->FF, m->E, lid(L, F_GATE), seed);
-    if (!rc) rc = synth_matrix(d.u, 0, m->FF, m->E, lid(L, F_UP), seed);
-    if (!rc) rc = synth_matrix(d.d, 0, m->E, m->FF, lid(L, F_DOWN), seed);
+    rc = synth_matrix(d.qkv, 0, m->QD, m->E, lid(L, F_Q), seed, q0);
+    if (!rc) rc = synth_matrix(d.qkv, m->QD, m->KVD, m->E, lid(L, F_K), seed, kv0);
+    if (!rc) rc = synth_matrix(d.qkv, m->QD + m->KVD, m->KVD, m->E, lid(L, F_V), seed, kv0);
+    if (!rc) rc = synth_matrix_cols(d.o, QDf, q0, lid(L, F_O), seed);
+    if (!rc) rc = synth_matrix(d.g, 0, m->FF, m->E, lid(L, F_GATE), seed, f0);
+    if (!rc) rc = synth_matrix(d.u, 0, m->FF, m->E, lid(L, F_UP), seed, f0);
+    if (!rc) rc = synth_matrix_cols(d.d, FFf, f0, lid(L, F_DOWN), seed);
     struct { const float *p; int n, f; } norms[] = {
         {d.attn_norm, m->E, F_ATTN_NORM}, {d.ffn_norm, m->E, F_FFN_NORM}, {d.post_attn, m->E, F_POST_ATTN},
         {d.post_ffw, m->E, F_POST_FFW}, {d.q_norm, m->HD, F_QN}, {d.k_norm, m->HD, F_KN}};
@@ -434,14 +504,40 @@ extern "C" int spb_model_synthetic(const spb_config *cfg, uint64_t seed, int dev
         if (e != cudaSuccess) rc = set_err(SPB_ECUDA, "synth norm: %s", cudaGetErrorString(e));
       }
   }
-  if (!rc) rc = synth_matrix(m->embd, 0, m->V, m->E, 1, seed);
-  if (!rc && !m->gemma) rc = synth_matrix(m->out, 0, m->V, m->E, 2, seed);
+  if (!rc) rc = synth_matrix(m->embd, 0, m->Vfull, m->E, 1, seed);
+  if (!rc && m->out_sep) rc = synth_matrix(m->out, 0, m->V, m->E, m->gemma ? 1 : 2, seed, v0);
   if (!rc) {
     cudaError_t e = launch_synth_norm((float *)m->out_norm, m->E, stream_key(seed, 2ull * 3), 0);
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
     if (e != cudaSuccess) rc = set_err(SPB_ECUDA, "synth: %s", cudaGetErrorString(e));
   }
   if (!rc) rc = mark_small_scales(m);
+  return rc;
+}
+
+extern "C" int spb_model_synthetic(const spb_config *cfg, uint64_t seed, int device, spb_model **out) {
+  if (!cfg || !out) return set_err(SPB_EBADARG, "spb_model_synthetic: null arg");
+  *out = nullptr;
+  spb_model *m = nullptr;
+  int rc = model_alloc(*cfg, device, &m);
+  if (!rc) rc = synth_fill(m, *cfg, seed, nullptr);
+  if (rc) { spb_model_free(m); return rc; }
+  *out = m;
+  return SPB_OK;
+}
+
+extern "C" int spb_model_synthetic_tp(const spb_config *cfg, uint64_t seed, spb_tp *tp, spb_model **out) {
+  if (!cfg || !out || !tp) return set_err(SPB_EBADARG, "spb_model_synthetic_tp: null arg");
+  *out = nullptr;
+  int32_t sh[8];
+  int rc = spb_tp_shard(cfg, spb_tp_rank(tp), spb_tp_world(tp), sh);
+  if (rc) return rc;
+  spb_model *m = nullptr;
+  rc = model_alloc(local_cfg(*cfg, sh), tp_device(tp), &m, sh[7]);
+  if (rc) return rc;
+  m->tp = tp;
+  m->vbase = sh[6];
+  rc = synth_fill(m, *cfg, seed, sh);
   if (rc) { spb_model_free(m); return rc; }
   *out = m;
   return SPB_OK;
@@ -482,6 +578,10 @@ struct spb_session {
   int dgrid = 0;                  // CTAs of the persistent decode kernel (0: not available)
   DecodeArgs dargs{};             // its arguments (fixed for the session's lifetime)
   unsigned long long *trace_dev = nullptr;   // phase trace of the persistent kernel (on request)
+  // tensor parallel: int64 partial sums of the K-split matrices [NT_MAX][E], this rank's LM-head
+  // logits [NT_MAX][V] and the all-gathered slices [world][NT_MAX][V]
+  int64_t *y64 = nullptr;
+  float *logits_l = nullptr, *logits_g = nullptr;
 };
 
 // 1: decode steps run as the persistent kernel where it covers the shape; 0 (default, the
@@ -496,7 +596,7 @@ extern "C" int spb_decode_mode(int mode) {
 
 // the persistent kernel can serve a step whose new token lands at position `pos`
 static bool decode_kernel_covers(const spb_session *s, int pos) {
-  return s->dgrid > 0 && decode_unsupported(s->dargs, s->dgrid, pos + 1) == nullptr;
+  return s->dgrid > 0 && !s->m->tp && decode_unsupported(s->dargs, s->dgrid, pos + 1) == nullptr;
 }
 // ... and is selected for it
 static bool use_decode_kernel(const spb_session *s, int pos) { return g_decode_mode == 1 && decode_kernel_covers(s, pos); }
@@ -519,7 +619,10 @@ extern "C" int spb_session_open(spb_model *m, int pmax, spb_session **out) {
   const size_t o_x = take((size_t)NT_MAX * E * 4), o_qkv = take((size_t)NT_MAX * QKV * 4);
   const size_t o_ao = take((size_t)NT_MAX * m->QD * 4), o_ap = take((size_t)NT_MAX * E * 4);
   const size_t o_gg = take((size_t)NT_MAX * m->FF * 4), o_dn = take((size_t)NT_MAX * E * 4);
-  const size_t o_lg = take((size_t)NT_MAX * m->V * 4), o_qi = take((size_t)NT_MAX * m->QD * 4);
+  const size_t o_lg = take((size_t)NT_MAX * m->Vfull * 4), o_qi = take((size_t)NT_MAX * m->QD * 4);
+  const size_t o_y64 = m->tp ? take((size_t)NT_MAX * E * 8) : 0;
+  const size_t o_lgl = m->tp ? take((size_t)NT_MAX * m->V * 4) : 0;
+  const size_t o_lgg = m->tp ? take((size_t)NT_MAX * m->Vfull * 4) : 0;
   const size_t o_aq = take((size_t)NT_MAX * maxK), o_ab = take((size_t)NT_MAX * (maxK / 32) * 4);
   const size_t o_as = take(NT_MAX * 4), o_pos = take(4), o_tok = take(NT_MAX * 4), o_am = take(NT_MAX * 4);
   const size_t o_hist = take((size_t)pmax * 4), o_err = take(4), o_slots = take(2 * NT_MAX * 4);
@@ -545,6 +648,11 @@ extern "C" int spb_session_open(spb_model *m, int pmax, spb_session **out) {
   s->ao_max = (uint32_t *)(B + o_slots); s->gg_max = s->ao_max + NT_MAX;
   s->amax_keys = (unsigned long long *)(B + o_keys);
   s->rows_dev = (BatchRow *)(B + o_rows);
+  if (m->tp) {
+    s->y64 = (int64_t *)(B + o_y64);
+    s->logits_l = (float *)(B + o_lgl);
+    s->logits_g = (float *)(B + o_lgg);
+  }
   {
     DecodeArgs &a = s->dargs;
     a.layers = m->dec_layers; a.embd = m->embd; a.out = m->out; a.out_norm = m->out_norm;
@@ -602,7 +710,16 @@ static cudaError_t enqueue_rows(spb_session *s, int nt, bool want_logits, const 
     e = (x);                        \
     if (e != cudaSuccess) return e; \
   } while (0)
-  K(launch_embed(m->embd, s->tok_dev, nt, m->es, m->gemma ? 1 : 0, s->x, m->V, s->err_dev, st));
+  K(launch_embed(m->embd, s->tok_dev, nt, m->es, m->gemma ? 1 : 0, s->x, m->Vfull, s->err_dev, st));
+  // a K-split matrix (tensor parallel): exact int64 partial sums, summed over the group, then
+  // scaled with the GEMV's own rounding
+  auto split_gemv = [&](const DevQ4B &w, float *y) -> cudaError_t {
+    if (!m->tp) return launch_gemv(w, nullptr, s->act, nt, y, E, EPI_STORE, s->err_dev, st);
+    cudaError_t r = launch_gemv(w, nullptr, s->act, nt, reinterpret_cast<float *>(s->y64), E, EPI_I64, s->err_dev, st);
+    if (r == cudaSuccess) r = tp_sum_i64(m->tp, s->y64, (size_t)nt * E, st, s->err_dev);
+    if (r == cudaSuccess) r = launch_scale_i64(s->y64, s->act.scale, nt, E, y, E, st);
+    return r;
+  };
   const size_t kvl = kv_layer_elems(m, s->pmax);
   for (int L = 0; L < m->NL; L++) {
     const DevLayer &d = m->layers[L];
@@ -628,20 +745,35 @@ static cudaError_t enqueue_rows(spb_session *s, int nt, bool want_logits, const 
     aa.NH = m->NH; aa.NKV = m->NKV; aa.HD = m->HD; aa.P = rows ? Pmax : s->pmax; aa.win = d.win; aa.ntok = nt;
     aa.ascale = ascale; aa.err = s->err_dev; aa.ao_max = s->ao_max;
     K(launch_attn(aa, st));
+    if (m->tp) K(tp_max_u32(m->tp, s->ao_max, nt, st, s->err_dev));   // the quantizer's max over all heads
     K(launch_quant(s->ao, m->QD, m->QD, nt, s->act, s->ao_max, s->err_dev, st));
-    K(launch_gemv(d.o, nullptr, s->act, nt, s->ap, E, EPI_STORE, s->err_dev, st));
+    K(split_gemv(d.o, s->ap));
     K(launch_norm(s->x, s->ap, m->gemma ? d.post_attn : nullptr, d.ffn_norm, E, nt, s->act, nullptr, s->err_dev, st,
                   s->gg_max));
     K(launch_gemv(d.g, &d.u, s->act, nt, s->gg, m->FF, m->gemma ? EPI_GELU_MUL : EPI_SILU_MUL, s->err_dev, st, 0,
                   s->gg_max));
+    if (m->tp) K(tp_max_u32(m->tp, s->gg_max, nt, st, s->err_dev));   // ... over all FFN columns
     K(launch_quant(s->gg, m->FF, m->FF, nt, s->act, s->gg_max, s->err_dev, st));
-    K(launch_gemv(d.d, nullptr, s->act, nt, s->dn, E, EPI_STORE, s->err_dev, st));
+    K(split_gemv(d.d, s->dn));
   }
   if (want_logits) {
     const DevLayer &p = m->layers[m->NL - 1];
     K(launch_norm(s->x, s->dn, m->gemma ? p.post_ffw : nullptr, m->out_norm, E, nt, s->act, nullptr, s->err_dev, st));
-    K(launch_gemv(m->out, nullptr, s->act, nt, s->logits, m->V, EPI_STORE, s->err_dev, st, 0, nullptr,
-                  s->amax_keys));
+    if (!m->tp) {
+      K(launch_gemv(m->out, nullptr, s->act, nt, s->logits, m->V, EPI_STORE, s->err_dev, st, 0, nullptr,
+                    s->amax_keys));
+    } else {   // vocabulary rows [vbase, vbase + V): global argmax keys, then every rank's slice
+      K(launch_gemv(m->out, nullptr, s->act, nt, s->logits_l, m->V, EPI_STORE, s->err_dev, st, 0, nullptr,
+                    s->amax_keys));
+      K(launch_keys_rebase(s->amax_keys, nt, m->vbase, st));
+      K(tp_max_u64(m->tp, s->amax_keys, nt, st, s->err_dev));
+      K(tp_gather_f32(m->tp, s->logits_l, s->logits_g, (size_t)nt * m->V, st));
+      const int world = spb_tp_world(m->tp);
+      for (int r = 0; r < world; r++)   // [rank][t][V] -> [t][rank * V + j]
+        K(cudaMemcpy2DAsync(s->logits + (size_t)r * m->V, (size_t)m->Vfull * 4,
+                            s->logits_g + (size_t)r * nt * m->V, (size_t)m->V * 4, (size_t)m->V * 4, nt,
+                            cudaMemcpyDeviceToDevice, st));
+    }
     K(launch_argmax_take(s->amax_keys, nt, s->argmax_dev, st));
   }
 #undef K
@@ -679,7 +811,7 @@ extern "C" int spb_session_prefill(spb_session *s, const int32_t *tokens, int n_
     CU(enqueue_rows(s, nt, logits != nullptr));
     CU(launch_advance(s->pos_dev, nt, nullptr, nullptr, s->st));
     if (logits)
-      CU(cudaMemcpyAsync(logits + (size_t)done * s->m->V, s->logits, (size_t)nt * s->m->V * 4,
+      CU(cudaMemcpyAsync(logits + (size_t)done * s->m->Vfull, s->logits, (size_t)nt * s->m->Vfull * 4,
                          cudaMemcpyDeviceToHost, s->st));
     // the pinned token staging is reused next chunk: wait for the H2D copy
     CU(cudaStreamSynchronize(s->st));
@@ -728,7 +860,7 @@ extern "C" int spb_session_decode_step_argmax(spb_session *s, int32_t token, flo
   } else if (!persistent) {
     CU(cudaGraphLaunch(s->step_graph, s->st));
   }
-  if (logits) CU(cudaMemcpyAsync(logits, s->logits, (size_t)s->m->V * 4, cudaMemcpyDeviceToHost, s->st));
+  if (logits) CU(cudaMemcpyAsync(logits, s->logits, (size_t)s->m->Vfull * 4, cudaMemcpyDeviceToHost, s->st));
   if (argmax) CU(cudaMemcpyAsync(s->h_pinned + NT_MAX + 1, s->argmax_dev, 4, cudaMemcpyDeviceToHost, s->st));
   rc = collect_errors(s);
   if (rc) { sync_pos(s); cudaStreamSynchronize(s->st); return rc; }
@@ -794,7 +926,7 @@ extern "C" int spb_batch_decode_step(spb_session *const *ss, int B, const int32_
   CU(cudaMemcpyAsync(lead->rows_dev, lead->h_rows, (size_t)B * sizeof(BatchRow), cudaMemcpyHostToDevice, lead->st));
   CU(enqueue_rows(lead, B, true, lead->rows_dev, Pmax));
   if (logits)
-    CU(cudaMemcpyAsync(logits, lead->logits, (size_t)B * lead->m->V * 4, cudaMemcpyDeviceToHost, lead->st));
+    CU(cudaMemcpyAsync(logits, lead->logits, (size_t)B * lead->m->Vfull * 4, cudaMemcpyDeviceToHost, lead->st));
   CU(cudaMemcpyAsync(lead->h_argmax, lead->argmax_dev, (size_t)B * 4, cudaMemcpyDeviceToHost, lead->st));
   int rc = collect_errors(lead);
   if (rc) return rc;   // no position moved

@@ -30,6 +30,8 @@ CORE_SYMBOLS = [
     "spb_silu_exact_dev", "spb_rope_cordic_dev", "spb_take_device_errors", "spb_rope_freq_table",
     "spb_cordic_tables", "spb_graph_begin", "spb_graph_end", "spb_graph_launch", "spb_graph_free",
     "spb_decode_mode", "spb_session_decode_trace", "spb_batch_decode_step",
+    "spb_tp_shard", "spb_tp_unique_id", "spb_tp_open", "spb_tp_close", "spb_tp_rank", "spb_tp_world",
+    "spb_model_synthetic_tp", "spb_model_upload_tp", "spb_tp_p2p_init", "spb_tp_p2p_connect",
 ]
 L1_SYMBOLS = ["spb_l1_forward", "spb_l1_backend", "spb_l1_kvdecode_table", "spb_l1_kvdecode_clone",
               "spb_l1_set_device", "spb_l1_release_model"]
@@ -146,6 +148,13 @@ def load(path: str = CORE_SO):
         "spb_cordic_tables": ([vp, vp], None),
         "spb_graph_begin": ([vp], C.c_int), "spb_graph_end": ([vp, C.POINTER(vp)], C.c_int),
         "spb_graph_launch": ([vp, vp], C.c_int), "spb_graph_free": ([vp], None),
+        "spb_tp_shard": ([vp, C.c_int, C.c_int, vp], C.c_int),
+        "spb_tp_unique_id": ([vp], C.c_int),
+        "spb_tp_open": ([vp, C.c_int, C.c_int, C.c_int, C.POINTER(vp)], C.c_int),
+        "spb_tp_close": ([vp], None), "spb_tp_rank": ([vp], C.c_int), "spb_tp_world": ([vp], C.c_int),
+        "spb_model_synthetic_tp": ([vp, C.c_uint64, vp, C.POINTER(vp)], C.c_int),
+        "spb_model_upload_tp": ([vp, vp, C.POINTER(vp)], C.c_int),
+        "spb_tp_p2p_init": ([vp, C.c_int, vp], C.c_int), "spb_tp_p2p_connect": ([vp, vp], C.c_int),
     }
     for name, (args, res) in sig.items():
         f = getattr(L, name)
@@ -174,9 +183,81 @@ def cordic_tables():
     return T, g.value
 
 
+TP_ID_BYTES = 128
+TP_P2P_BLOB_BYTES = 80
+
+
+def tp_shard(cfg, rank, world):
+    """(h0, nh, kv0, nkv, f0, nff, v0, nv): rank's query heads, KV heads, FFN columns and
+    LM-head rows (host only)."""
+    c = config_struct(cfg)
+    out = np.zeros(8, np.int32)
+    check(load().spb_tp_shard(C.byref(c), rank, world, out.ctypes.data))
+    return tuple(int(v) for v in out)
+
+
+def tp_unique_id():
+    b = (C.c_uint8 * TP_ID_BYTES)()
+    check(load().spb_tp_unique_id(b))
+    return bytes(b)
+
+
+def tp_uid_from_dist(group=None):
+    """The group's unique id on every rank of the current torch.distributed group: rank 0 makes
+    it, a broadcast shares it (any backend; host only)."""
+    import torch.distributed as dist
+    obj = [tp_unique_id() if dist.get_rank(group) == 0 else None]
+    dist.broadcast_object_list(obj, src=0, group=group)
+    return obj[0]
+
+
+class TensorParallel:
+    """One rank of a tensor-parallel group (one process per GPU); every rank opens it with the
+    same unique id (from tp_unique_id on one rank, shared by the caller)."""
+
+    def __init__(self, uid: bytes, rank, world, device):
+        if len(uid) != TP_ID_BYTES:
+            raise ValueError("unique id must be 128 bytes")
+        b = (C.c_uint8 * TP_ID_BYTES).from_buffer_copy(uid)
+        self.h = C.c_void_p()
+        check(load().spb_tp_open(b, rank, world, device, C.byref(self.h)))
+        self.rank, self.world, self.device = rank, world, device
+
+    def enable_p2p(self, cap, group=None):
+        """Collective: exchanges of at most `cap` values (the decode step's) run over peer
+        memory instead of NCCL; the mailbox handles travel over the torch.distributed group."""
+        import torch.distributed as dist
+        blob = (C.c_uint8 * TP_P2P_BLOB_BYTES)()
+        check(load().spb_tp_p2p_init(self.h, cap, blob))
+        blobs = [None] * self.world
+        dist.all_gather_object(blobs, bytes(blob), group=group)
+        allb = (C.c_uint8 * (TP_P2P_BLOB_BYTES * self.world)).from_buffer_copy(b"".join(blobs))
+        check(load().spb_tp_p2p_connect(self.h, allb))
+
+    def close(self):
+        if self.h:
+            load().spb_tp_close(self.h)
+            self.h = None
+
+
 class Model:
     def __init__(self, handle, cfg):
         self.h, self.cfg = handle, cfg
+
+    @classmethod
+    def upload_tp(cls, cfg, T, tp):
+        """This rank's shard of a whole host model (logits and argmax stay full-vocabulary)."""
+        d = model_desc(cfg, T)
+        h = C.c_void_p()
+        check(load().spb_model_upload_tp(C.byref(d), tp.h, C.byref(h)))
+        return cls(h, cfg)
+
+    @classmethod
+    def synthetic_tp(cls, cfg, tp, seed=0):
+        c = config_struct(cfg)
+        h = C.c_void_p()
+        check(load().spb_model_synthetic_tp(C.byref(c), seed, tp.h, C.byref(h)))
+        return cls(h, cfg)
 
     @classmethod
     def upload(cls, cfg, T, device=0):
