@@ -413,7 +413,7 @@ __device__ __forceinline__ int32_t scale_word(uint32_t h) {
 template <int MT, int TH, int EPI, bool SMALL>
 __global__ void __launch_bounds__(GEMM_THREADS * TH, 2)
 k_gemm(DevQ4B w, DevQ4B w2, DevAct act, int ntok, float *__restrict__ y, int ldy, uint32_t *err, uint32_t *ymax,
-       unsigned long long *amax) {
+       unsigned long long *amax, int ks) {
   constexpr int NM = epi_pair(EPI) ? 2 : 1;
   constexpr int M = MT * TH * 16;
   constexpr int NTHR = GEMM_THREADS * TH;
@@ -424,8 +424,11 @@ k_gemm(DevQ4B w, DevQ4B w2, DevAct act, int ntok, float *__restrict__ y, int ldy
   __shared__ double dsc[M];
   const int tid = threadIdx.x, lane = tid & 31, g = lane >> 2, tig = lane & 3;
   const int warp = (tid >> 5) & 3, mt0 = (tid >> 7) * MT;   // weight-row group, first token tile
-  const int K = w.cols, rows = w.rows;
-  const int nch = (K + GEMM_KC - 1) / GEMM_KC;
+  // ks > 1 (EPI_I64 only): work item (row block, K part) writes its part's int64 partial sums
+  // to y + part * ntok * ldy; K / ks is a multiple of 256
+  const int K = w.cols, rows = w.rows, kper = K / ks;
+  const int nch = (kper + GEMM_KC - 1) / GEMM_KC;
+  const int nrb = (rows + GEMM_ROWS - 1) / GEMM_ROWS;
   int32_t *KS = reinterpret_cast<int32_t *>(gsm + 2 * SM::STAGE);
   pdl_trigger();
   pdl_wait();
@@ -434,15 +437,16 @@ k_gemm(DevQ4B w, DevQ4B w2, DevAct act, int ntok, float *__restrict__ y, int ldy
     tmax[t] = 0.0f;
     tkey[t] = 0ull;
   }
-  // stage chunk ci of row block row0 into buffer `buf` (asynchronous copies, one commit group)
-  auto stage = [&](int buf, int row0, int ci) {
+  // stage the chunk at column k0 (ending at kend) of row block row0 into buffer `buf`
+  // (asynchronous copies, one commit group)
+  auto stage = [&](int buf, int row0, int k0, int kend) {
     uint8_t *base = gsm + buf * SM::STAGE;
     int8_t *A = reinterpret_cast<int8_t *>(base);
     uint8_t *W = base + SM::A;
     uint8_t *S = W + SM::W;
     // chunk widths are powers of two of at least 256 columns (K % 256 == 0), so every split
     // below is a shift
-    const int k0 = ci * GEMM_KC, kc = min(GEMM_KC, K - k0);
+    const int kc = min(GEMM_KC, kend - k0);
     const int l16 = 31 - __clz(kc >> 4);   // log2(kc / 16)
     for (int i = tid; i < (M << l16); i += NTHR) {
       const int t = i >> l16, c = (i & ((1 << l16) - 1)) << 4;
@@ -468,8 +472,9 @@ k_gemm(DevQ4B w, DevQ4B w2, DevAct act, int ntok, float *__restrict__ y, int ldy
     }
     cp_async_commit();
   };
-  for (int rb = blockIdx.x; rb * GEMM_ROWS < rows; rb += gridDim.x) {
-    const int row0 = rb * GEMM_ROWS;
+  for (int wi = blockIdx.x; wi < nrb * ks; wi += gridDim.x) {
+    const int rb = wi % nrb, part = wi / nrb;
+    const int row0 = rb * GEMM_ROWS, kb0 = part * kper, kend = kb0 + kper;
     int64_t acc[NM][MT][4];
 #pragma unroll
     for (int m = 0; m < NM; m++)
@@ -478,16 +483,16 @@ k_gemm(DevQ4B w, DevQ4B w2, DevAct act, int ntok, float *__restrict__ y, int ldy
 #pragma unroll
         for (int i = 0; i < 4; i++) acc[m][mt][i] = 0;
     __syncthreads();   // both buffers are free
-    stage(0, row0, 0);
+    stage(0, row0, kb0, kend);
     for (int ci = 0; ci < nch; ci++) {
-      if (ci + 1 < nch) stage((ci + 1) & 1, row0, ci + 1);
+      if (ci + 1 < nch) stage((ci + 1) & 1, row0, kb0 + (ci + 1) * GEMM_KC, kend);
       else cp_async_commit();   // an empty group keeps the wait count uniform
       cp_async_wait_prev();
       __syncthreads();
       const uint8_t *base = gsm + (ci & 1) * SM::STAGE;
       const int8_t *A = reinterpret_cast<const int8_t *>(base);
       const uint8_t *W = base + SM::A;
-      const int kc = min(GEMM_KC, K - ci * GEMM_KC);
+      const int kc = min(GEMM_KC, kend - (kb0 + ci * GEMM_KC));
       {   // decode the chunk's block scales once: KS[m][block][row]
         const uint16_t *S = reinterpret_cast<const uint16_t *>(W + SM::W);
         for (int i = tid; i < NM * GEMM_ROWS * (GEMM_KC / 32); i += NTHR) {
@@ -560,7 +565,7 @@ k_gemm(DevQ4B w, DevQ4B w2, DevAct act, int ntok, float *__restrict__ y, int ldy
         const int row = row0 + warp * 8 + tig * 2 + (i & 1);
         if (t >= ntok || row >= rows) continue;
         if (EPI == EPI_I64) {
-          reinterpret_cast<int64_t *>(y)[(size_t)t * ldy + row] = acc[0][mt][i];
+          reinterpret_cast<int64_t *>(y)[((size_t)part * ntok + t) * ldy + row] = acc[0][mt][i];
           continue;
         }
         float v = __double2float_rn(__dmul_rn(__ll2double_rn(acc[0][mt][i]), dsc[t]));
@@ -588,7 +593,7 @@ k_gemm(DevQ4B w, DevQ4B w2, DevAct act, int ntok, float *__restrict__ y, int ldy
 
 template <int MT, int TH, int EPI, bool SMALL>
 static cudaError_t gemm_launch(const DevQ4B &w, const DevQ4B &w2, const DevAct &act, int ntok, float *y, int ldy,
-                               uint32_t *err, uint32_t *ymax, unsigned long long *amax, cudaStream_t st) {
+                               uint32_t *err, uint32_t *ymax, unsigned long long *amax, cudaStream_t st, int ks) {
   constexpr int NM = epi_pair(EPI) ? 2 : 1;
   const size_t smem = GemmSmem<MT * TH, NM>::TOTAL;
   auto kern = k_gemm<MT, TH, EPI, SMALL>;
@@ -603,9 +608,9 @@ static cudaError_t gemm_launch(const DevQ4B &w, const DevQ4B &w2, const DevAct &
   cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
   cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, GEMM_THREADS * TH, smem);
   const int nrb = (w.rows + GEMM_ROWS - 1) / GEMM_ROWS;
-  const int grid = std::min(nrb, nsm * std::max(occ, 1));
+  const int grid = std::min(nrb * ks, nsm * std::max(occ, 1));
   return launch_k(kern, dim3(grid), dim3(GEMM_THREADS * TH), smem, st, 1, w, w2, act, ntok, y, ldy, err, ymax,
-                  amax);
+                  amax, ks);
 }
 
 // 16-token tiles per warp for full 64-token pieces: 2 (two token groups, 8 warps; the default)
@@ -621,11 +626,11 @@ static bool gemm_split() {
 
 template <int EPI>
 static cudaError_t gemm_mt(const DevQ4B &w, const DevQ4B &w2, const DevAct &act, int ntok, float *y, int ldy,
-                           uint32_t *err, uint32_t *ymax, unsigned long long *amax, cudaStream_t st) {
+                           uint32_t *err, uint32_t *ymax, unsigned long long *amax, cudaStream_t st, int ks = 1) {
   const bool small = w.small && (!epi_pair(EPI) || w2.small);
-#define SPB_GEMM_MT(MTV, THV)                                                                        \
-  return small ? gemm_launch<MTV, THV, EPI, true>(w, w2, act, ntok, y, ldy, err, ymax, amax, st) \
-               : gemm_launch<MTV, THV, EPI, false>(w, w2, act, ntok, y, ldy, err, ymax, amax, st)
+#define SPB_GEMM_MT(MTV, THV)                                                                            \
+  return small ? gemm_launch<MTV, THV, EPI, true>(w, w2, act, ntok, y, ldy, err, ymax, amax, st, ks) \
+               : gemm_launch<MTV, THV, EPI, false>(w, w2, act, ntok, y, ldy, err, ymax, amax, st, ks)
   switch ((ntok + 15) / 16) {   // 16-token tiles: split across two warp groups when even
     case 1: SPB_GEMM_MT(1, 1);
     case 2: SPB_GEMM_MT(1, 2);
@@ -635,6 +640,16 @@ static cudaError_t gemm_mt(const DevQ4B &w, const DevQ4B &w2, const DevAct &act,
       SPB_GEMM_MT(4, 1);
   }
 #undef SPB_GEMM_MT
+}
+
+// SPB_SPLITK=0 keeps every GEMM whole (comparisons; results are identical)
+static bool splitk_enabled() {
+  static int on = -1;
+  if (on < 0) {
+    const char *e = getenv("SPB_SPLITK");
+    on = (e && e[0] == '0') ? 0 : 1;
+  }
+  return on != 0;
 }
 
 // SPB_GEMM=0 keeps token batches on the dp4a k_gemv (comparisons; results are identical)
@@ -649,7 +664,7 @@ static bool gemm_enabled() {
 
 cudaError_t launch_gemv(const DevQ4B &w, const DevQ4B *w2, const DevAct &act, int ntok, float *y, int ldy,
                         int epi, uint32_t *err, cudaStream_t st, int grid_limit, uint32_t *ymax,
-                        unsigned long long *amax) {
+                        unsigned long long *amax, int64_t *ws, size_t ws_elems) {
   if ((w.cols & 31) || w.cols <= 0 || w.rows <= 0 || w.cols > 16384) return cudaErrorInvalidValue;
   if (epi < EPI_STORE || epi > EPI_I64) return cudaErrorInvalidValue;
   if (epi_pair(epi) && (!w2 || w2->rows != w.rows || w2->cols != w.cols)) return cudaErrorInvalidValue;
@@ -659,6 +674,11 @@ cudaError_t launch_gemv(const DevQ4B &w, const DevQ4B *w2, const DevAct &act, in
   const bool odd = ntok > 1 && (ntok & (ntok - 1)) != 0;
   if ((ntok >= 16 || odd) && grid_limit == 0 && (w.cols & 255) == 0 && (gemm_enabled() || odd)) {
     const DevQ4B ww2 = w2 ? *w2 : w;
+    // split-K: matrices with fewer 32-row blocks than SMs run their two K halves as separate
+    // CTAs into the workspace; the exact int64 halves are summed and scaled afterwards
+    const int nrb = (w.rows + GEMM_ROWS - 1) / GEMM_ROWS;
+    const bool split = epi == EPI_STORE && !ymax && !amax && ws && splitk_enabled() && nrb < 148 &&
+                       (w.cols % 512) == 0 && (size_t)2 * 64 * w.rows <= ws_elems;
     for (int t0 = 0; t0 < ntok; t0 += 64) {
       const int n = std::min(64, ntok - t0);
       const DevAct a2{act.q + (size_t)t0 * w.cols, act.bsum + (size_t)t0 * (w.cols >> 5), act.scale + t0};
@@ -666,6 +686,12 @@ cudaError_t launch_gemv(const DevQ4B &w, const DevQ4B *w2, const DevAct &act, in
       uint32_t *ym = ymax ? ymax + t0 : nullptr;
       unsigned long long *am = amax ? amax + t0 : nullptr;
       cudaError_t e;
+      if (split) {
+        e = gemm_mt<EPI_I64>(w, ww2, a2, n, reinterpret_cast<float *>(ws), w.rows, err, nullptr, nullptr, st, 2);
+        if (e == cudaSuccess) e = launch_scale_i64(ws, a2.scale, n, w.rows, y2, ldy, st, 2, (size_t)n * w.rows);
+        if (e != cudaSuccess) return e;
+        continue;
+      }
       switch (epi) {
         case EPI_STORE: e = gemm_mt<EPI_STORE>(w, ww2, a2, n, y2, ldy, err, ym, am, st); break;
         case EPI_GELU_MUL: e = gemm_mt<EPI_GELU_MUL>(w, ww2, a2, n, y2, ldy, err, ym, am, st); break;
@@ -681,10 +707,11 @@ cudaError_t launch_gemv(const DevQ4B &w, const DevQ4B *w2, const DevAct &act, in
   if (ntok > 1 && per_tok * ntok > 160 * 1024) {
     const int h = ntok / 2;
     const DevAct a2{act.q + (size_t)h * w.cols, act.bsum + (size_t)h * (w.cols >> 5), act.scale + h};
-    cudaError_t e = launch_gemv(w, w2, act, h, y, ldy, epi, err, st, grid_limit, ymax, amax);
+    cudaError_t e = launch_gemv(w, w2, act, h, y, ldy, epi, err, st, grid_limit, ymax, amax, ws, ws_elems);
     if (e != cudaSuccess) return e;
     return launch_gemv(w, w2, a2, h, reinterpret_cast<float *>(reinterpret_cast<char *>(y) + (size_t)h * ldy * yb),
-                       ldy, epi, err, st, grid_limit, ymax ? ymax + h : nullptr, amax ? amax + h : nullptr);
+                       ldy, epi, err, st, grid_limit, ymax ? ymax + h : nullptr, amax ? amax + h : nullptr, ws,
+                       ws_elems);
   }
   const DevQ4B ww2 = w2 ? *w2 : w;
   if (ntok == 1 && grid_limit == 0 && epi != EPI_I64 && ring_gemv_enabled()) {   // batch 1: the TMA-ring GEMV
@@ -1665,18 +1692,23 @@ cudaError_t launch_argmax_take(unsigned long long *keys, int ntok, int32_t *out,
   return launch_k(k_argmax_take, dim3(1), dim3(128), 0, st, 1, keys, ntok, out);
 }
 
-__global__ void k_scale_i64(const int64_t *acc, const float *scale, int n, float *y, int ldy) {
+__global__ void k_scale_i64(const int64_t *acc, const float *scale, int n, float *y, int ldy, int parts,
+                            size_t pstride) {
   pdl_trigger();
   pdl_wait();
   const int t = blockIdx.y;
   const double d = __dmul_rn(__ddiv_rn((double)scale[t], 127.0), 0x1p-24);
-  for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < n; j += gridDim.x * blockDim.x)
-    y[(size_t)t * ldy + j] = __double2float_rn(__dmul_rn(__ll2double_rn(acc[(size_t)t * n + j]), d));
+  for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < n; j += gridDim.x * blockDim.x) {
+    int64_t a = acc[(size_t)t * n + j];
+    for (int p = 1; p < parts; p++) a += acc[p * pstride + (size_t)t * n + j];
+    y[(size_t)t * ldy + j] = __double2float_rn(__dmul_rn(__ll2double_rn(a), d));
+  }
 }
 
 cudaError_t launch_scale_i64(const int64_t *acc, const float *scale, int ntok, int n, float *y, int ldy,
-                             cudaStream_t st) {
-  return launch_k(k_scale_i64, dim3((n + 255) / 256, ntok), dim3(256), 0, st, 1, acc, scale, n, y, ldy);
+                             cudaStream_t st, int parts, size_t part_stride) {
+  return launch_k(k_scale_i64, dim3((n + 255) / 256, ntok), dim3(256), 0, st, 1, acc, scale, n, y, ldy, parts,
+                  part_stride);
 }
 
 // the key's low word is 0xFFFFFFFF - row: a row offset subtracts from it

@@ -53,14 +53,18 @@ __host__ __device__ constexpr int epi_bytes(int epi) { return epi == EPI_I64 ? 8
 // y[t][j] for t < ntok over `w` (and `w2` for the gated epilogues). ymax (nullable):
 // per-token slots receiving atomicMax of the f32 bits of max |y| (the next quantizer's scale).
 // amax (nullable, zero on entry): per-token 64-bit greedy-argmax keys (first maximum).
+// ws (nullable): int64 workspace of ws_elems for split-K token batches (2 * 64 * rows values
+// for a K-halved matrix; without it every GEMM stays whole)
 cudaError_t launch_gemv(const DevQ4B &w, const DevQ4B *w2, const DevAct &act, int ntok, float *y,
                         int ldy, int epi, uint32_t *err, cudaStream_t st, int grid_limit = 0,
-                        uint32_t *ymax = nullptr, unsigned long long *amax = nullptr);
+                        uint32_t *ymax = nullptr, unsigned long long *amax = nullptr, int64_t *ws = nullptr,
+                        size_t ws_elems = 0);
 
 // y[t][j] = (float)(acc[t][j] * (scale[t] / 127 * 2^-24)), the GEMV epilogue's rounding, for
-// n outputs of ntok rows (acc row stride n, y row stride ldy)
+// n outputs of ntok rows (acc row stride n, y row stride ldy); with parts > 1, acc is the exact
+// sum of the parts at acc + p * part_stride
 cudaError_t launch_scale_i64(const int64_t *acc, const float *scale, int ntok, int n, float *y, int ldy,
-                             cudaStream_t st);
+                             cudaStream_t st, int parts = 1, size_t part_stride = 0);
 // greedy-argmax keys of a row slice starting at global row `base` -> keys over global rows
 cudaError_t launch_keys_rebase(unsigned long long *keys, int ntok, int base, cudaStream_t st);
 

@@ -582,6 +582,8 @@ struct spb_session {
   // logits [NT_MAX][V] and the all-gathered slices [world][NT_MAX][V]
   int64_t *y64 = nullptr;
   float *logits_l = nullptr, *logits_g = nullptr;
+  int64_t *ws = nullptr;          // split-K workspace of the token-batch GEMM [2][NT_MAX][E]
+  size_t ws_elems = 0;
 };
 
 // 1: decode steps run as the persistent kernel where it covers the shape; 0 (default, the
@@ -621,6 +623,7 @@ extern "C" int spb_session_open(spb_model *m, int pmax, spb_session **out) {
   const size_t o_gg = take((size_t)NT_MAX * m->FF * 4), o_dn = take((size_t)NT_MAX * E * 4);
   const size_t o_lg = take((size_t)NT_MAX * m->Vfull * 4), o_qi = take((size_t)NT_MAX * m->QD * 4);
   const size_t o_y64 = m->tp ? take((size_t)NT_MAX * E * 8) : 0;
+  const size_t o_ws = take((size_t)2 * NT_MAX * E * 8);
   const size_t o_lgl = m->tp ? take((size_t)NT_MAX * m->V * 4) : 0;
   const size_t o_lgg = m->tp ? take((size_t)NT_MAX * m->Vfull * 4) : 0;
   const size_t o_aq = take((size_t)NT_MAX * maxK), o_ab = take((size_t)NT_MAX * (maxK / 32) * 4);
@@ -648,6 +651,8 @@ extern "C" int spb_session_open(spb_model *m, int pmax, spb_session **out) {
   s->ao_max = (uint32_t *)(B + o_slots); s->gg_max = s->ao_max + NT_MAX;
   s->amax_keys = (unsigned long long *)(B + o_keys);
   s->rows_dev = (BatchRow *)(B + o_rows);
+  s->ws = (int64_t *)(B + o_ws);
+  s->ws_elems = (size_t)2 * NT_MAX * E;
   if (m->tp) {
     s->y64 = (int64_t *)(B + o_y64);
     s->logits_l = (float *)(B + o_lgl);
@@ -714,7 +719,8 @@ static cudaError_t enqueue_rows(spb_session *s, int nt, bool want_logits, const 
   // a K-split matrix (tensor parallel): exact int64 partial sums, summed over the group, then
   // scaled with the GEMV's own rounding
   auto split_gemv = [&](const DevQ4B &w, float *y) -> cudaError_t {
-    if (!m->tp) return launch_gemv(w, nullptr, s->act, nt, y, E, EPI_STORE, s->err_dev, st);
+    if (!m->tp) return launch_gemv(w, nullptr, s->act, nt, y, E, EPI_STORE, s->err_dev, st, 0, nullptr, nullptr, s->ws,
+                                   s->ws_elems);
     cudaError_t r = launch_gemv(w, nullptr, s->act, nt, reinterpret_cast<float *>(s->y64), E, EPI_I64, s->err_dev, st);
     if (r == cudaSuccess) r = tp_sum_i64(m->tp, s->y64, (size_t)nt * E, st, s->err_dev);
     if (r == cudaSuccess) r = launch_scale_i64(s->y64, s->act.scale, nt, E, y, E, st);
