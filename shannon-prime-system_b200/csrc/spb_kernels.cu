@@ -1308,7 +1308,9 @@ __global__ void __launch_bounds__(ATTN_THREADS, 2) k_attn(AttnArgs a, int cmax, 
   extern __shared__ __align__(128) uint8_t asm_raw[];
   int32_t *ring = reinterpret_cast<int32_t *>(asm_raw);            // [STAGES][SUB*HD]
   int32_t *qs = ring + ATTN_STAGES * SUB * HD;                       // [G][HD]
-  int32_t *sc = qs + G * HD;                                         // [G][cmax] scores, then e
+  const bool fused = a.qkv != nullptr;
+  int32_t *kvn = qs + G * HD;                                        // fused: [2][HD] new K, V rows
+  int32_t *sc = kvn + (fused ? 2 * HD : 0);                          // [G][cmax] scores, then e
   // [GROUPS][G][HD] this CTA's V-sums (absent when one thread per head dim pushes them
   // straight from registers), then with CL > 1 the [CL][G][HD/CL] V-sums pushed by each rank
   const bool direct = GROUPS == 1 && CL > 1;
@@ -1321,6 +1323,8 @@ __global__ void __launch_bounds__(ATTN_THREADS, 2) k_attn(AttnArgs a, int cmax, 
   __shared__ int32_t mx_in[16][G];        // CL > 1: each rank's score maximum, pushed by that rank
   __shared__ int64_t s_in[16][G];         // CL > 1: each rank's exponential sum
   __shared__ float fred[33];
+  __shared__ acc128 gred[ATTN_THREADS / 32];   // fused: per-warp QK-norm sums of squares
+  __shared__ uint64_t ginv[ATTN_THREADS / 32]; // fused: inverse rms per head group
 
   const int rank = CL > 1 ? (int)cluster.block_rank() : 0;
   // the partials are pushed into the owning rank's shared memory (no remote loads): this
@@ -1366,8 +1370,10 @@ __global__ void __launch_bounds__(ATTN_THREADS, 2) k_attn(AttnArgs a, int cmax, 
   };
 
   // K/V rows before this launch's first new position were written by earlier steps, so a
-  // CTA whose slice ends before it can start its copies before the predecessor finishes
-  const bool early = c1 <= (a.rows ? p : a.pos_dev[0]);
+  // CTA whose slice ends before it can start its copies before the predecessor finishes; fused,
+  // the new position's rows are patched into shared memory, so every CTA starts early
+  const bool own = fused && cn > 0 && c1 == p + 1;   // this CTA's slice ends at the new position
+  const bool early = fused || c1 <= (a.rows ? p : a.pos_dev[0]);
   pdl_trigger();
   if (threadIdx.x == 0) {
     for (int s = 0; s < ATTN_STAGES; s++) mbar_init(&full[s], 1);
@@ -1376,7 +1382,80 @@ __global__ void __launch_bounds__(ATTN_THREADS, 2) k_attn(AttnArgs a, int cmax, 
       for (int i = 0; i < min(ATTN_STAGES, total); i++) issue(i);
   }
   pdl_wait();
-  for (int i = threadIdx.x; i < G * HD; i += ATTN_THREADS) qs[i] = a.qi[(size_t)t * QD + (size_t)g * G * HD + i];
+  if (!fused) {
+    for (int i = threadIdx.x; i < G * HD; i += ATTN_THREADS) qs[i] = a.qi[(size_t)t * QD + (size_t)g * G * HD + i];
+  } else {
+    // QK-norm + CORDIC-RoPE of the G query heads (and, for the owner, the new K row), HD/2
+    // threads per head, one pair each, the same island steps as k_rope_kv
+    constexpr int HALF = HD / 2, GPP = ATTN_THREADS / HALF, WPG = HALF / 32;
+    const int KVD = a.NKV * HD;
+    const float *row = a.qkv + (size_t)t * (QD + 2 * KVD);
+    const int gi = threadIdx.x / HALF, i = threadIdx.x % HALF;
+    const int nrot = G + (own ? 1 : 0);
+    const uint64_t phase = (uint64_t)(int64_t)p * a.W[i];
+    for (int j0 = 0; j0 < nrot; j0 += GPP) {
+      const int j = j0 + gi;
+      const bool act = j < nrot, is_k = j == G;
+      const float *src = row + (is_k ? QD + g * HD : (g * G + j) * HD);
+      float x0 = act ? src[i] : 0.0f, x1 = act ? src[i + HALF] : 0.0f;
+      if (a.q_norm) {
+        acc128 ss{0ull, 0ll};
+        bool bad = false;
+        if (act) {
+          if (!(fabsf(x0) < 32768.0f)) bad = true;
+          else { const int64_t xi = q16_round(x0); acc128_add(ss, xi * xi); }
+          if (!(fabsf(x1) < 32768.0f)) bad = true;
+          else { const int64_t xi = q16_round(x1); acc128_add(ss, xi * xi); }
+        }
+        if (bad) raise_err(a.err, ERR_NORM_RANGE);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+          acc128 r;
+          r.lo = __shfl_xor_sync(0xffffffffu, ss.lo, o);
+          r.hi = __shfl_xor_sync(0xffffffffu, ss.hi, o);
+          acc128_add(ss, r);
+        }
+        if (lane == 0) gred[warp] = ss;
+        __syncthreads();
+        if (act && i == 0) {
+          acc128 tot = gred[gi * WPG];
+          for (int w = 1; w < WPG; w++) acc128_add(tot, gred[gi * WPG + w]);
+          ginv[gi] = rms_inv(tot, HD, a.err);
+        }
+        __syncthreads();
+        if (act) {
+          const float *nw = is_k ? a.k_norm : a.q_norm;
+          const uint64_t inv = ginv[gi];
+          x0 = rms_apply(x0, nw[i], inv, a.err);
+          x1 = rms_apply(x1, nw[i + HALF], inv, a.err);
+        }
+      }
+      if (act) {
+        int32_t oa, ob;
+        cordic_rotate(x0, x1, phase, a.T, a.gain, oa, ob, a.err);
+        int32_t *dst = is_k ? kvn : qs + j * HD;
+        dst[i] = oa;
+        dst[i + HALF] = ob;
+        if (is_k) {
+          int32_t *kr = const_cast<int32_t *>(kbase) + (size_t)p * HD;
+          kr[i] = oa;
+          kr[i + HALF] = ob;
+        }
+      }
+    }
+    if (own) {   // the new V row on the 2^16 grid
+      const float *src = row + QD + KVD + g * HD;
+      int32_t *vr = const_cast<int32_t *>(vbase) + (size_t)p * HD;
+      for (int d = threadIdx.x; d < HD; d += ATTN_THREADS) {
+        const float v = src[d];
+        int32_t q = 0;
+        if (!(fabsf(v) < 16384.0f)) raise_err(a.err, ERR_V_RANGE);
+        else q = __float2int_rn(__fmul_rn(v, 65536.0f));
+        kvn[HD + d] = q;
+        vr[d] = q;
+      }
+    }
+  }
   if (threadIdx.x < G) { mx_loc[threadIdx.x] = INT32_MIN; s_loc[threadIdx.x] = 0; }
   __syncthreads();
   if (threadIdx.x == 0 && !early)
@@ -1400,6 +1479,10 @@ __global__ void __launch_bounds__(ATTN_THREADS, 2) k_attn(AttnArgs a, int cmax, 
     mbar_wait(&full[stage], (uint32_t)(i / ATTN_STAGES) & 1u, a.err);
     const int32_t *buf = ring + stage * SUB * HD;
     const int len = min(SUB, cn - i * SUB);
+    if (own && i == nsub - 1) {   // the new position (the slice's last) from this kernel's K row
+      for (int d = threadIdx.x; d < HD; d += ATTN_THREADS) ring[stage * SUB * HD + (len - 1) * HD + d] = kvn[d];
+      __syncthreads();
+    }
     for (int p4 = warp * 4; p4 < len; p4 += ATTN_THREADS / 8) {   // warp-uniform bound
       const int pp = p4 + gq;
       const bool ok = pp < len;
@@ -1486,6 +1569,10 @@ __global__ void __launch_bounds__(ATTN_THREADS, 2) k_attn(AttnArgs a, int cmax, 
     const int32_t *buf = ring + stage * SUB * HD;
     const int j0 = (i - nsub) * SUB;
     const int len = min(SUB, cn - j0);
+    if (own && i == total - 1) {   // ... and its V row
+      for (int d = threadIdx.x; d < HD; d += ATTN_THREADS) ring[stage * SUB * HD + (len - 1) * HD + d] = kvn[HD + d];
+      __syncthreads();
+    }
     // eight positions per fold into 128 bits: e <= 2^30 and |v| < 2^30, so 8 |e v| < 2^63
     // (positions pp < SUB always stay inside the stage; those past len weigh 0)
     for (int p8 = grp; p8 < len; p8 += 8 * GROUPS) {
@@ -1571,10 +1658,11 @@ __global__ void __launch_bounds__(ATTN_THREADS, 2) k_attn(AttnArgs a, int cmax, 
 
 
 template <int HD, int G>
-static size_t attn_smem(int cmax, int cl) {
+static size_t attn_smem(int cmax, int cl, bool fused) {
   constexpr int SUB = AttnSub<HD>::SUB, GROUPS = ATTN_THREADS / HD;
   const bool direct = GROUPS == 1 && cl > 1;
-  return (size_t)ATTN_STAGES * SUB * HD * 4 + (size_t)G * HD * 4 + (size_t)((G * cmax + 3) & ~3) * 4 +
+  return (size_t)ATTN_STAGES * SUB * HD * 4 + (size_t)G * HD * 4 + (fused ? (size_t)2 * HD * 4 : 0) +
+         (size_t)((G * cmax + 3) & ~3) * 4 +
          (direct ? 0 : (size_t)GROUPS * G * HD * sizeof(acc128)) + (cl > 1 ? (size_t)G * HD * sizeof(acc128) : 0);
 }
 
@@ -1599,7 +1687,7 @@ static cudaError_t attn_cl(const AttnArgs &a, cudaStream_t st) {
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3(16, 1, 1);
       cfg.blockDim = dim3(ATTN_THREADS);
-      cfg.dynamicSmemBytes = attn_smem<HD, G>((a.P + 15) / 16, 16);
+      cfg.dynamicSmemBytes = attn_smem<HD, G>((a.P + 15) / 16, 16, a.qkv != nullptr);
       cudaLaunchAttribute attr[1];
       attr[0].id = cudaLaunchAttributeClusterDimension;
       attr[0].val.clusterDim.x = 16;
@@ -1617,9 +1705,10 @@ static cudaError_t attn_cl(const AttnArgs &a, cudaStream_t st) {
   const int span = a.win >= 0 ? std::min(a.P, a.win) : a.P;
   int cl = 1;
   while (cl < clmax && ((long)a.ntok * a.NKV * cl < 2L * nsm || span > cl * ATTN_SPAN)) cl *= 2;
-  while (cl < clmax && attn_smem<HD, G>((a.P + cl - 1) / cl, cl) > 200 * 1024) cl *= 2;
+  const bool fused = a.qkv != nullptr;
+  while (cl < clmax && attn_smem<HD, G>((a.P + cl - 1) / cl, cl, fused) > 200 * 1024) cl *= 2;
   const int cmax = (a.P + cl - 1) / cl;
-  const size_t smem = attn_smem<HD, G>(cmax, cl);
+  const size_t smem = attn_smem<HD, G>(cmax, cl, fused);
   if (smem > 200 * 1024) return cudaErrorInvalidValue;
   return launch_k(kern, dim3(cl, a.NKV, a.ntok), dim3(ATTN_THREADS), smem, st, cl, a, cmax, cl);
 }

@@ -117,6 +117,14 @@ struct AttnArgs {
   const BatchRow *rows;    // nullable: rows of different sessions (kc, vc, pos_dev unused;
                            // P = the largest capacity, sizes the shared memory)
   int layer;               // with rows: the layer whose cache rows are read
+  // fused QK-norm + RoPE + K/V store, for rows whose only new position is their own (decode
+  // rows, batch rows): with qkv set, every CTA normalises and rotates its query heads itself
+  // (qi unused) and the CTA whose position slice ends at the new position stores that
+  // position's rotated K row and quantized V row (as k_rope_kv does)
+  const float *qkv;        // nullable: [ntok][QD + 2*KVD] projections
+  const float *q_norm, *k_norm;
+  const uint64_t *W, *T;
+  uint64_t gain;
 };
 cudaError_t launch_attn(const AttnArgs &a, cudaStream_t st);
 

@@ -700,6 +700,17 @@ extern "C" void spb_session_close(spb_session *s) {
 extern "C" void *spb_session_stream(spb_session *s) { return s ? (void *)s->st : nullptr; }
 extern "C" int spb_session_position(const spb_session *s) { return s ? s->pos : -1; }
 
+// SPB_ROPE_FUSED=0 keeps k_rope_kv as its own launch for decode rows too (comparisons; results
+// are identical)
+static bool rope_fused_enabled() {
+  static int on = -1;
+  if (on < 0) {
+    const char *e = getenv("SPB_ROPE_FUSED");
+    on = (e && e[0] == '0') ? 0 : 1;
+  }
+  return on != 0;
+}
+
 // Enqueue the schedule for nt rows (tokens already in tok_dev, positions at pos_dev). With
 // rows (device, [nt]), row t belongs to its own session: RoPE/KV store and attention use that
 // session's cache and position; Pmax is the largest of their capacities.
@@ -716,6 +727,10 @@ static cudaError_t enqueue_rows(spb_session *s, int nt, bool want_logits, const 
     if (e != cudaSuccess) return e; \
   } while (0)
   K(launch_embed(m->embd, s->tok_dev, nt, m->es, m->gemma ? 1 : 0, s->x, m->Vfull, s->err_dev, st));
+  // rows whose only new position is their own (a decode row, or rows of distinct sessions) get
+  // QK-norm, RoPE and the K/V store inside the attention kernel; prefill chunks, whose rows read
+  // each other's new K/V, keep the separate k_rope_kv
+  const bool fuse_rope = (nt == 1 || rows != nullptr) && rope_fused_enabled();
   // a K-split matrix (tensor parallel): exact int64 partial sums, summed over the group, then
   // scaled with the GEMV's own rounding
   auto split_gemv = [&](const DevQ4B &w, float *y) -> cudaError_t {
@@ -729,11 +744,13 @@ static cudaError_t enqueue_rows(spb_session *s, int nt, bool want_logits, const 
   const size_t kvl = kv_layer_elems(m, s->pmax);
   for (int L = 0; L < m->NL; L++) {
     const DevLayer &d = m->layers[L];
+    // the attention norm also clears the attention output's max slots (filled by k_attn)
     if (L == 0) {
-      K(launch_norm(s->x, nullptr, nullptr, d.attn_norm, E, nt, s->act, nullptr, s->err_dev, st));
+      K(launch_norm(s->x, nullptr, nullptr, d.attn_norm, E, nt, s->act, nullptr, s->err_dev, st, s->ao_max));
     } else {
       const DevLayer &p = m->layers[L - 1];
-      K(launch_norm(s->x, s->dn, m->gemma ? p.post_ffw : nullptr, d.attn_norm, E, nt, s->act, nullptr, s->err_dev, st));
+      K(launch_norm(s->x, s->dn, m->gemma ? p.post_ffw : nullptr, d.attn_norm, E, nt, s->act, nullptr, s->err_dev, st,
+                    s->ao_max));
     }
     K(launch_gemv(d.qkv, nullptr, s->act, nt, s->qkv, QKV, EPI_STORE, s->err_dev, st));
     RopeArgs ra{};
@@ -744,12 +761,16 @@ static cudaError_t enqueue_rows(spb_session *s, int nt, bool want_logits, const 
     ra.T = m->tabs; ra.gain = m->gain; ra.pos_dev = s->pos_dev;
     ra.NH = m->NH; ra.NKV = m->NKV; ra.HD = m->HD; ra.P = s->pmax; ra.ntok = nt; ra.err = s->err_dev;
     ra.zero_slot = s->ao_max;
-    K(launch_rope_kv(ra, st));
+    if (!fuse_rope) K(launch_rope_kv(ra, st));
     AttnArgs aa{};
     aa.rows = rows; aa.layer = L;
     aa.qi = s->qi; aa.kc = ra.kc; aa.vc = ra.vc; aa.ao = s->ao; aa.pos_dev = s->pos_dev;
     aa.NH = m->NH; aa.NKV = m->NKV; aa.HD = m->HD; aa.P = rows ? Pmax : s->pmax; aa.win = d.win; aa.ntok = nt;
     aa.ascale = ascale; aa.err = s->err_dev; aa.ao_max = s->ao_max;
+    if (fuse_rope) {
+      aa.qkv = s->qkv; aa.q_norm = d.q_norm; aa.k_norm = d.k_norm;
+      aa.W = ra.W; aa.T = m->tabs; aa.gain = m->gain;
+    }
     K(launch_attn(aa, st));
     if (m->tp) K(tp_max_u32(m->tp, s->ao_max, nt, st, s->err_dev));   // the quantizer's max over all heads
     K(launch_quant(s->ao, m->QD, m->QD, nt, s->act, s->ao_max, s->err_dev, st));
