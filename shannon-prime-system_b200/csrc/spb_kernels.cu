@@ -709,9 +709,25 @@ cudaError_t launch_gemv(const DevQ4B &w, const DevQ4B *w2, const DevAct &act, in
     const DevAct a2{act.q + (size_t)h * w.cols, act.bsum + (size_t)h * (w.cols >> 5), act.scale + h};
     cudaError_t e = launch_gemv(w, w2, act, h, y, ldy, epi, err, st, grid_limit, ymax, amax, ws, ws_elems);
     if (e != cudaSuccess) return e;
-    return launch_gemv(w, w2, a2, h, reinterpret_cast<float *>(reinterpret_cast<char *>(y) + (size_t)h * ldy * yb),
-                       ldy, epi, err, st, grid_limit, ymax ? ymax + h : nullptr, amax ? amax + h : nullptr, ws,
-                       ws_elems);
+    return launch_gemv(w, w2, a2, ntok - h,
+                       reinterpret_cast<float *>(reinterpret_cast<char *>(y) + (size_t)h * ldy * yb), ldy, epi, err,
+                       st, grid_limit, ymax ? ymax + h : nullptr, amax ? amax + h : nullptr, ws, ws_elems);
+  }
+  // row counts the k_gemv templates do not cover (K not a multiple of 256, so no GEMM: e.g. a
+  // tensor-parallel rank's slice of the attention output or FFN down projection): pieces of
+  // 16, 8, 4, 2, 1 rows
+  if (ntok > 16 || (ntok & (ntok - 1))) {
+    for (int t0 = 0; t0 < ntok;) {
+      int n = 16;
+      while (n > ntok - t0) n >>= 1;
+      const DevAct a2{act.q + (size_t)t0 * w.cols, act.bsum + (size_t)t0 * (w.cols >> 5), act.scale + t0};
+      cudaError_t e = launch_gemv(w, w2, a2, n, reinterpret_cast<float *>(reinterpret_cast<char *>(y) + (size_t)t0 * ldy * yb),
+                                  ldy, epi, err, st, grid_limit, ymax ? ymax + t0 : nullptr, amax ? amax + t0 : nullptr,
+                                  ws, ws_elems);
+      if (e != cudaSuccess) return e;
+      t0 += n;
+    }
+    return cudaSuccess;
   }
   const DevQ4B ww2 = w2 ? *w2 : w;
   if (ntok == 1 && grid_limit == 0 && epi != EPI_I64 && ring_gemv_enabled()) {   // batch 1: the TMA-ring GEMV

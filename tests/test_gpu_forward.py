@@ -160,3 +160,18 @@ def test_attention_head_shapes(xr, cuda_ok, hd, nh, nkv):
     s.close()
     want_s.close()
     m.free()
+
+
+@pytest.mark.parametrize("name", ["micro_qwen", "micro_gemma"])
+def test_prefill_k_not_multiple_of_256(xr, cuda_ok, name):
+    """Attention output projection with K = 128 and FFN down with K = 384 (what a
+    tensor-parallel rank holds of a small model): no tensor-core GEMM for those matrices, so a
+    40-row prefill chunk runs them as GEMV pieces of 32 + 8 rows; == XREF."""
+    cfg = dataclasses.replace(spmodel.CONFIGS[name], n_layers=2, n_head=2, n_head_kv=1, n_ff=384)
+    T = spmodel.gen_model(cfg, seed=12)
+    m = spb200.Model.upload(cfg, T)
+    toks = spmodel.gen_tokens(33, 40, cfg.n_vocab)
+    got = m.forward(toks)
+    want = xr.session(xref.build_desc(cfg, T), cfg.max_context).prefill(toks)
+    m.free()
+    assert np.array_equal(u32(got), u32(want))
