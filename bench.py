@@ -459,7 +459,11 @@ def run_spb(args):
             cpu = {"value": round(r["value"], 5), "unit": "tokens/s", "cores": r["cores"], "kind": "reference",
                    "sample": r["sample"]}
 
-    kernels_per_step = 1 + 10 * cfg.n_layers + 4
+    # embed; per layer norm, QKV, attention (QK-norm + RoPE + KV store fused; a separate
+    # k_rope_kv with SPB_ROPE_FUSED=0), quantize, O, norm, gate/up, quantize, down; final norm,
+    # LM head, argmax take, position advance
+    per_layer = 10 if os.environ.get("SPB_ROPE_FUSED") == "0" else 9
+    kernels_per_step = 1 + per_layer * cfg.n_layers + 4
     line = {
         "metric": METRIC, "value": round(world * K / (ms / 1e3), 3), "unit": "tokens/s",
         "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": round(ms / K, 4),
