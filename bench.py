@@ -15,6 +15,10 @@ K timed greedy decode steps. A step is one decode token through the whole model.
            memory and the full-vocab logits copied device->host every step
   roofline the dequant-GEMV alone, per decode shape, CUDA-event timed over weights
            larger than L2, weighted by its share of a decode token's bytes
+  prefill  the untimed --prefill ingestion timed with CUDA events: tokens/s and the
+           tensor-core GEMM's int8 ops/s against an int8 dense peak (2 x measured bf16)
+  b64      --batch sessions (default 64) decoding together (spb_batch_decode_step)
+  tp       with --tp and N > 1: one session tensor-parallel over the N GPUs
 Multi-GPU (torchrun): independent sessions spread one per GPU (weak scaling); the only
 collectives are the barrier and the max-over-ranks of the timings.
 
@@ -371,8 +375,13 @@ def run_spb(args):
     stream = torch.cuda.ExternalStream(s.stream(), device=torch.device("cuda", local))
     toks = spmodel.gen_tokens(args.seed + 100 + rank, args.prefill, cfg.n_vocab)
     t0 = time.perf_counter()
+    p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    p0.record(stream)
     s.prefill(toks, logits=False)
+    p1.record(stream)
+    p1.synchronize()
     prefill_s = time.perf_counter() - t0
+    prefill_dev_s = p0.elapsed_time(p1) / 1e3
     tok = int(toks[-1])
     s.greedy(tok, W)
 
@@ -464,6 +473,25 @@ def run_spb(args):
     # LM head, argmax take, position advance
     per_layer = 10 if os.environ.get("SPB_ROPE_FUSED") == "0" else 9
     kernels_per_step = 1 + per_layer * cfg.n_layers + 4
+    # prefill on the tensor cores: the layer matmuls' int8 MACs (no LM head: no logits asked;
+    # the attention dots are exact int64 work, not tensor work), against an int8 dense peak of
+    # twice the measured bf16 GEMM burst (B200 tensor cores run dense int8 at 2x bf16)
+    layer_params = sum(r * c * (2 if gated else 1) for name, r, c, gated, n in gemv_shapes(cfg)
+                       if name != "lm_head")
+    prefill_ops = 2.0 * args.prefill * cfg.n_layers * layer_params
+    bf16 = None
+    pk = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(pk):
+        bf16 = json.load(open(pk)).get("bf16_tflops")
+    int8_peak = 2.0 * (bf16 or 1590.0)
+    prefill = {"tokens": args.prefill, "s": round(prefill_dev_s, 4),
+               "tokens_per_s": round(args.prefill / prefill_dev_s, 1),
+               "int8_ops": prefill_ops, "achieved_tops": round(prefill_ops / prefill_dev_s / 1e12, 2),
+               "peak_tops": round(int8_peak, 1),
+               "peak_source": ("2 x measured" if bf16 else "2 x fallback") + " bf16 dense TF/s (int8 dense = 2 x bf16)",
+               "frac": round(prefill_ops / prefill_dev_s / 1e12 / int8_peak, 4),
+               "kernel": "k_gemm (mma.sync m16n8k32 int8 with a per-32-column int64 block-scale epilogue); "
+                         "CUDA events around spb_session_prefill on the session stream"}
     line = {
         "metric": METRIC, "value": round(world * K / (ms / 1e3), 3), "unit": "tokens/s",
         "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": round(ms / K, 4),
@@ -483,6 +511,7 @@ def run_spb(args):
         "roofline": roof,
         "cpu_baseline": cpu,
         "b64": b64,
+        "prefill": prefill,
     }
     if tpr:
         line["tp"] = tpr
