@@ -308,26 +308,14 @@ static cudaError_t gemv_launch(const DevQ4B &w, const DevQ4B &w2, const DevAct &
   return launch_k(kern, dim3(grid), dim3(GEMV_THREADS), smem, st, 1, w, w2, act, y, ldy, err, ymax, amax);
 }
 
-// rows per warp group: keep ~16 vectors of 16 bytes per lane in flight, but no more rows per
-// warp than leave every SM a CTA (a 3840-row matrix at 4 rows per warp fills only 120 SMs)
+// one row per warp group: the most warps (and CTAs) per matrix. Measured per decode step at the
+// 12B shape, 1 row per warp beats 2-4 (259 vs 251-255 tok/s) although 2-4 rows time a little
+// better launched alone: smaller first loads shorten each launch's ramp behind its predecessor.
 template <int NT, int EPI, int NCH>
 static cudaError_t gemv_rpw(const DevQ4B &w, const DevQ4B &w2, const DevAct &act, float *y, int ldy,
                             uint32_t *err, uint32_t *ymax, unsigned long long *amax, cudaStream_t st,
                             int grid_limit) {
-  constexpr int NM = epi_pair(EPI) ? 2 : 1;
-  constexpr int R0 = 16 / (NCH * NM);
-  constexpr int RPW = NT > 1 ? 1 : (R0 < 1 ? 1 : (R0 > 4 ? 4 : R0));
-  static int nsm = 0;
-  if (nsm == 0) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
-    if (nsm <= 0) nsm = 148;
-  }
-  auto ctas = [&](int r) { return (w.rows + r * GEMV_WARPS - 1) / (r * GEMV_WARPS); };
-  if (RPW >= 4 && ctas(4) < nsm && ctas(2) >= nsm)
-    return gemv_launch<NT, EPI, NCH, (RPW >= 4 ? 2 : RPW)>(w, w2, act, y, ldy, err, ymax, amax, st, grid_limit);
-  return gemv_launch<NT, EPI, NCH, RPW>(w, w2, act, y, ldy, err, ymax, amax, st, grid_limit);
+  return gemv_launch<NT, EPI, NCH, 1>(w, w2, act, y, ldy, err, ymax, amax, st, grid_limit);
 }
 
 template <int NT, int EPI>
