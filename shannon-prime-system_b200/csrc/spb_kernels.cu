@@ -308,9 +308,9 @@ static cudaError_t gemv_launch(const DevQ4B &w, const DevQ4B &w2, const DevAct &
   return launch_k(kern, dim3(grid), dim3(GEMV_THREADS), smem, st, 1, w, w2, act, y, ldy, err, ymax, amax);
 }
 
-// one row per warp group: the most warps (and CTAs) per matrix. Measured per decode step at the
-// 12B shape, 1 row per warp beats 2-4 (259 vs 251-255 tok/s) although 2-4 rows time a little
-// better launched alone: smaller first loads shorten each launch's ramp behind its predecessor.
+// one row per warp group: the most warps (and CTAs) per matrix, and the fewest registers (64 for
+// a single matrix at K <= 4096, 79 for the gate/up pair, against ~126 at 2-4 rows), so 4 CTAs
+// instead of 2 fit an SM. Measured per decode step at the 12B shape: 257-259 vs 251-255 tok/s.
 template <int NT, int EPI, int NCH>
 static cudaError_t gemv_rpw(const DevQ4B &w, const DevQ4B &w2, const DevAct &act, float *y, int ldy,
                             uint32_t *err, uint32_t *ymax, unsigned long long *amax, cudaStream_t st,
