@@ -122,21 +122,29 @@ k_gemv(DevQ4B w, DevQ4B w2, DevAct act, float *__restrict__ y, int ldy, uint32_t
   int32_t *xs = xw + NT * kw;                                               // [NT][nblk]
   double *dsc = reinterpret_cast<double *>(xs + ((NT * nblk + 1) & ~1));   // [NT]
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  // KS = 2 (single wide rows, e.g. the FFN down projection): the two warps of a pair take the
+  // two halves of a row's 32-column blocks, so each holds half the code vectors (half the
+  // registers: twice the resident warps); the odd warp hands its exact int64 half to the even
+  // warp through shared memory under a 64-thread named barrier, and only even warps finish rows
+  constexpr int KS = (NT == 1 && RPW == 1 && NM == 1 && NCH == 16) ? 2 : 1;
+  constexpr int NCHW = NCH / KS;   // code vectors per lane per row held by one warp
+  const int half = warp % KS, pair = warp / KS;
+  __shared__ int64_t ks_part[GEMV_WARPS / KS];
   const int rows = w.rows;
   const size_t rstride = (size_t)(K >> 1);
   const int ngroups = (rows + RPW - 1) / RPW;
-  const int gstride = gridDim.x * GEMV_WARPS;
-  int g = blockIdx.x * GEMV_WARPS + warp;
+  const int gstride = gridDim.x * (GEMV_WARPS / KS);
+  int g = blockIdx.x * (GEMV_WARPS / KS) + pair;
 
-  uint4 cw[NM][RPW][NCH];
-  uint32_t hw[NM][RPW][NCH];
+  uint4 cw[NM][RPW][NCHW];
+  uint32_t hw[NM][RPW][NCHW];
   auto load_group = [&](int grp) {
 #pragma unroll
     for (int r = 0; r < RPW; r++) {
       const int row = grp * RPW + r;
 #pragma unroll
-      for (int j = 0; j < NCH; j++) {
-        const int b = lane + 32 * j;
+      for (int j = 0; j < NCHW; j++) {
+        const int b = lane + 32 * (half * NCHW + j);
         if (row < rows && b < nblk) {
           cw[0][r][j] = ld_stream_u4(w.codes + (size_t)row * rstride + (size_t)b * 16);
           hw[0][r][j] = __ldg(w.scales + (size_t)row * nblk + b);
@@ -208,8 +216,8 @@ k_gemv(DevQ4B w, DevQ4B w2, DevAct act, float *__restrict__ y, int ldy, uint32_t
 #pragma unroll
         for (int t = 0; t < NT; t++) acc[m][r][t] = 0;
 #pragma unroll
-    for (int j = 0; j < NCH; j++) {
-      const int b = lane + 32 * j;
+    for (int j = 0; j < NCHW; j++) {
+      const int b = lane + 32 * (half * NCHW + j);
       if (b < nblk) {
 #pragma unroll
         for (int t = 0; t < NT; t++) {
@@ -233,6 +241,13 @@ k_gemv(DevQ4B w, DevQ4B w2, DevAct act, float *__restrict__ y, int ldy, uint32_t
       for (int t = 0; t < NT; t++) {
 #pragma unroll
         for (int m = 0; m < NM; m++) acc[m][r][t] = warp_sum_i64(acc[m][r][t]);
+        if (KS == 2) {   // (KS = 2 only with NM = 1, RPW = 1, NT = 1)
+          if (half == 1 && lane == 0) ks_part[pair] = acc[0][r][t];
+          asm volatile("bar.sync %0, 64;" ::"r"(1 + pair) : "memory");
+          if (half == 0) acc[0][r][t] += ks_part[pair];
+          asm volatile("bar.sync %0, 64;" ::"r"(1 + pair) : "memory");   // the slot is free again
+          if (half == 1) continue;
+        }
         if (lane == npend && row < rows) {
           pa = acc[0][r][t];
           pa2 = acc[NM - 1][r][t];
@@ -301,7 +316,10 @@ static cudaError_t gemv_launch(const DevQ4B &w, const DevQ4B &w2, const DevAct &
     occ_smem = smem;
   }
   const int ngroups = (w.rows + RPW - 1) / RPW;
-  int grid = (ngroups + GEMV_WARPS - 1) / GEMV_WARPS;
+  constexpr int NM = epi_pair(EPI) ? 2 : 1;
+  constexpr int KS = (NT == 1 && RPW == 1 && NM == 1 && NCH == 16) ? 2 : 1;   // as in k_gemv
+  constexpr int GPC = GEMV_WARPS / KS;                                      // row groups per CTA round
+  int grid = (ngroups + GPC - 1) / GPC;
   const int resident = nsm * occ;
   if (grid > resident) grid = resident;       // persistent: each warp walks several groups
   if (grid_limit > 0 && grid > grid_limit) grid = grid_limit;
