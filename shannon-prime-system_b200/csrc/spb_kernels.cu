@@ -122,14 +122,15 @@ k_gemv(DevQ4B w, DevQ4B w2, DevAct act, float *__restrict__ y, int ldy, uint32_t
   int32_t *xs = xw + NT * kw;                                               // [NT][nblk]
   double *dsc = reinterpret_cast<double *>(xs + ((NT * nblk + 1) & ~1));   // [NT]
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  // KS = 2 (single wide rows, e.g. the FFN down projection): the two warps of a pair take the
+  // KS = 2 (single rows of >= 8 code vectors per lane: the FFN down projection, the gate/up
+  // pair at K > 1024): the two warps of a pair take the
   // two halves of a row's 32-column blocks, so each holds half the code vectors (half the
   // registers: twice the resident warps); the odd warp hands its exact int64 half to the even
   // warp through shared memory under a 64-thread named barrier, and only even warps finish rows
-  constexpr int KS = (NT == 1 && RPW == 1 && NM == 1 && NCH == 16) ? 2 : 1;
+  constexpr int KS = (NT == 1 && RPW == 1 && NCH * NM >= 8) ? 2 : 1;
   constexpr int NCHW = NCH / KS;   // code vectors per lane per row held by one warp
   const int half = warp % KS, pair = warp / KS;
-  __shared__ int64_t ks_part[GEMV_WARPS / KS];
+  __shared__ int64_t ks_part[GEMV_WARPS / KS][NM];
   const int rows = w.rows;
   const size_t rstride = (size_t)(K >> 1);
   const int ngroups = (rows + RPW - 1) / RPW;
@@ -241,10 +242,14 @@ k_gemv(DevQ4B w, DevQ4B w2, DevAct act, float *__restrict__ y, int ldy, uint32_t
       for (int t = 0; t < NT; t++) {
 #pragma unroll
         for (int m = 0; m < NM; m++) acc[m][r][t] = warp_sum_i64(acc[m][r][t]);
-        if (KS == 2) {   // (KS = 2 only with NM = 1, RPW = 1, NT = 1)
-          if (half == 1 && lane == 0) ks_part[pair] = acc[0][r][t];
+        if (KS == 2) {   // (KS = 2 only with RPW = 1, NT = 1)
+#pragma unroll
+          for (int m = 0; m < NM; m++)
+            if (half == 1 && lane == 0) ks_part[pair][m] = acc[m][r][t];
           asm volatile("bar.sync %0, 64;" ::"r"(1 + pair) : "memory");
-          if (half == 0) acc[0][r][t] += ks_part[pair];
+#pragma unroll
+          for (int m = 0; m < NM; m++)
+            if (half == 0) acc[m][r][t] += ks_part[pair][m];
           asm volatile("bar.sync %0, 64;" ::"r"(1 + pair) : "memory");   // the slot is free again
           if (half == 1) continue;
         }
@@ -317,7 +322,7 @@ static cudaError_t gemv_launch(const DevQ4B &w, const DevQ4B &w2, const DevAct &
   }
   const int ngroups = (w.rows + RPW - 1) / RPW;
   constexpr int NM = epi_pair(EPI) ? 2 : 1;
-  constexpr int KS = (NT == 1 && RPW == 1 && NM == 1 && NCH == 16) ? 2 : 1;   // as in k_gemv
+  constexpr int KS = (NT == 1 && RPW == 1 && NCH * NM >= 8) ? 2 : 1;   // as in k_gemv
   constexpr int GPC = GEMV_WARPS / KS;                                      // row groups per CTA round
   int grid = (ngroups + GPC - 1) / GPC;
   const int resident = nsm * occ;

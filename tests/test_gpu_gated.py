@@ -23,7 +23,7 @@ def P(x):
 
 @pytest.mark.parametrize("m", [1, 2, 4, 8, 16])
 @pytest.mark.parametrize("act", [0, 1])
-@pytest.mark.parametrize("rows,cols", [(1536, 512), (4000, 3840)])
+@pytest.mark.parametrize("rows,cols", [(1536, 512), (4000, 3840), (512, 15360)])
 def test_gated_gemv(xr, spb, cuda_ok, m, act, rows, cols):
     import torch
     wg = spmodel.gen_matrix(1, "blk.0.ffn_gate.weight", rows, cols)
