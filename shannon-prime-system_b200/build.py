@@ -3,8 +3,9 @@
   libspb200.so     sm_100a kernels + runtime + C ABI (include/spb200.h)   -- nvcc
   libspb200_l1.so  section-6/6b binding to the reference's L1 ABI          -- gcc,
                    compiled against the reference's own headers
-                   (SPB_REF_INCLUDE, default /root/reference/include); skipped,
-                   with a note, when those headers are absent.
+                   (SPB_REF_INCLUDE; default: the `reference` tree beside this
+                   repository, <repo>/../reference/include); skipped, with a
+                   note, when those headers are absent.
 
 Run: python shannon-prime-system_b200/build.py [--force]
 """
@@ -22,7 +23,8 @@ OBJ = os.path.join(HERE, "_build")
 CORE_SO = os.path.join(HERE, "libspb200.so")
 L1_SO = os.path.join(HERE, "libspb200_l1.so")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
-REF_INCLUDE = os.environ.get("SPB_REF_INCLUDE", "/root/reference/include")
+REF_INCLUDE = os.environ.get("SPB_REF_INCLUDE",
+                             os.path.join(os.path.dirname(ROOT), "reference", "include"))
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVFLAGS = ["-std=c++17", "-O3", "-lineinfo", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr"] + ARCH
