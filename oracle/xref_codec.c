@@ -18,8 +18,10 @@
 #include "xref.h"
 
 #include <math.h>
+#include <pthread.h>
 #include <stdlib.h>
 #include <string.h>
+#include <unistd.h>
 
 float xref_f16_to_f32(uint16_t h) {
     uint32_t sign = (uint32_t)(h >> 15) & 1u;
@@ -92,28 +94,67 @@ void xref_quant_vec(const float *u, int n, int8_t *q, float *s) {
     *s = m;
 }
 
-void xref_matvec_q(const xref_q4b *w, const int8_t *q, const float *s, int n_tok, float *Y) {
+/* Rows are independent, so large matvecs are split over host threads (XREF_THREADS, default the
+ * online cores, at most 64); every output is the same integer whatever the split. */
+typedef struct {
+    const xref_q4b *w; const int8_t *q; const float *s; int n_tok; float *Y; int r0, r1;
+} mv_part;
+
+static void *matvec_rows(void *arg) {
+    const mv_part *p = (const mv_part *)arg;
+    const xref_q4b *w = p->w;
     const int K = w->cols, nib = (K + 1) / 2, nblk = (K + 31) / 32;
     int8_t *c = (int8_t *)malloc((size_t)K);
     int64_t *kk = (int64_t *)malloc((size_t)nblk * sizeof(int64_t));
-    if (!c || !kk) { free(c); free(kk); return; }
-    for (int j = 0; j < w->rows; j++) {
-        xref_unpack_q4(w->codes + (size_t)j * nib, K, c);
-        for (int b = 0; b < nblk; b++) (void)xref_f16_to_k(w->bscale[(size_t)j * nblk + b], &kk[b]);
-        for (int t = 0; t < n_tok; t++) {
-            const int8_t *x = q + (size_t)t * K;
-            int64_t acc = 0;
-            for (int b = 0; b < nblk; b++) {
-                int i0 = b * 32, i1 = i0 + 32 < K ? i0 + 32 : K;
-                int32_t isum = 0;
-                for (int i = i0; i < i1; i++) isum += (int32_t)c[i] * (int32_t)x[i];
-                acc += kk[b] * (int64_t)isum;
+    if (c && kk) {
+        for (int j = p->r0; j < p->r1; j++) {
+            xref_unpack_q4(w->codes + (size_t)j * nib, K, c);
+            for (int b = 0; b < nblk; b++) (void)xref_f16_to_k(w->bscale[(size_t)j * nblk + b], &kk[b]);
+            for (int t = 0; t < p->n_tok; t++) {
+                const int8_t *x = p->q + (size_t)t * K;
+                int64_t acc = 0;
+                for (int b = 0; b < nblk; b++) {
+                    int i0 = b * 32, i1 = i0 + 32 < K ? i0 + 32 : K;
+                    int32_t isum = 0;
+                    for (int i = i0; i < i1; i++) isum += (int32_t)c[i] * (int32_t)x[i];
+                    acc += kk[b] * (int64_t)isum;
+                }
+                double dsc = ((double)p->s[t] / 127.0) * 0x1p-24;
+                p->Y[(size_t)t * w->rows + j] = (float)((double)acc * dsc);
             }
-            double dsc = ((double)s[t] / 127.0) * 0x1p-24;
-            Y[(size_t)t * w->rows + j] = (float)((double)acc * dsc);
         }
     }
     free(c); free(kk);
+    return NULL;
+}
+
+static int mv_threads(void) {
+    static int n = 0;
+    if (!n) {
+        const char *e = getenv("XREF_THREADS");
+        long v = e ? strtol(e, NULL, 10) : sysconf(_SC_NPROCESSORS_ONLN);
+        n = v < 1 ? 1 : v > 64 ? 64 : (int)v;
+    }
+    return n;
+}
+
+void xref_matvec_q(const xref_q4b *w, const int8_t *q, const float *s, int n_tok, float *Y) {
+    int nt = mv_threads();
+    if ((int64_t)w->rows * w->cols * n_tok < (INT64_C(1) << 22)) nt = 1;
+    if (nt > w->rows) nt = w->rows;
+    mv_part parts[64];
+    pthread_t th[64];
+    int started[64] = {0};
+    for (int i = 0; i < nt; i++) {
+        parts[i] = (mv_part){w, q, s, n_tok, Y, (int)((int64_t)w->rows * i / nt),
+                             (int)((int64_t)w->rows * (i + 1) / nt)};
+        if (i > 0) started[i] = pthread_create(&th[i], NULL, matvec_rows, &parts[i]) == 0;
+    }
+    matvec_rows(&parts[0]);
+    for (int i = 1; i < nt; i++) {
+        if (started[i]) pthread_join(th[i], NULL);
+        else matvec_rows(&parts[i]);   /* no thread: this caller does the part */
+    }
 }
 
 int xref_matvec(const xref_q4b *w, const float *X, int n_tok, float *Y) {
