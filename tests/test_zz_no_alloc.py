@@ -29,7 +29,9 @@ def _p(t):
 
 def test_noalloc_gemv_matches_allocating_gemv_twice(spb, cuda_ok):
     import torch
-    cases = [(3840, 3840, 1, 11), (1000, 15360, 16, 12)]   # the second call exercises the size limit's edge
+    # the last case fills the fixed scratch exactly: 16 rows x 16384 columns = 262144 elements,
+    # the widest row the GEMV takes, so the scratch's last activation and block-sum bytes are used
+    cases = [(3840, 3840, 1, 11), (1000, 15360, 16, 12), (512, 16384, 16, 13)]
     for rows, cols, m, seed in cases:
         w = spmodel.gen_matrix(seed, "blk.0.ffn_down.weight", rows, cols)
         x = np.random.default_rng(seed).standard_normal((m, cols)).astype(np.float32)
@@ -45,6 +47,11 @@ def test_noalloc_gemv_matches_allocating_gemv_twice(spb, cuda_ok):
 def test_noalloc_gemv_rejects_oversize(spb, cuda_ok):
     import torch
     d = torch.zeros(1 << 20, dtype=torch.uint8, device="cuda")
-    rc = spb.spb_gemv_q4b_noalloc(_p(d), _p(d), 8, 32768, _p(d), 16, _p(d), None)
+    rc = spb.spb_gemv_q4b_noalloc(_p(d), _p(d), 8, 16384, _p(d), 32, _p(d), None)
+    assert rc == spb200.SPB_EBADARG                       # n_tok outside {1, 2, 4, 8, 16}
+    rc = spb.spb_gemv_q4b_noalloc(_p(d), _p(d), 8, 32768, _p(d), 1, _p(d), None)
+    assert rc == spb200.SPB_EBADARG                       # one row, but wider than the GEMV takes
+    assert b"16384-column limit" in spb.spb_last_error()
+    rc = spb.spb_gemv_q4b_noalloc(_p(d), _p(d), 8, 16416, _p(d), 16, _p(d), None)
     assert rc == spb200.SPB_EBADARG
-    assert b"exceeds the fixed scratch" in spb.spb_last_error()
+    assert b"16384-column limit" in spb.spb_last_error()
