@@ -57,10 +57,6 @@ def parse():
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-roofline", action="store_true")
-    p.add_argument("--decode-mode", type=int, default=None, choices=[0, 1],
-                   help="0: multi-kernel graph per step, 1: persistent kernel per step (default: the library's)")
-    p.add_argument("--trace", action="store_true",
-                   help="also print the persistent decode kernel's per-phase times (one extra step)")
     # profiling-size overrides (smaller device footprint for ncu captures); a line printed
     # with either set is not the configs[2] measurement and says so in config.workload
     p.add_argument("--layers", type=int, default=0)
@@ -86,6 +82,44 @@ def bench_config(args):
     if over:
         cfg = dataclasses.replace(cfg, name=cfg.name + "_profile", **over)
     return cfg
+
+
+def line_config(cfg, args, world):
+    """The config object both arms print (the same workload, so the driver can pair them)."""
+    return {"workload": f"{cfg.name} decode B=1 after a {args.prefill}-token prefill (BASELINE configs[2])",
+            "model": "Gemma-3-12B shape: 48L d3840 16/8 heads hd256 FFN15360 vocab262144 SWA1024 (5 of 6)"
+            if cfg.name == "gemma12b" else cfg.name,
+            "global_batch": world, "seq_len": args.prefill + args.warmup + args.steps,
+            "parallelism": f"sessions spread: {world} independent session(s), one per GPU",
+            "l2": "weights 6.6 GB per step >> 126 MB L2: every step streams from HBM"}
+
+
+def measure_config1_gpu(device):
+    """BASELINE configs[0] (tiny Gemma) on the GPU through the public session API, the same
+    steps as the CPU's unscaled config-1 run: spb_session_prefill of 64 tokens, then 64 greedy
+    spb_session_decode_step_argmax calls with the full-vocab logits copied to host memory."""
+    import torch
+    import spb200
+    import spmodel
+    cfg = spmodel.CONFIGS["tiny"]
+    m = spb200.Model.synthetic(cfg, seed=0, device=device)
+    toks = spmodel.gen_tokens(1, 64, cfg.n_vocab)
+    lg = np.empty(cfg.n_vocab, np.float32)
+    for rep in range(2):   # the first pass builds the step graph; the second is timed
+        s = m.session(64 + 64 + 8)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        out = s.prefill(toks)
+        t1 = time.perf_counter()
+        tok = int(out[-1].argmax())
+        for _ in range(64):
+            _, tok = s.step_argmax(tok, out=lg)
+        t2 = time.perf_counter()
+        s.close()
+    m.free()
+    return {"prefill_s": round(t1 - t0, 5), "decode_s": round(t2 - t1, 5),
+            "decode_tokens_per_s": round(64 / (t2 - t1), 1), "e2e_tokens_per_s": round(128 / (t2 - t0), 1),
+            "timing": "wall clock, host-buffer API (tokens in, every step's full-vocab logits out)"}
 
 
 def dist_env():
@@ -223,44 +257,6 @@ def gemv_roofline(cfg, spb, device, stream, iters=60):
     return out, tot_b, tot_t, launches
 
 
-PHASES = ["norm", "qkv_gemv", "barrier", "attention", "barrier", "quantize", "o_gemv", "barrier", "norm",
-          "gate_up_gemv", "barrier", "quantize", "down_gemv", "barrier"]
-
-
-def trace_report(tr, n_layers, sm_mhz=1965.0):
-    """Per-phase microseconds of one persistent decode step, averaged over the layers:
-    `cta0` from CTA 0's SM cycle counter (at sm_mhz), `spread` = latest minus earliest CTA
-    (%globaltimer) at the phase's end."""
-    t0 = tr[:, 0].astype(np.float64) * (1e3 / sm_mhz)   # cycles -> ns
-    late, early = tr[:, 1].astype(np.int64), tr[:, 2].astype(np.int64)
-    P = 24   # trace points per layer
-    out = {}
-    # phase ends of layer L: 1 + P L + i; the previous point of phase 0 is the previous layer's
-    # last phase end (or the kernel start)
-    prev = lambda L, i: 1 + P * L + i - 1 if i > 0 else (0 if L == 0 else 1 + P * (L - 1) + 13)
-    for i, name in enumerate(PHASES):
-        d = [(t0[1 + P * L + i] - t0[prev(L, i)]) / 1e3 for L in range(n_layers)]
-        sp = [(late[1 + P * L + i] - early[1 + P * L + i]) / 1e3 for L in range(n_layers)]
-        out[f"{i:02d}_{name}"] = {"cta0": round(float(np.mean(d)), 2), "spread": round(float(np.mean(sp)), 2)}
-    # inside attention (between the post-QKV barrier and the attention end) and the first norm
-    sub = {"attn_rope": (2, 14), "attn_scores": (14, 15), "attn_head_barrier1": (15, 16), "attn_exp": (16, 17),
-           "attn_vsum": (17, 18), "attn_head_barrier2": (18, 19), "attn_finalize": (19, 3),
-           "norm_inputs": (-1, 20), "norm_postnorm": (20, 21), "norm_residual": (21, 22), "norm_apply": (22, 23),
-           "norm_quantize": (23, 0)}
-    for name, (i0, i1) in sub.items():
-        d = []
-        for L in range(n_layers):
-            a_ = prev(L, 0) if i0 < 0 else 1 + P * L + i0
-            d.append((t0[1 + P * L + i1] - t0[a_]) / 1e3)
-        out[name] = round(float(np.mean(d)), 2)
-    last, f = 1 + P * (n_layers - 1) + 13, 1 + P * n_layers   # last layer's end; final norm point
-    out["final_norm"] = round((t0[f] - t0[last]) / 1e3, 2)
-    out["lm_head"] = round((t0[f + 1] - t0[f]) / 1e3, 2)
-    out["last_barrier"] = round((t0[f + 2] - t0[f + 1]) / 1e3, 2)
-    out["total"] = round((t0[f + 2] - t0[0]) / 1e3, 2)
-    return out
-
-
 def measure_batch(m, cfg, B, K, W, seed, max_over_ranks):
     """B independent sessions (seeded ragged contexts, U[128, 512] tokens each) decoding
     greedily together through spb_batch_decode_step: B*K tokens over the time of K steps
@@ -337,20 +333,6 @@ def measure_tp(cfg, args, rank, local, world, max_over_ranks, barrier, p2p=True)
                            f"logits all-gathered by NCCL"}
 
 
-def tile_report(tiles, pts):
-    """CTA 0's ring tiles: copy latency (issue -> found complete) and the gap between
-    consecutive issues, as percentiles, over the last 256 tiles of the step (the LM head)."""
-    t = tiles.astype(np.int64)
-    n = int(np.count_nonzero(t[:, 0]))
-    sel = t[max(0, n - 256):n]
-    lat = (sel[:, 1] - sel[:, 0]) / 1e3
-    gap = np.diff(sel[:, 0]) / 1e3
-    cons = np.diff(sel[:, 1]) / 1e3
-    q = lambda v: [round(float(np.percentile(v, x)), 2) for x in (10, 50, 90)]
-    return {"tiles": n, "latency_p10_50_90": q(lat), "issue_gap_p10_50_90": q(gap),
-            "consume_gap_p10_50_90": q(cons)}
-
-
 # ----------------------------------------------------------------------------- arms
 def run_spb(args):
     import torch
@@ -365,8 +347,6 @@ def run_spb(args):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
     spb = spb200.load()
-    if args.decode_mode is not None:
-        spb.spb_decode_mode(args.decode_mode)
     cfg = bench_config(args)
     K, W = args.steps, args.warmup
     pmax = args.prefill + W + K + 8
@@ -444,10 +424,6 @@ def run_spb(args):
                 "algorithmic_bytes_per_token": int(tot_b), "gemv_us_per_token": round(tot_us, 1),
                 "per_shape": shapes}
     clk = clocks.stop()
-    if args.trace and rank == 0:
-        pts, tiles = s.decode_trace(int(generated[-1]))
-        print(json.dumps({"decode_phase_trace_us": trace_report(pts, cfg.n_layers, clk.get("sm_mhz") or 1965.0),
-                          "tile_latency_us": tile_report(tiles, pts)}), file=sys.stderr)
 
     b64 = None
     if args.batch > 0:
@@ -460,13 +436,21 @@ def run_spb(args):
         tpr["nccl_only"] = measure_tp(cfg, args, rank, local, world, max_over_ranks, barrier, p2p=False)
 
     cpu = None
+    config1 = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         sys.path.insert(0, ORACLE)
         import cpu_baseline
         r = cpu_baseline.measure(cfg, procs=min(os.cpu_count() or 1, 32), steps=1)
         if r:
             cpu = {"value": round(r["value"], 5), "unit": "tokens/s", "cores": r["cores"], "kind": "reference",
-                   "sample": r["sample"]}
+                   "sample": r["sample"], "scaled": True, "scale": round(r["scale"], 3),
+                   "sample_step_s": round(r["sample_step_s_median"], 4),
+                   "per_core_tokens_per_s": round(r["per_core_tokens_per_s"], 6)}
+        # BASELINE configs[0], unscaled, CPU beside GPU
+        config1 = {"workload": "tiny (BASELINE configs[0]): prefill 64 + 64 greedy decode steps",
+                   "gpu": measure_config1_gpu(local),
+                   "cpu_reference": cpu_baseline.config1_e2e("reference"),
+                   "cpu_xref": cpu_baseline.config1_e2e("xref")}
 
     # embed; per layer norm, QKV, attention (QK-norm + RoPE + KV store fused; a separate
     # k_rope_kv with SPB_ROPE_FUSED=0), quantize, O, norm, gate/up, quantize, down; final norm,
@@ -497,19 +481,16 @@ def run_spb(args):
         "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": round(ms / K, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8xint4->int64 (exact)",
         "data": "synthetic (random-init OK_Q4B weights from a seed, uniform random tokens)",
-        "config": {"workload": f"{cfg.name} decode B=1 after a {args.prefill}-token prefill (BASELINE configs[2])",
-                   "model": "Gemma-3-12B shape: 48L d3840 16/8 heads hd256 FFN15360 vocab262144 SWA1024 (5 of 6)",
-                   "global_batch": world, "seq_len": args.prefill + W + K,
-                   "ctx_at_timing": [args.prefill + W, args.prefill + W + K],
-                   "parallelism": f"sessions spread: {world} independent session(s), one per GPU",
-                   "l2": "weights 6.6 GB per step >> 126 MB L2: every step streams from HBM",
-                   "weight_bytes_per_token": m.weight_bytes(), "prefill_s_untimed": round(prefill_s, 3)},
+        "config": line_config(cfg, args, world),
+        "ctx_at_timing": [args.prefill + W, args.prefill + W + K],
+        "weight_bytes_per_token": m.weight_bytes(), "prefill_s_untimed": round(prefill_s, 3),
         "e2e": {"value": round(world * K / (ms_e2e / 1e3), 3), "unit": "tokens/s", "h2d_bytes_per_step": 4,
                 "d2h_bytes_per_step": cfg.n_vocab * 4 + 4 + 4},
         "gpu_launches": kernels_per_step * K,
         "clocks": clk,
         "roofline": roof,
         "cpu_baseline": cpu,
+        "config1": config1,
         "b64": b64,
         "prefill": prefill,
     }
@@ -524,6 +505,11 @@ def run_spb(args):
 
 
 def run_reference(args):
+    """The reference arm: the reference's own CPU decode (oracle/_ref/libspref.so, compiled from
+    the reference sources) on all host cores. Each of the K timed steps is one decode token of
+    the 12B-width 1-layer sample in every process at once (ms_per_step = the slowest process's
+    wall time of that step, measured); `value` is the full model's tokens/s, the sample scaled by
+    streamed parameters (cpu_baseline.measure says what that leaves out). Rank 0 alone runs."""
     rank, _, world = dist_env()
     if rank != 0:
         return
@@ -532,24 +518,29 @@ def run_reference(args):
     import spmodel
     cfg = spmodel.CONFIGS[args.config]
     procs = os.cpu_count() or 1
-    # each step is one sampled token per process (a 1-layer slice, scaled); bounded to ~2 min
-    steps = max(1, min(args.steps, 8))
+    K, W = args.steps, args.warmup
     t0 = time.perf_counter()
-    r = cpu_baseline.measure(cfg, procs=procs, steps=steps)
+    r = cpu_baseline.measure(cfg, procs=procs, steps=K, warmup=W)
     wall = time.perf_counter() - t0
     if r is None:
         print(json.dumps({"impl": "reference", "unavailable": "reference library oracle/_ref/libspref.so not built"}))
         return
     v = round(r["value"], 5)
+    c1 = {"reference": cpu_baseline.config1_e2e("reference"), "xref": cpu_baseline.config1_e2e("xref")}
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "steps_sampled_per_process": steps,
-        "ms_per_step": round(1e3 / v, 1), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "f32", "data": "synthetic", "config": {"workload": f"{cfg.name} decode B=1 (BASELINE configs[2])",
-                                                        "model": cfg.name, "global_batch": 1},
+        "steps": K, "warmup": W, "ms_per_step": round(1e3 * sum(r["step_wall_s"]) / K, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (random-init OK_Q4B weights from a seed)",
+        "config": line_config(cfg, args, 1),
         "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": r["cores"], "kind": "reference",
-                         "sample": r["sample"]},
+                         "sample": r["sample"], "scaled": True, "scale": round(r["scale"], 3),
+                         "sample_step_s_median": round(r["sample_step_s_median"], 4),
+                         "per_core_tokens_per_s": round(r["per_core_tokens_per_s"], 6)},
+        "step_definition": "one sample decode token (12B widths, 1 layer, vocab 2048) in each of "
+                           f"{procs} concurrent processes; ms_per_step is measured, value is scaled",
         "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "config1_unscaled": c1,
         "wall_s": round(wall, 1)}), flush=True)
 
 

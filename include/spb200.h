@@ -100,22 +100,6 @@ int  spb_session_decode_step_argmax(spb_session *s, int32_t token, float *logits
 /* n_steps greedy steps entirely on the device (no host sync between steps): feeds
  * `token`, then each step's argmax; writes the n_steps argmaxes (host). */
 int  spb_session_decode_greedy(spb_session *s, int32_t token, int n_steps, int32_t *tokens_out);
-/* How decode steps run (process-wide): 0 = the multi-kernel schedule replayed as a CUDA
- * graph (default), 1 = one persistent cooperative kernel per step where the model shape
- * and context fit it. Any other value only queries. Returns the previous mode. Both give
- * byte-identical results. */
-int  spb_decode_mode(int mode);
-/* One decode step through the persistent kernel with its phase trace on (diagnostics):
- * out receives 3 * (2 + 24 * n_layers + 2) words, per trace point CTA 0's SM clock
- * cycles and the %globaltimer nanoseconds of the latest and of the earliest CTA. Points: kernel start; per
- * layer: norm, QKV GEMV, barrier, attention, barrier, quantize, O GEMV, barrier, norm,
- * gate/up GEMV, barrier, quantize, down GEMV, barrier (the phase ends), then inside
- * attention: RoPE, scores, head barrier, exponentials, V-sum, head barrier, and inside
- * the first norm: inputs, post-norm sum, residual sum, apply; then final norm, LM head,
- * barrier.
- * With cap >= that + 8192, the next 8192 words are CTA 0's first 4096 ring tiles as
- * (copy issued, found complete) time pairs. */
-int  spb_session_decode_trace(spb_session *s, int32_t token, uint64_t *out, int cap);
 /* One decode step for B (1..64) sessions of one model at once, each at its own position:
  * tokens[B] in, full-vocab logits [B][n_vocab] (host, or NULL) and the greedy argmaxes [B]
  * (host, or NULL) out, every position advanced by one. Same bytes as B separate
@@ -147,13 +131,35 @@ int spb_gemv_q4b(const uint8_t *codes, const uint16_t *bscale, int rows, int col
  * callers that may not call cudaMalloc, e.g. when the device memory is already owned by
  * another pool or a latency-critical path must avoid the allocator's implicit device sync).
  * Same arguments and bytes as spb_gemv_q4b. Its scratch is one fixed array inside the
- * library (about 288 KB per GPU, held until the process exits): n_tok * cols must be at most
- * 262144, else SPB_EBADARG. All calls on a device share that scratch, so calls that can
- * overlap on the GPU race; serialise them. The first call on a device sets up the scratch's
- * device address and should come before any stream capture. Inputs must be finite: this
- * variant does not report range errors. */
+ * library (about 288 KB per GPU, held until the process exits): cols must be at most 16384
+ * (the GEMV's widest row) and n_tok * cols at most 262144, else SPB_EBADARG before anything
+ * is launched. All calls on a device share that scratch, so calls that can overlap on the
+ * GPU race; serialise them. The first call on a device (and in each new context on it) sets
+ * up the scratch's device address and should come before any stream capture. Inputs must be
+ * finite: spb_gemv_q4b's range-error bits live in an allocated word (read by
+ * spb_take_device_errors), so this variant records none. */
 int spb_gemv_q4b_noalloc(const uint8_t *codes, const uint16_t *bscale, int rows, int cols,
                          const float *x, int n_tok, float *y, void *stream);
+/* A prepared OK_Q4B matrix in device memory (codes and bscale stay the caller's and must
+ * outlive the handle). Preparing replaces what matmul_arena redoes on every call
+ * (forward_dispatch.c:69-86: sp_arena_find, the per-row unpack) and the arena freeze
+ * (arena.c:28-31) with one pass over the block scales: the exact int64 accumulation bound
+ * is checked per row (SPB_ERANGE when a row breaks it, the test xref_q4b_check restates),
+ * and the scales are described for the kernels (the small-scale flag of the token-batch
+ * GEMM; per-row exponent shifts and the digit planes of the tensor-core GEMM). Stream-ordered
+ * on `stream`, then synchronises it. cols a multiple of 32, at most 16384; codes 16-byte
+ * aligned. */
+typedef struct spb_q4b_mat spb_q4b_mat;
+int  spb_q4b_prepare(const uint8_t *codes, const uint16_t *bscale, int rows, int cols, void *stream,
+                     spb_q4b_mat **out);
+void spb_q4b_release(spb_q4b_mat *m);
+/* out = {rows, cols, small-scale flag, digit planes (0: the tensor-core GEMM does not cover it)} */
+int  spb_q4b_info(const spb_q4b_mat *m, int32_t out[4]);
+/* y [n_tok][rows] = the exact OK_Q4B matmul of the f32 rows x [n_tok][cols] (device pointers), any
+ * n_tok >= 1: the sp_matmul of forward_dispatch.c:100-106 over the Q4B branch. Rows are quantized
+ * by sp_frob_quant1 over each row's max|x|; batches of 16 and more run the token-batch GEMM,
+ * fewer the dequant-GEMV; the bytes are the same either way. Uses the per-device workspace. */
+int  spb_q4b_matmul(const spb_q4b_mat *m, const float *x, int n_tok, float *y, void *stream);
 /* The activation quantizer alone: n_tok rows of cols floats -> the GEMV's input form:
  * q [n_tok][cols] int8 (per 8 columns: the 4 even then the 4 odd), bsum [n_tok][cols/32]
  * int32 block sums of q, scale [n_tok] f32 (max|x|). All device pointers. */
@@ -206,12 +212,21 @@ int  spb_tp_world(const spb_tp *tp);
 /* Optional, collective: a mailbox of `cap` 8-byte values per rank and exchange parity in this
  * rank's HBM, mapped into every rank through CUDA IPC; afterwards every exchange of at most cap
  * values (the decode step's) runs as one kernel over peer memory (stores over NVLink, a system
- * fence, a flag per rank, a wait bounded at 2 s that reports SPB_ERANGE "timeout" when a rank
+ * fence, a flag per rank, a wait bounded at 2 s that reports SPB_ECUDA "timeout" when a rank
  * does not arrive) instead of NCCL. init returns this rank's blob; connect takes all ranks'
  * blobs in rank order (SPB_TP_P2P_BLOB_BYTES each) and refuses two ranks on one GPU. */
 #define SPB_TP_P2P_BLOB_BYTES 80
 int  spb_tp_p2p_init(spb_tp *tp, int cap, uint8_t blob[SPB_TP_P2P_BLOB_BYTES]);
 int  spb_tp_p2p_connect(spb_tp *tp, const uint8_t *blobs);
+/* Diagnostics of the exchange kernel's bounded wait (no group needed): one exchange of n
+ * (<= 4096) int64 values through that kernel as rank 0 of a loopback group of `world` (2..8)
+ * mailboxes that all live on the current device. The sources outside absent_mask have arrived
+ * before the launch; those in it (never bit 0) never do, so the wait runs out after timeout_ms
+ * (1..10000) and the call returns SPB_ECUDA with "timeout" in spb_last_error(), the device and
+ * context staying usable. With absent_mask 0 it returns SPB_OK once the exact sum is checked.
+ * This is the failure contract of sp_status (SP_ECUDA, sp_status.h:19-56) for a peer that never
+ * arrives; a decode step whose exchange times out reports the same SPB_ECUDA. */
+int  spb_tp_p2p_loopback(int world, uint32_t absent_mask, int timeout_ms, int n);
 /* The rank's shard of the counter-generated model of spb_model_synthetic (same bytes as the
  * corresponding slices of the unsplit model), on the group's device. */
 int  spb_model_synthetic_tp(const spb_config *cfg, uint64_t seed, spb_tp *tp, spb_model **out);

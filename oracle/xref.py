@@ -143,6 +143,10 @@ class Xref:
             raise RuntimeError(f"xref_matvec rc={rc}")
         return Y
 
+    def q4b_check(self, t):
+        """0 when every row keeps the exact int64 accumulation bound, else -1 (xref_q4b_check)."""
+        return int(self.lib.xref_q4b_check(C.byref(_q4b(t, XQ4B))))
+
     def matvec_q(self, t, q, s):
         q = np.ascontiguousarray(q, np.int8).reshape(-1, t.cols); s = np.ascontiguousarray(s, np.float32)
         Y = np.empty((q.shape[0], t.rows), np.float32)

@@ -1,8 +1,6 @@
-// spb_device.cuh -- element-level device helpers shared by the multi-kernel schedule
-// (spb_kernels.cu) and the persistent decode-step kernel (spb_decode.cu): the OK_Q4B block
-// dot and block-scale accumulation, the RMSNorm island's per-element pieces, the CORDIC
-// rotation and the greedy-argmax key. Block-level reductions are not here: the two files
-// synchronise their threads differently.
+// spb_device.cuh -- element-level device helpers of the kernels: the OK_Q4B block dot and
+// block-scale accumulation, the RMSNorm island's per-element pieces, the CORDIC rotation and
+// the greedy-argmax key.
 #pragma once
 #include <cstdint>
 #include <cuda_fp16.h>

@@ -48,18 +48,6 @@ namespace spb {
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
-// SPB_GEMV_RING=1 sends batch-1 GEMVs to the TMA-ring kernel of spb_decode.cu instead of
-// k_gemv (identical results; at the 12B shape k_gemv is faster for every matrix but the LM
-// head, where the two tie, because its ramp is shorter)
-static bool ring_gemv_enabled() {
-  static int on = -1;
-  if (on < 0) {
-    const char *e = getenv("SPB_GEMV_RING");
-    on = (e && e[0] == '1') ? 1 : 0;
-  }
-  return on != 0;
-}
-
 static int pdl_enabled() {
   static int on = -1;
   if (on < 0) {
@@ -752,13 +740,6 @@ cudaError_t launch_gemv(const DevQ4B &w, const DevQ4B *w2, const DevAct &act, in
     return cudaSuccess;
   }
   const DevQ4B ww2 = w2 ? *w2 : w;
-  if (ntok == 1 && grid_limit == 0 && epi != EPI_I64 && ring_gemv_enabled()) {   // batch 1: the TMA-ring GEMV
-    const int mode = epi == EPI_GELU_MUL ? 1 : epi == EPI_SILU_MUL ? 2 : amax ? 3 : 0;
-    if (gemv_ring_covers(w, mode)) {
-      GemvRingArgs g{w, ww2, mode, act, y, ymax, amax, err};
-      return launch_gemv_ring(g, st, pdl_enabled() != 0);
-    }
-  }
   switch (epi) {
     case EPI_STORE: return gemv_nt<EPI_STORE>(w, ww2, act, ntok, y, ldy, err, ymax, amax, st, grid_limit);
     case EPI_GELU_MUL: return gemv_nt<EPI_GELU_MUL>(w, ww2, act, ntok, y, ldy, err, ymax, amax, st, grid_limit);
@@ -1791,20 +1772,51 @@ cudaError_t launch_embed(const DevQ4B &emb, const int32_t *tok_dev, int ntok, fl
   return cudaGetLastError();
 }
 
-// decode the keys left by the LM-head GEMV into token ids and clear them for the next step
-__global__ void k_scale_emax(const uint16_t *s, size_t n, int *out) {
-  int e = 0;
-  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
-    e = max(e, (int)((s[i] >> 10) & 31u));
-  e = warp_max_i32(e);
-  if ((threadIdx.x & 31) == 0) atomicMax(out, e);
+// one warp per row (8 rows per CTA); the int64 bound restates xref_q4b_check (the checker's
+// upload test): a lane saturates its partial sum at the limit, so the warp sum cannot wrap
+__global__ void __launch_bounds__(256) k_q4b_rowinfo(const uint16_t *scales, int rows, int nblk, uint8_t *shift,
+                                                     int *info) {
+  const int lane = threadIdx.x & 31, r = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (r >= rows) return;
+  const uint64_t lim = (1ull << 63) / (32u * 8u * 127u);
+  const uint16_t *row = scales + (size_t)r * nblk;
+  uint64_t sum = 0;
+  int bad = 0, emax = 0, smin = 64, smax = -1;
+  for (int b = lane; b < nblk; b += 32) {
+    const uint32_t h = row[b], e = (h >> 10) & 31u, mant = h & 1023u;
+    if (e == 31) { bad = 1; continue; }
+    const uint32_t m = e ? (mant | 1024u) : mant;
+    const int sh = e ? (int)e - 1 : 0;
+    sum += (uint64_t)m << sh;
+    if (sum >= lim) sum = lim;
+    emax = max(emax, (int)e);
+    if (m) { smin = min(smin, sh); smax = max(smax, sh); }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    bad |= __shfl_xor_sync(0xffffffffu, bad, o);
+    emax = max(emax, __shfl_xor_sync(0xffffffffu, emax, o));
+    smin = min(smin, __shfl_xor_sync(0xffffffffu, smin, o));
+    smax = max(smax, __shfl_xor_sync(0xffffffffu, smax, o));
+  }
+  if (lane == 0) {
+    if (bad || sum >= lim) atomicOr(info, 1);
+    atomicMax(info + 1, emax);
+    const int s0 = smax < 0 ? 0 : smin;
+    if (shift) shift[r] = (uint8_t)s0;
+    atomicMax(info + 2, smax < 0 ? 0 : smax - s0);
+  }
 }
 
-cudaError_t launch_scale_emax(const uint16_t *scales, size_t n, int *out, cudaStream_t st) {
-  k_scale_emax<<<296, 256, 0, st>>>(scales, n, out);
+cudaError_t launch_q4b_rowinfo(const uint16_t *scales, int rows, int nblk, uint8_t *shift, int *info,
+                               cudaStream_t st) {
+  if (rows <= 0 || nblk <= 0) return cudaErrorInvalidValue;
+  k_q4b_rowinfo<<<(rows + 7) / 8, 256, 0, st>>>(scales, rows, nblk, shift, info);
   return cudaGetLastError();
 }
 
+// decode the keys left by the LM-head GEMV into token ids and clear them for the next step
 __global__ void k_argmax_take(unsigned long long *keys, int ntok, int32_t *out) {
   pdl_trigger();
   pdl_wait();

@@ -25,10 +25,25 @@ struct DevQ4B {
   int rows, cols;
   int small;   // 1 when every block scale is below 128 in magnitude (f16 exponent field <= 21),
                // so each scale as the integer k = value * 2^24 fits in int32 (set after upload)
+  // Row facts for the tensor-core GEMM (set after upload with launch_q4b_rowinfo): shift[r] =
+  // the smallest exponent shift s = max(e - 1, 0) among row r's nonzero block scales, and
+  // planes = the 8-bit digit planes (2..4) that hold every weight code * mantissa *
+  // 2^(s_block - shift[r]) of the matrix as a two's-complement integer; 0 = not described.
+  const uint8_t *shift;
+  int planes;
 };
 
-// largest f16 exponent field among n block scales (device reduction, for DevQ4B::small)
-cudaError_t launch_scale_emax(const uint16_t *scales, size_t n, int *out, cudaStream_t st);
+// Per-row facts of an OK_Q4B matrix's block scales, one warp per row:
+//   shift[r]  as DevQ4B::shift (0 for a row without a nonzero block)
+//   info[0]  |= 1 when a row breaks the exact int64 accumulation bound (sum_b |k_b| * 32 * 8 * 127
+//               must stay below 2^63, k_b the scale as an integer times 2^24) or holds an inf/NaN
+//   info[1]   max= the largest f16 exponent field (DevQ4B::small iff <= 21)
+//   info[2]   max= the largest spread max_b s_b - shift[r] over nonzero blocks
+// info must be zero on entry.
+cudaError_t launch_q4b_rowinfo(const uint16_t *scales, int rows, int nblk, uint8_t *shift, int *info,
+                               cudaStream_t st);
+// digit planes for a spread (2, 3, 4), or 0 beyond what the tensor-core GEMM covers
+inline int q4b_planes_for_spread(int spread) { return spread <= 1 ? 2 : spread <= 9 ? 3 : spread <= 17 ? 4 : 0; }
 
 // A quantized activation set: NTOK rows of K int8 codes in the GEMV's interleaved
 // order (per 8-column group: even columns then odd columns), the per-32-block code
@@ -146,80 +161,6 @@ cudaError_t launch_synth_codes_cols(uint8_t *dst, int rows, size_t dst_row_bytes
 cudaError_t launch_synth_scales_cols(uint16_t *dst, int rows, int nblk_dst, int nblk_src, int blk_off,
                                     int exp_field, uint64_t key, cudaStream_t st);
 cudaError_t launch_synth_norm(float *dst, int n, uint64_t key, cudaStream_t st);
-
-// ---- the decode step as one persistent kernel (spb_decode.cu) ----
-// Weights and tables of one layer as the persistent kernel reads them (a device array of
-// n_layers entries, built once per model).
-struct DecLayer {
-  DevQ4B qkv, o, g, u, d;
-  const float *attn_norm, *post_attn, *ffn_norm, *post_ffw;
-  const float *q_norm, *k_norm;   // nullable when the model has no QK-norm
-  const uint64_t *W;              // CORDIC turn table of this layer's RoPE base [HD/2]
-  int win;                        // sliding window, -1 for global attention
-  int pad_;
-};
-
-struct DecodeArgs {
-  const DecLayer *layers;         // device [NL]
-  DevQ4B embd, out;
-  const float *out_norm;
-  const uint64_t *T;              // CORDIC arctangent table [30]
-  uint64_t gain;
-  int NL, E, FF, NH, NKV, HD, QD, KVD, V, P, gemma;
-  float es, ascale;
-  int32_t *kc, *vc;               // KV cache base, [NL][NKV][P][HD]
-  size_t kvl;                     // elements per layer of the cache
-  int32_t *pos_dev, *tok_dev, *argmax_dev;   // position in, token in / next token out
-  float *x2;                      // [2][E] residual ping-pong
-  float *qkv, *ao, *ap, *gg, *dn, *logits;
-  uint32_t *slots;                // [NL][2] max |attention out|, max |gate*up| (f32 bits); zero on entry
-  int32_t *pmx;                   // [grid][G] per-CTA attention partial maxima
-  int64_t *psum;                  // [grid][G] per-CTA exponential sums
-  uint64_t *pnum;                 // [grid][G][HD][2] per-CTA 128-bit V-sums (lo, hi)
-  uint32_t *sync;                 // [(3 + NKV) * 32] counters (zero on entry, reset by the kernel)
-  unsigned long long *amax;       // greedy-argmax key (zero on entry, cleared by the kernel)
-  uint32_t *err;
-  // nullable: per trace point k, [k][0] = CTA 0's %globaltimer, [k][1] = the latest and
-  // [k][2] = the earliest CTA (host-initialised to 0 and ~0)
-  unsigned long long *trace;
-};
-// trace points (column 0: CTA 0's SM clock cycles; 1, 2: %globaltimer ns of the latest and
-// the earliest CTA): DEC_TRACE_PER_LAYER per layer (14 phase ends, then 6 inside attention and 4
-// inside the first norm), then the final norm, LM head, last barrier; after the points, CTA
-// 0's per-tile record [DEC_TRACE_TILES][2]: the time the producer issued the tile's copy and
-// the time warp 0 found it complete
-constexpr int DEC_TRACE_PER_LAYER = 24;
-constexpr int DEC_TRACE_TILES = 4096;
-__host__ __device__ inline int decode_trace_points(int nl) { return 1 + nl * DEC_TRACE_PER_LAYER + 3; }
-__host__ __device__ inline int decode_trace_words(int nl) { return 3 * decode_trace_points(nl) + 2 * DEC_TRACE_TILES; }
-
-// words of DecodeArgs::sync: the grid counter, the exit counter, the abort word, then one
-// counter per KV head, each on its own 128-byte line
-constexpr int DEC_SYNC_WORDS_PER = 32;
-inline int decode_sync_words(int nkv) { return (3 + nkv) * DEC_SYNC_WORDS_PER; }
-
-// Whether the persistent kernel covers this model shape and context length on `grid` CTAs
-// (one per SM); 0 if so, else a reason string.
-const char *decode_unsupported(const DecodeArgs &a, int grid, int ctx);
-// CTAs the persistent kernel runs with on the current device (0 if it cannot be resident)
-int decode_grid();
-cudaError_t launch_decode(const DecodeArgs &a, int grid, cudaStream_t st);
-
-// ---- batch-1 GEMV through a TMA ring (spb_decode.cu): one CTA per SM, a producer warp
-// streaming the CTA's row tiles, 16 consumer warps. mode 0: y = W x; 1 / 2: y = gelu / silu
-// (W x) * (W2 x) with the per-row max |y| folded into ymax; 3: LM head, y = W x and the
-// greedy-argmax key folded into amax (zero on entry). act: one quantized row.
-struct GemvRingArgs {
-  DevQ4B w, w2;
-  int mode;
-  DevAct act;
-  float *y;
-  uint32_t *ymax;
-  unsigned long long *amax;
-  uint32_t *err;
-};
-bool gemv_ring_covers(const DevQ4B &w, int mode);
-cudaError_t launch_gemv_ring(const GemvRingArgs &g, cudaStream_t st, bool pdl);
 
 // store `msg` as this thread's spb_last_error() text and return `code` (host runtime)
 int record_error(int code, const char *msg);

@@ -62,7 +62,7 @@ static const char *err_bits_text(uint32_t b) {
   if (b & ERR_ROPE_RANGE) return "q/k outside the exact RoPE range (|x| < 256)";
   if (b & ERR_V_RANGE) return "v outside the exact range (|v| < 16384)";
   if (b & ERR_SCORE_RANGE) return "attention score outside the exact range (|z| < 2^17)";
-  if (b & ERR_TIMEOUT) return "a bounded wait on an asynchronous copy gave up";
+  if (b & ERR_TIMEOUT) return "a bounded wait gave up (timeout)";
   return "unknown";
 }
 
@@ -177,15 +177,15 @@ struct spb_model {
   uint64_t gain = 0;
   float es = 1.0f;
   int64_t stream_bytes = 0;
-  DecLayer *dec_layers = nullptr;   // device [NL]: the persistent decode kernel's view of the layers
   // tensor parallel: this rank's shard (NH, NKV, FF local; V = its LM-head rows [vbase, vbase+V)
   // of Vfull); without a group Vfull == V and vbase == 0
   spb_tp *tp = nullptr;
   int Vfull = 0, vbase = 0;
   bool out_sep = false;   // the LM head has its own storage (untied, or a vocabulary slice)
+  uint8_t *shifts = nullptr;   // every matrix's DevQ4B::shift rows (one allocation)
 };
 
-static int mark_small_scales(spb_model *m);
+static int describe_matrices(spb_model *m);
 
 static size_t q4b_bytes(int rows, int cols) { return (size_t)rows * (cols / 2) + (size_t)rows * (cols / 32) * 2; }
 
@@ -277,22 +277,6 @@ static int model_alloc(const spb_config &c, int device, spb_model **out, int nv_
   if (rc) { cudaFree(m->wbuf); delete m; return rc; }
   e = cudaMemcpy(m->tabs, ht.data(), ht.size() * 8, cudaMemcpyHostToDevice);
   if (e != cudaSuccess) { cudaFree(m->wbuf); delete m; return set_err(SPB_ECUDA, "spb_model: tables: %s", cudaGetErrorString(e)); }
-  {
-    std::vector<DecLayer> dl(m->NL);
-    for (int L = 0; L < m->NL; L++) {
-      const DevLayer &d = m->layers[L];
-      dl[L] = DecLayer{d.qkv, d.o, d.g, d.u, d.d, d.attn_norm, d.post_attn, d.ffn_norm, d.post_ffw,
-                       d.q_norm, d.k_norm, m->tabs + 32 + (d.global ? 0 : m->HD / 2), d.win, 0};
-    }
-    e = cudaMalloc(&m->dec_layers, sizeof(DecLayer) * m->NL);
-    if (e == cudaSuccess) e = cudaMemcpy(m->dec_layers, dl.data(), sizeof(DecLayer) * m->NL, cudaMemcpyHostToDevice);
-    if (e != cudaSuccess) {
-      cudaFree(m->dec_layers);
-      cudaFree(m->wbuf);
-      delete m;
-      return set_err(SPB_ECUDA, "spb_model: layer table: %s", cudaGetErrorString(e));
-    }
-  }
   m->stream_bytes = (int64_t)m->NL * (int64_t)(q4b_bytes(QKV, m->E) + q4b_bytes(m->E, m->QD) +
                                               2 * q4b_bytes(m->FF, m->E) + q4b_bytes(m->E, m->FF)) +
                     (int64_t)q4b_bytes(m->V, m->E);
@@ -381,7 +365,7 @@ static int upload_fill(spb_model *m, const spb_model_desc *desc, const int32_t *
   if (m->out_sep)
     PUT(put_q4b_part(m->gemma ? desc->token_embd : desc->output, m->Vfull, E, v0, m->V, 0, E, m->out, 0, "output"));
   PUT(put_f32(desc->output_norm, m->out_norm, m->E, "output_norm"));
-  PUT(mark_small_scales(m));
+  PUT(describe_matrices(m));
 #undef PUT
   return SPB_OK;
 }
@@ -423,25 +407,39 @@ extern "C" int spb_model_upload_tp(const spb_model_desc *desc, spb_tp *tp, spb_m
   return SPB_OK;
 }
 
-// Mark the matrices whose block scales are all below 128 (DevQ4B::small): the token-batch
-// GEMM then accumulates each block with one widening multiply-add.
-static int mark_small_scales(spb_model *m) {
+// Describe every matrix's block scales once (launch_q4b_rowinfo): the exact-range check, the
+// small-scale flag of the token-batch GEMM and the per-row shifts and digit planes of the
+// tensor-core GEMM. A matrix outside the exact int64 bound is refused with SPB_ERANGE.
+static int describe_matrices(spb_model *m) {
   std::vector<DevQ4B *> ws;
   for (DevLayer &d : m->layers) {
     ws.push_back(&d.qkv); ws.push_back(&d.o); ws.push_back(&d.g); ws.push_back(&d.u); ws.push_back(&d.d);
   }
   ws.push_back(&m->embd);
   if (m->out_sep) ws.push_back(&m->out);
+  size_t nrows = 0;
+  for (DevQ4B *w : ws) nrows += ((size_t)w->rows + 255) & ~(size_t)255;
+  cudaFree(m->shifts);
+  m->shifts = nullptr;
   int *dev = nullptr;
-  CU(cudaMalloc(&dev, ws.size() * sizeof(int)));
-  cudaError_t e = cudaMemset(dev, 0, ws.size() * sizeof(int));
-  for (size_t i = 0; i < ws.size() && e == cudaSuccess; i++)
-    e = launch_scale_emax(ws[i]->scales, (size_t)ws[i]->rows * (ws[i]->cols / 32), dev + i, 0);
-  std::vector<int> emax(ws.size(), 31);
-  if (e == cudaSuccess) e = cudaMemcpy(emax.data(), dev, ws.size() * sizeof(int), cudaMemcpyDeviceToHost);
+  CU(cudaMalloc(&m->shifts, nrows));
+  CU(cudaMalloc(&dev, ws.size() * 4 * sizeof(int)));
+  cudaError_t e = cudaMemset(dev, 0, ws.size() * 4 * sizeof(int));
+  size_t off = 0;
+  for (size_t i = 0; i < ws.size() && e == cudaSuccess; i++) {
+    ws[i]->shift = m->shifts + off;
+    e = launch_q4b_rowinfo(ws[i]->scales, ws[i]->rows, ws[i]->cols / 32, m->shifts + off, dev + 4 * i, 0);
+    off += ((size_t)ws[i]->rows + 255) & ~(size_t)255;
+  }
+  std::vector<int> info(ws.size() * 4, 0);
+  if (e == cudaSuccess) e = cudaMemcpy(info.data(), dev, info.size() * sizeof(int), cudaMemcpyDeviceToHost);
   cudaFree(dev);
   if (e != cudaSuccess) return set_err(SPB_ECUDA, "spb_model: scale check: %s", cudaGetErrorString(e));
-  for (size_t i = 0; i < ws.size(); i++) ws[i]->small = emax[i] <= 21 ? 1 : 0;
+  for (size_t i = 0; i < ws.size(); i++) {
+    if (info[4 * i]) return set_err(SPB_ERANGE, "spb_model: block scales exceed the exact int64 accumulation bound");
+    ws[i]->small = info[4 * i + 1] <= 21 ? 1 : 0;
+    ws[i]->planes = q4b_planes_for_spread(info[4 * i + 2]);
+  }
   if (!m->out_sep) m->out = m->embd;
   return SPB_OK;
 }
@@ -511,7 +509,7 @@ static int synth_fill(spb_model *m, const spb_config &full, uint64_t seed, const
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
     if (e != cudaSuccess) rc = set_err(SPB_ECUDA, "synth: %s", cudaGetErrorString(e));
   }
-  if (!rc) rc = mark_small_scales(m);
+  if (!rc) rc = describe_matrices(m);
   return rc;
 }
 
@@ -546,8 +544,8 @@ extern "C" int spb_model_synthetic_tp(const spb_config *cfg, uint64_t seed, spb_
 extern "C" void spb_model_free(spb_model *m) {
   if (!m) return;
   cudaSetDevice(m->device);
-  cudaFree(m->dec_layers);
   cudaFree(m->wbuf);
+  cudaFree(m->shifts);
   delete m;
 }
 
@@ -575,9 +573,6 @@ struct spb_session {
   BatchRow *h_rows = nullptr;     // pinned staging for rows_dev
   int32_t *h_argmax = nullptr;    // pinned [NT_MAX] batch argmaxes
   cudaGraphExec_t step_graph = nullptr;
-  int dgrid = 0;                  // CTAs of the persistent decode kernel (0: not available)
-  DecodeArgs dargs{};             // its arguments (fixed for the session's lifetime)
-  unsigned long long *trace_dev = nullptr;   // phase trace of the persistent kernel (on request)
   // tensor parallel: int64 partial sums of the K-split matrices [NT_MAX][E], this rank's LM-head
   // logits [NT_MAX][V] and the all-gathered slices [world][NT_MAX][V]
   int64_t *y64 = nullptr;
@@ -585,23 +580,6 @@ struct spb_session {
   int64_t *ws = nullptr;          // split-K workspace of the token-batch GEMM [2][NT_MAX][E]
   size_t ws_elems = 0;
 };
-
-// 1: decode steps run as the persistent kernel where it covers the shape; 0 (default, the
-// faster of the two at the 12B shape today): always the multi-kernel graph
-static int g_decode_mode = 0;
-
-extern "C" int spb_decode_mode(int mode) {
-  const int prev = g_decode_mode;
-  if (mode == 0 || mode == 1) g_decode_mode = mode;
-  return prev;
-}
-
-// the persistent kernel can serve a step whose new token lands at position `pos`
-static bool decode_kernel_covers(const spb_session *s, int pos) {
-  return s->dgrid > 0 && !s->m->tp && decode_unsupported(s->dargs, s->dgrid, pos + 1) == nullptr;
-}
-// ... and is selected for it
-static bool use_decode_kernel(const spb_session *s, int pos) { return g_decode_mode == 1 && decode_kernel_covers(s, pos); }
 
 static size_t kv_layer_elems(const spb_model *m, int pmax) { return (size_t)m->NKV * pmax * m->HD; }
 
@@ -631,13 +609,6 @@ extern "C" int spb_session_open(spb_model *m, int pmax, spb_session **out) {
   const size_t o_hist = take((size_t)pmax * 4), o_err = take(4), o_slots = take(2 * NT_MAX * 4);
   const size_t o_keys = take(NT_MAX * 8);
   const size_t o_rows = take(NT_MAX * sizeof(BatchRow));
-  const int G = m->NH / m->NKV;
-  s->dgrid = decode_grid();
-  (void)cudaGetLastError();
-  const int dg = std::max(s->dgrid, 1);
-  const size_t o_dsync = take((size_t)decode_sync_words(m->NKV) * 4), o_dslots = take((size_t)m->NL * 2 * 4);
-  const size_t o_pmx = take((size_t)dg * G * 4), o_psum = take((size_t)dg * G * 8);
-  const size_t o_pnum = take((size_t)dg * G * m->HD * 16);
   cudaError_t e = cudaMalloc(&s->buf, off);
   if (e != cudaSuccess) { delete s; return set_err(SPB_EOOM, "spb_session_open: cudaMalloc(%zu): %s", off, cudaGetErrorString(e)); }
   uint8_t *B = s->buf;
@@ -658,20 +629,6 @@ extern "C" int spb_session_open(spb_model *m, int pmax, spb_session **out) {
     s->logits_l = (float *)(B + o_lgl);
     s->logits_g = (float *)(B + o_lgg);
   }
-  {
-    DecodeArgs &a = s->dargs;
-    a.layers = m->dec_layers; a.embd = m->embd; a.out = m->out; a.out_norm = m->out_norm;
-    a.T = m->tabs; a.gain = m->gain;
-    a.NL = m->NL; a.E = E; a.FF = m->FF; a.NH = m->NH; a.NKV = m->NKV; a.HD = m->HD; a.QD = m->QD;
-    a.KVD = m->KVD; a.V = m->V; a.P = pmax; a.gemma = m->gemma ? 1 : 0;
-    a.es = m->es; a.ascale = 1.0f / sqrtf((float)m->HD);
-    a.kc = s->kc; a.vc = s->vc; a.kvl = kv_layer_elems(m, pmax);
-    a.pos_dev = s->pos_dev; a.tok_dev = s->tok_dev; a.argmax_dev = s->argmax_dev;
-    a.x2 = s->x; a.qkv = s->qkv; a.ao = s->ao; a.ap = s->ap; a.gg = s->gg; a.dn = s->dn; a.logits = s->logits;
-    a.slots = (uint32_t *)(B + o_dslots); a.pmx = (int32_t *)(B + o_pmx); a.psum = (int64_t *)(B + o_psum);
-    a.pnum = (uint64_t *)(B + o_pnum); a.sync = (uint32_t *)(B + o_dsync); a.amax = s->amax_keys;
-    a.err = s->err_dev;
-  }
   e = cudaStreamCreateWithFlags(&s->st, cudaStreamNonBlocking);
   if (e == cudaSuccess) e = cudaMallocHost(&s->h_pinned, (NT_MAX + 4) * 4);
   if (e == cudaSuccess) e = cudaMallocHost(&s->h_rows, NT_MAX * sizeof(BatchRow));
@@ -688,7 +645,6 @@ extern "C" void spb_session_close(spb_session *s) {
   cudaSetDevice(s->m->device);
   if (s->st) cudaStreamSynchronize(s->st);
   if (s->step_graph) cudaGraphExecDestroy(s->step_graph);
-  cudaFree(s->trace_dev);
   if (s->st) cudaStreamDestroy(s->st);
   cudaFreeHost(s->h_pinned);
   cudaFreeHost(s->h_rows);
@@ -813,6 +769,9 @@ static int collect_errors(spb_session *s) {
   CU(cudaMemcpyAsync(h, s->err_dev, 4, cudaMemcpyDeviceToHost, s->st));
   CU(cudaMemsetAsync(s->err_dev, 0, 4, s->st));
   CU(cudaStreamSynchronize(s->st));
+  // a bounded device wait that gave up is a device failure (SP_ECUDA), every other bit a value
+  // that left the exact range
+  if (*h & ERR_TIMEOUT) return set_err(SPB_ECUDA, "spb: %s (error bits 0x%x)", err_bits_text(ERR_TIMEOUT), *h);
   if (*h) return set_err(SPB_ERANGE, "spb: %s (error bits 0x%x)", err_bits_text(*h), *h);
   return SPB_OK;
 }
@@ -871,53 +830,16 @@ extern "C" int spb_session_decode_step_argmax(spb_session *s, int32_t token, flo
   if (!s) return set_err(SPB_EBADARG, "spb_session_decode_step: null session");
   if (s->pos >= s->pmax) return set_err(SPB_ECONTEXT_FULL, "spb_session_decode_step: context full");
   CU(cudaSetDevice(s->m->device));
-  const bool persistent = use_decode_kernel(s, s->pos);
-  int rc = persistent ? SPB_OK : ensure_step_graph(s);
+  int rc = ensure_step_graph(s);
   if (rc) return rc;
   s->h_pinned[0] = token;
   CU(cudaMemcpyAsync(s->tok_dev, s->h_pinned, 4, cudaMemcpyHostToDevice, s->st));
-  if (persistent && launch_decode(s->dargs, s->dgrid, s->st) != cudaSuccess) {
-    // the cooperative launch did not fit beside other work on the device: this session
-    // falls back to the multi-kernel schedule from here on
-    (void)cudaGetLastError();
-    s->dgrid = 0;
-    rc = ensure_step_graph(s);
-    if (rc) return rc;
-    CU(cudaGraphLaunch(s->step_graph, s->st));
-  } else if (!persistent) {
-    CU(cudaGraphLaunch(s->step_graph, s->st));
-  }
+  CU(cudaGraphLaunch(s->step_graph, s->st));
   if (logits) CU(cudaMemcpyAsync(logits, s->logits, (size_t)s->m->Vfull * 4, cudaMemcpyDeviceToHost, s->st));
   if (argmax) CU(cudaMemcpyAsync(s->h_pinned + NT_MAX + 1, s->argmax_dev, 4, cudaMemcpyDeviceToHost, s->st));
   rc = collect_errors(s);
   if (rc) { sync_pos(s); cudaStreamSynchronize(s->st); return rc; }
   if (argmax) *argmax = s->h_pinned[NT_MAX + 1];
-  s->pos += 1;
-  return SPB_OK;
-}
-
-// One persistent decode step with the phase trace on: out receives decode_trace_points(NL)
-// triples (CTA 0 time, latest CTA, earliest CTA) of %globaltimer nanoseconds.
-extern "C" int spb_session_decode_trace(spb_session *s, int32_t token, uint64_t *out, int cap) {
-  if (!s || !out) return set_err(SPB_EBADARG, "spb_session_decode_trace: bad arg");
-  const int np = decode_trace_points(s->m->NL), nw = decode_trace_words(s->m->NL);
-  if (cap < 3 * np) return set_err(SPB_EBADARG, "spb_session_decode_trace: need %d words", 3 * np);
-  if (s->pos >= s->pmax) return set_err(SPB_ECONTEXT_FULL, "spb_session_decode_trace: context full");
-  CU(cudaSetDevice(s->m->device));
-  if (!decode_kernel_covers(s, s->pos))
-    return set_err(SPB_EUNSUPPORTED, "spb_session_decode_trace: the persistent kernel does not serve this step");
-  if (!s->trace_dev) CU(cudaMalloc(&s->trace_dev, (size_t)nw * 8));
-  std::vector<uint64_t> init((size_t)nw, 0ull);
-  for (int k = 0; k < np; k++) init[3 * k + 2] = ~0ull;
-  CU(cudaMemcpy(s->trace_dev, init.data(), init.size() * 8, cudaMemcpyHostToDevice));
-  s->h_pinned[0] = token;
-  CU(cudaMemcpyAsync(s->tok_dev, s->h_pinned, 4, cudaMemcpyHostToDevice, s->st));
-  DecodeArgs a = s->dargs;
-  a.trace = s->trace_dev;
-  CU(launch_decode(a, s->dgrid, s->st));
-  CU(cudaMemcpyAsync(out, s->trace_dev, (size_t)std::min(cap, nw) * 8, cudaMemcpyDeviceToHost, s->st));
-  int rc = collect_errors(s);
-  if (rc) { sync_pos(s); cudaStreamSynchronize(s->st); return rc; }
   s->pos += 1;
   return SPB_OK;
 }
@@ -972,14 +894,12 @@ extern "C" int spb_session_decode_greedy(spb_session *s, int32_t token, int n_st
   if (n_steps > s->pmax - s->pos) return set_err(SPB_ECONTEXT_FULL, "spb_session_decode_greedy: context full");
   if (n_steps == 0) return SPB_OK;
   CU(cudaSetDevice(s->m->device));
-  int rc = SPB_OK;
-  if (!use_decode_kernel(s, s->pos) || !use_decode_kernel(s, s->pos + n_steps - 1)) rc = ensure_step_graph(s);
+  int rc = ensure_step_graph(s);
   if (rc) return rc;
   s->h_pinned[0] = token;
   CU(cudaMemcpyAsync(s->tok_dev, s->h_pinned, 4, cudaMemcpyHostToDevice, s->st));
   for (int i = 0; i < n_steps; i++) {
-    if (use_decode_kernel(s, s->pos + i)) CU(launch_decode(s->dargs, s->dgrid, s->st));
-    else CU(cudaGraphLaunch(s->step_graph, s->st));
+    CU(cudaGraphLaunch(s->step_graph, s->st));
     // after the step, tok_dev holds this step's argmax (the graph's last node copies it)
     CU(cudaMemcpyAsync(s->hist_dev + s->pos + i, s->tok_dev, 4, cudaMemcpyDeviceToDevice, s->st));
   }
@@ -1089,6 +1009,84 @@ extern "C" int spb_gemv_q4b(const uint8_t *codes, const uint16_t *bscale, int ro
   CU(launch_quant(x, cols, cols, n_tok, act, nullptr, err, st));
   DevQ4B w{codes, bscale, rows, cols};
   CU(launch_gemv(w, nullptr, act, n_tok, y, rows, EPI_STORE, err, st));
+  return SPB_OK;
+}
+
+// ---- a prepared matrix: the block scales described once, then any number of token rows
+struct spb_q4b_mat {
+  int device;
+  DevQ4B w;
+  uint8_t *shift;   // device [rows]
+};
+
+extern "C" int spb_q4b_prepare(const uint8_t *codes, const uint16_t *bscale, int rows, int cols, void *stream,
+                               spb_q4b_mat **out) {
+  if (!out) return set_err(SPB_EBADARG, "spb_q4b_prepare: null out");
+  *out = nullptr;
+  if (!codes || !bscale || rows <= 0 || cols <= 0 || (cols & 31) || cols > 16384)
+    return set_err(SPB_EBADARG, "spb_q4b_prepare: bad arg (cols a positive multiple of 32, at most 16384)");
+  if ((uintptr_t)codes & 15) return set_err(SPB_EBADARG, "spb_q4b_prepare: codes must be 16-byte aligned");
+  int dev = 0;
+  CU(cudaGetDevice(&dev));
+  cudaStream_t st = (cudaStream_t)stream;
+  uint8_t *buf = nullptr;
+  const size_t sh_bytes = ((size_t)rows + 255) & ~(size_t)255;
+  CU(cudaMalloc(&buf, sh_bytes + 16));
+  int *info = reinterpret_cast<int *>(buf + sh_bytes);
+  int h[4] = {0, 0, 0, 0};
+  cudaError_t e = cudaMemsetAsync(info, 0, 16, st);
+  if (e == cudaSuccess) e = launch_q4b_rowinfo(bscale, rows, cols / 32, buf, info, st);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(h, info, 16, cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) {
+    cudaFree(buf);
+    return set_err(SPB_ECUDA, "spb_q4b_prepare: %s", cudaGetErrorString(e));
+  }
+  if (h[0]) {
+    cudaFree(buf);
+    return set_err(SPB_ERANGE, "spb_q4b_prepare: block scales exceed the exact int64 accumulation bound "
+                               "(or hold inf/NaN)");
+  }
+  spb_q4b_mat *m = new spb_q4b_mat();
+  m->device = dev;
+  m->shift = buf;
+  m->w = DevQ4B{codes, bscale, rows, cols, h[1] <= 21 ? 1 : 0, buf, q4b_planes_for_spread(h[2])};
+  *out = m;
+  return SPB_OK;
+}
+
+extern "C" void spb_q4b_release(spb_q4b_mat *m) {
+  if (!m) return;
+  cudaFree(m->shift);
+  delete m;
+}
+
+extern "C" int spb_q4b_info(const spb_q4b_mat *m, int32_t out[4]) {
+  if (!m || !out) return set_err(SPB_EBADARG, "spb_q4b_info: null arg");
+  out[0] = m->w.rows;
+  out[1] = m->w.cols;
+  out[2] = m->w.small;
+  out[3] = m->w.planes;
+  return SPB_OK;
+}
+
+extern "C" int spb_q4b_matmul(const spb_q4b_mat *m, const float *x, int n_tok, float *y, void *stream) {
+  if (!m || !x || !y || n_tok <= 0) return set_err(SPB_EBADARG, "spb_q4b_matmul: bad arg");
+  const int rows = m->w.rows, cols = m->w.cols;
+  // quantized rows, their block sums and scales, then the split-K workspace of the token-batch GEMM
+  const size_t qb = ((size_t)n_tok * cols + 255) & ~(size_t)255;
+  const size_t bb = ((size_t)n_tok * (cols / 32) * 4 + 255) & ~(size_t)255;
+  const size_t sb = ((size_t)n_tok * 4 + 255) & ~(size_t)255;
+  const size_t ws_elems = (size_t)2 * 64 * rows;
+  uint8_t *wb;
+  uint32_t *err;
+  int rc = work_get(qb + bb + sb + ws_elems * 8, &wb, &err);
+  if (rc) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  DevAct act{(int8_t *)wb, (int32_t *)(wb + qb), (float *)(wb + qb + bb)};
+  CU(launch_quant(x, cols, cols, n_tok, act, nullptr, err, st));
+  CU(launch_gemv(m->w, nullptr, act, n_tok, y, rows, EPI_STORE, err, st, 0, nullptr, nullptr,
+                 (int64_t *)(wb + qb + bb + sb), ws_elems));
   return SPB_OK;
 }
 

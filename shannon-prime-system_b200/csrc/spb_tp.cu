@@ -16,6 +16,7 @@
 #include <cstdio>
 #include <cstring>
 #include <mutex>
+#include <vector>
 
 #include "../../include/spb200.h"
 #include "spb_kernels.cuh"
@@ -75,7 +76,8 @@ int nccl_fail(const char *what, ncclResult_t r) {
 // words [16 p] hold source p's flag (128 bytes apart), then data[2][world][cap] uint64. One CTA
 // pushes this rank's n values into slot [parity][rank] of every mailbox, fences at system
 // scope and raises its flag in each; then it waits for every source's flag in its own mailbox
-// (bounded by %globaltimer: ERR_TIMEOUT after 2 s) and reduces the world slots locally. The
+// (bounded by %globaltimer: ERR_TIMEOUT after 2 s, the wait then ends and the kernel returns
+// with the missing sources' slots unread) and reduces the world slots locally. The
 // exchange number e comes from a device counter (so graph replays stay in step); slots
 // alternate with e's parity, so a rank that is one exchange ahead never overwrites a slot that
 // is still being read.
@@ -92,7 +94,10 @@ struct P2PArgs {
   const void *src;
   void *dst;
   int n, cap, rank, world, op;
+  uint64_t timeout_ns;       // the bounded wait's limit
 };
+
+constexpr uint64_t P2P_TIMEOUT_NS = 2000000000ull;
 
 __device__ __forceinline__ uint64_t p2p_now() {
   uint64_t t;
@@ -120,7 +125,7 @@ __global__ void __launch_bounds__(P2P_THREADS) k_p2p_exchange(P2PArgs a) {
       uint64_t v;
       asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(mine) : "memory");
       if (v >= e) break;
-      if (p2p_now() - t0 > 2000000000ull) {
+      if (p2p_now() - t0 > a.timeout_ns) {
         atomicOr(a.err, spb::ERR_TIMEOUT);
         break;
       }
@@ -268,6 +273,63 @@ extern "C" int spb_tp_p2p_connect(spb_tp *tp, const uint8_t *blobs) {
   return SPB_OK;
 }
 
+// Diagnostics of the bounded wait: rank 0 of a group of `world` mailboxes that all live on the
+// current device. The sources not in absent_mask have already arrived (their flag and n values
+// are in place before the launch); the absent ones never do, so the kernel's wait runs out after
+// timeout_ms and it raises ERR_TIMEOUT. No second process or GPU takes part, so nothing else
+// can hang.
+extern "C" int spb_tp_p2p_loopback(int world, uint32_t absent_mask, int timeout_ms, int n) {
+  if (world < 2 || world > P2P_MAX || timeout_ms <= 0 || timeout_ms > 10000 || n <= 0 || n > 4096 ||
+      (absent_mask & 1u) || (absent_mask >> world))
+    return spb::record_error(SPB_EBADARG, "spb_tp_p2p_loopback: bad arg");
+  const size_t words = P2P_FLAG_WORDS + (size_t)2 * world * n;
+  uint64_t *mb = nullptr, *io = nullptr;
+  cudaError_t e = cudaMalloc(&mb, words * 8 * world);
+  if (e == cudaSuccess) e = cudaMalloc(&io, (size_t)(2 * n + 16) * 8);
+  std::vector<uint64_t> h0(words, 0), src(n), got(n);
+  for (int i = 0; i < n; i++) src[i] = (uint64_t)(i * 7 + 1);
+  uint64_t want_sum = 0;
+  for (int p = 1; p < world; p++) {
+    if (absent_mask & (1u << p)) continue;
+    h0[16 * p] = 1;   // exchange 1 (odd parity): this source has arrived
+    for (int i = 0; i < n; i++) h0[P2P_FLAG_WORDS + ((size_t)world + p) * n + i] = (uint64_t)(1000 * p + i);
+  }
+  if (e == cudaSuccess) e = cudaMemset(mb, 0, words * 8 * world);
+  if (e == cudaSuccess) e = cudaMemset(io, 0, (size_t)(2 * n + 16) * 8);
+  if (e == cudaSuccess) e = cudaMemcpy(mb, h0.data(), words * 8, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemcpy(io, src.data(), (size_t)n * 8, cudaMemcpyHostToDevice);
+  uint32_t herr = 0;
+  if (e == cudaSuccess) {
+    P2PArgs a{};
+    for (int p = 0; p < world; p++) a.mbox[p] = mb + (size_t)p * words;
+    a.epoch = io + 2 * n;
+    a.err = reinterpret_cast<uint32_t *>(io + 2 * n + 8);
+    a.src = io;
+    a.dst = io + n;
+    a.n = n;
+    a.cap = n;
+    a.rank = 0;
+    a.world = world;
+    a.op = P2P_SUM_I64;
+    a.timeout_ns = (uint64_t)timeout_ms * 1000000ull;
+    k_p2p_exchange<<<1, P2P_THREADS>>>(a);
+    e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaMemcpy(got.data(), io + n, (size_t)n * 8, cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess) e = cudaMemcpy(&herr, a.err, 4, cudaMemcpyDeviceToHost);
+  }
+  cudaFree(mb);
+  cudaFree(io);
+  if (e != cudaSuccess) return spb::record_error(SPB_ECUDA, cudaGetErrorString(e));
+  if (herr & spb::ERR_TIMEOUT)
+    return spb::record_error(SPB_ECUDA, "spb_tp_p2p_loopback: a bounded wait gave up (timeout)");
+  for (int i = 0; i < n; i++) {
+    want_sum = src[i];
+    for (int p = 1; p < world; p++) want_sum += (uint64_t)(1000 * p + i);
+    if (got[i] != want_sum) return spb::record_error(SPB_ERANGE, "spb_tp_p2p_loopback: wrong sum");
+  }
+  return SPB_OK;
+}
+
 extern "C" int spb_tp_rank(const spb_tp *tp) { return tp ? tp->rank : -1; }
 extern "C" int spb_tp_world(const spb_tp *tp) { return tp ? tp->world : 0; }
 
@@ -291,6 +353,7 @@ static cudaError_t p2p_launch(const spb_tp *tp, const void *src, void *dst, size
   a.rank = tp->rank;
   a.world = tp->world;
   a.op = op;
+  a.timeout_ns = P2P_TIMEOUT_NS;
   k_p2p_exchange<<<1, P2P_THREADS, 0, st>>>(a);
   return cudaGetLastError();
 }

@@ -29,9 +29,10 @@ CORE_SYMBOLS = [
     "spb_gemv_q4b_gated_q", "spb_rmsnorm_exact_dev", "spb_gelu_exact_dev",
     "spb_silu_exact_dev", "spb_rope_cordic_dev", "spb_take_device_errors", "spb_rope_freq_table",
     "spb_cordic_tables", "spb_graph_begin", "spb_graph_end", "spb_graph_launch", "spb_graph_free",
-    "spb_decode_mode", "spb_session_decode_trace", "spb_batch_decode_step",
+    "spb_batch_decode_step", "spb_q4b_prepare", "spb_q4b_release", "spb_q4b_info", "spb_q4b_matmul",
     "spb_tp_shard", "spb_tp_unique_id", "spb_tp_open", "spb_tp_close", "spb_tp_rank", "spb_tp_world",
     "spb_model_synthetic_tp", "spb_model_upload_tp", "spb_tp_p2p_init", "spb_tp_p2p_connect",
+    "spb_tp_p2p_loopback",
 ]
 L1_SYMBOLS = ["spb_l1_forward", "spb_l1_backend", "spb_l1_kvdecode_table", "spb_l1_kvdecode_clone",
               "spb_l1_set_device", "spb_l1_release_model"]
@@ -125,9 +126,7 @@ def load(path: str = CORE_SO):
         "spb_session_decode_step": ([vp, i32, vp], C.c_int),
         "spb_session_decode_step_argmax": ([vp, i32, vp, vp], C.c_int),
         "spb_session_decode_greedy": ([vp, i32, C.c_int, vp], C.c_int),
-        "spb_decode_mode": ([C.c_int], C.c_int),
         "spb_batch_decode_step": ([vp, C.c_int, vp, vp, vp], C.c_int),
-        "spb_session_decode_trace": ([vp, i32, vp, C.c_int], C.c_int),
         "spb_session_rewind": ([vp, C.c_int], C.c_int), "spb_session_position": ([vp], C.c_int),
         "spb_session_clone": ([vp, C.POINTER(vp)], C.c_int), "spb_session_close": ([vp], None),
         "spb_session_kv_read": ([vp, C.c_int, C.c_int, C.c_int, vp], C.c_int),
@@ -135,6 +134,11 @@ def load(path: str = CORE_SO):
         "spb_forward": ([vp, vp, C.c_int, vp], C.c_int),
         "spb_gemv_q4b": ([vp, vp, C.c_int, C.c_int, vp, C.c_int, vp, vp], C.c_int),
         "spb_gemv_q4b_noalloc": ([vp, vp, C.c_int, C.c_int, vp, C.c_int, vp, vp], C.c_int),
+        "spb_q4b_prepare": ([vp, vp, C.c_int, C.c_int, vp, C.POINTER(vp)], C.c_int),
+        "spb_tp_p2p_loopback": ([C.c_int, C.c_uint32, C.c_int, C.c_int], C.c_int),
+        "spb_q4b_release": ([vp], None),
+        "spb_q4b_info": ([vp, vp], C.c_int),
+        "spb_q4b_matmul": ([vp, vp, C.c_int, vp, vp], C.c_int),
         "spb_quantize_rows": ([vp, C.c_int, C.c_int, vp, vp, vp, vp], C.c_int),
         "spb_gemv_q4b_q": ([vp, vp, C.c_int, C.c_int, vp, vp, vp, C.c_int, vp, vp], C.c_int),
         "spb_gemv_q4b_gated_q": ([vp, vp, vp, vp, C.c_int, C.c_int, vp, vp, vp, C.c_int, C.c_int, vp, vp],
@@ -318,14 +322,6 @@ class Session:
         check(load().spb_session_decode_step_argmax(self.h, int(token), lg.ctypes.data, C.byref(am)))
         return lg, am.value
 
-    def decode_trace(self, token):
-        """One decode step through the persistent kernel with its phase trace; returns an
-        array [points][3] of %globaltimer ns (CTA 0, latest CTA, earliest CTA)."""
-        npts = 1 + self.model.cfg.n_layers * 24 + 3
-        out = np.zeros(3 * npts + 2 * 4096, np.uint64)
-        check(load().spb_session_decode_trace(self.h, int(token), out.ctypes.data, out.size))
-        return out[:3 * npts].reshape(npts, 3), out[3 * npts:].reshape(4096, 2)
-
     def greedy(self, token, n):
         out = np.empty(n, np.int32)
         check(load().spb_session_decode_greedy(self.h, int(token), n, out.ctypes.data))
@@ -369,6 +365,30 @@ def batch_decode(sessions, tokens, logits=True):
     check(load().spb_batch_decode_step(hs, B, tok.ctypes.data, lg.ctypes.data if logits else None,
                                        am.ctypes.data))
     return lg, am
+
+
+class PreparedQ4B:
+    """An OK_Q4B matrix already in device memory, prepared once (spb_q4b_prepare: the exact-range
+    check and the block-scale description); matmul takes any number of token rows. Pointers are
+    device addresses (ints or c_void_p); the codes and scales must outlive the handle."""
+
+    def __init__(self, codes, bscale, rows, cols, stream=None):
+        h = C.c_void_p()
+        check(load().spb_q4b_prepare(codes, bscale, rows, cols, stream, C.byref(h)))
+        self.h, self.rows, self.cols = h, rows, cols
+
+    def info(self):
+        o = (C.c_int32 * 4)()
+        check(load().spb_q4b_info(self.h, o))
+        return {"rows": o[0], "cols": o[1], "small": o[2], "planes": o[3]}
+
+    def matmul(self, x, n_tok, y, stream=None):
+        check(load().spb_q4b_matmul(self.h, x, n_tok, y, stream))
+
+    def release(self):
+        if self.h:
+            load().spb_q4b_release(self.h)
+            self.h = None
 
 
 def load_l1(path: str = L1_SO):

@@ -187,6 +187,103 @@ def gen_matrix(seed, name, rows, cols) -> Q4B:
                rows, cols)
 
 
+# ----------------------------------------------------------------------------- adversarial scales
+# The exact int64 accumulation bound every row must keep (the checker's xref_q4b_check and the
+# library's upload/prepare test): sum_b |k_b| * 32 * 8 * 127 < 2^63, k_b the f16 scale * 2^24.
+BOUND_LIMIT = (1 << 63) // (32 * 8 * 127)
+
+
+def f16_k(h: int) -> int:
+    """The f16 bit pattern h as the integer k = value * 2^24 (finite values only)."""
+    e, m = (h >> 10) & 31, h & 1023
+    k = m if e == 0 else (1024 | m) << (e - 1)
+    return -k if h & 0x8000 else k
+
+
+def k_to_f16(k: int) -> int:
+    """The f16 bits of the value k * 2^-24, for a k that f16 represents exactly."""
+    neg, k = k < 0, abs(k)
+    if k < 1024:
+        h = k
+    else:
+        sh = k.bit_length() - 11
+        assert k == (k >> sh) << sh and 0 <= sh <= 29, k
+        h = ((sh + 1) << 10) | ((k >> sh) & 1023)
+    return h | (0x8000 if neg else 0)
+
+
+def adversarial_bscale(seed: int, rows: int, cols: int, kind: str) -> np.ndarray:
+    """Block scales that the seeded generator never makes, row-major [rows][cols/32] f16 bits:
+      signs     random signs, one exponent per row (spread 0), a few zero and subnormal blocks
+      large     |scale| >= 128 (exponent fields 22-23): outside the token-batch GEMM's small form
+      spreadN   exponent fields vary within a row by up to N (N = 1, 9, 17), random signs
+      full      exponent fields 0-30 within a row (subnormal to the f16 maximum), random signs
+    Rows whose sum would break the exact bound have their largest blocks lowered until it holds."""
+    rng = np.random.default_rng(seed)
+    nblk = cols // 32
+    mant = rng.integers(0, 1024, (rows, nblk))
+    sign = rng.integers(0, 2, (rows, nblk)) << 15
+    if kind == "signs":
+        base = rng.integers(4, 12, (rows, 1))
+        e = np.broadcast_to(base, (rows, nblk)).copy()
+        z = rng.random((rows, nblk))
+        e[z < 0.05] = 0                               # subnormal (mantissa may be 0: a zero block)
+        mant[z < 0.02] = 0
+        if rows > 1:
+            e[1], mant[1] = 0, 0                      # an all-zero row
+    elif kind == "large":
+        e = rng.integers(22, 24, (rows, nblk))
+    elif kind.startswith("spread"):
+        n = int(kind[6:])
+        lo = rng.integers(1, 30 - n, (rows, 1))
+        e = lo + rng.integers(0, n + 1, (rows, nblk))
+    elif kind == "full":
+        e = rng.integers(0, 31, (rows, nblk))
+    else:
+        raise ValueError(kind)
+    h = ((e.astype(np.int64) << 10) | mant | sign).astype(np.uint16)
+    for r in range(rows):   # keep every row inside the bound
+        while sum(abs(f16_k(int(x))) for x in h[r]) >= BOUND_LIMIT:
+            b = int(np.argmax((h[r] >> 10) & 31))
+            h[r, b] = np.uint16(int(h[r, b]) - (1 << 10))
+    return h
+
+
+def model_bscale(seed: int, rows: int, cols: int, spread: int) -> np.ndarray:
+    """Block scales for whole-model tests: the seeded generator's magnitude (its exponent for
+    `cols` is the largest), lowered per block by 0..spread exponent steps (down to subnormal),
+    random signs and 3 % zero blocks, so activations keep the exact range."""
+    rng = np.random.default_rng(seed)
+    nblk = cols // 32
+    e = np.maximum(scale_exponent(cols) + 15 - rng.integers(0, spread + 1, (rows, nblk)), 0)
+    mant = rng.integers(0, 1024, (rows, nblk))
+    mant[rng.random((rows, nblk)) < 0.03] = 0
+    mant[e == 0] |= 0            # subnormal blocks keep their mantissa (value mant * 2^-24)
+    e = np.where(mant == 0, 0, e)
+    sign = rng.integers(0, 2, (rows, nblk)) << 15
+    return ((e.astype(np.int64) << 10) | mant | sign).astype(np.uint16)
+
+
+def bound_edge_row(nblk: int, total: int) -> np.ndarray:
+    """One row of nblk positive block scales whose integers k sum to exactly `total` (as many
+    f16-maximum blocks as fit, then the remainder greedily), for the bound's edge cases."""
+    kmax = 2047 << 29
+    out = []
+    r = total
+    while r > 0:
+        if r >= kmax:
+            k = kmax
+        elif r < 1024:
+            k = r
+        else:
+            sh = r.bit_length() - 11
+            k = (r >> sh) << sh
+        out.append(k_to_f16(k))
+        r -= k
+    assert len(out) <= nblk, (len(out), nblk)
+    return np.array(out + [0] * (nblk - len(out)), np.uint16)
+
+
 def gen_model(cfg: Config, seed: int = 0) -> dict:
     """All tensors of a random-init model, keyed by their .sp-model names."""
     T = {}

@@ -139,7 +139,8 @@ def test_sliding_window_long_context(xr, cuda_ok):
     assert np.array_equal(u32(got), u32(want))
 
 
-@pytest.mark.parametrize("hd,nh,nkv", [(256, 8, 2), (128, 8, 8), (128, 16, 2), (256, 4, 2)])
+@pytest.mark.parametrize("hd,nh,nkv", [(256, 8, 2), (128, 8, 8), (128, 16, 2), (256, 4, 2), (128, 8, 2),
+                                       (128, 32, 8)])
 def test_attention_head_shapes(xr, cuda_ok, hd, nh, nkv):
     """Head widths 128 / 256 and GQA groups 1-8: q held in registers (G * hd <= 512) or read
     from shared memory, one CTA per (row, KV head) when rows x KV heads fill the GPU (the
