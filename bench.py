@@ -64,6 +64,7 @@ def parse():
     p.add_argument("--batch", type=int, default=64,
                    help="sessions decoded together for the b64 figure (0: skip it)")
     p.add_argument("--batch-steps", type=int, default=16)
+    p.add_argument("--no-sweep", action="store_true", help="skip the isolated matmul sweep (configs[1])")
     p.add_argument("--tp", action="store_true",
                    help="N>1: also time one session tensor-parallel over all N GPUs (strong scaling), "
                         "reported as the line's 'tp' object")
@@ -255,6 +256,65 @@ def gemv_roofline(cfg, spb, device, stream, iters=60):
         launches += n + 5
         del codes, scl
     return out, tot_b, tot_t, launches
+
+
+SWEEP_SHAPES = [(3840, 3840), (15360, 3840), (3840, 15360), (262144, 3840)]
+SWEEP_M = [1, 4, 16, 2048]
+
+
+def gemm_sweep(spb, device, stream, int8_peak_tops, hbm_gbs, iters=20):
+    """the OK_Q4B matmul alone (spb_q4b_matmul on a prepared matrix: the
+    activation quantizer, then the dequant-GEMV for 1-16 token rows or the tcgen05 GEMM for
+    2048), 4 weight shapes x M in {1, 4, 16, 2048}, random codes and seeded block scales with
+    one exponent per matrix (two digit planes). CUDA events on the launching stream over
+    `iters` launches; weight sets rotated so every launch reads from HBM for the small M.
+    GB/s counts the algorithmic bytes (codes, scales, int8 activations, f32 outputs); TOP/s
+    counts 2 x M x rows x K exact integer multiply-adds."""
+    import ctypes as C
+    import torch
+    import spb200
+    L2 = 126 * 2 ** 20
+    P = lambda t: C.c_void_p(t.data_ptr())
+    out = []
+    for rows, cols in SWEEP_SHAPES:
+        wbytes = rows * cols // 2 + rows * (cols // 32) * 2
+        copies = max(1, -(-3 * L2 // wbytes))
+        codes = [torch.randint(0, 256, (rows * cols // 2,), dtype=torch.uint8, device=device) for _ in range(copies)]
+        e = (int(np.floor(np.log2(1.0 / (8.0 * np.sqrt(cols))))) + 15) << 10
+        scl = [(torch.randint(0, 1024, (rows * (cols // 32),), dtype=torch.int16, device=device) | e)
+               for _ in range(copies)]
+        mats = [spb200.PreparedQ4B(P(c), P(sc_), rows, cols, stream.cuda_stream) for c, sc_ in zip(codes, scl)]
+        for M in SWEEP_M:
+            x = torch.randn(M, cols, device=device)
+            y = torch.empty(M, rows, dtype=torch.float32, device=device)
+            n = iters if M < 2048 else max(3, iters // 4)
+            for i in range(3):
+                mats[i % copies].matmul(P(x), M, P(y), stream.cuda_stream)
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for i in range(n):
+                mats[i % copies].matmul(P(x), M, P(y), stream.cuda_stream)
+            e1.record(stream)
+            e1.synchronize()
+            us = e0.elapsed_time(e1) * 1e3 / n
+            byts = wbytes + M * cols + M * (cols // 32) * 4 + M * rows * 4
+            ops = 2.0 * M * rows * cols
+            r = {"rows": rows, "cols": cols, "m": M, "us": round(us, 2), "gbs": round(byts / us / 1e3, 1),
+                 "tops": round(ops / us / 1e6, 2)}
+            if M >= 1024:
+                r["frac_int8"] = round(ops / us / 1e6 / int8_peak_tops, 4)
+                r["kernel"] = "k_gemm_tc (tcgen05.mma kind::i8, 2 digit planes)" if mats[0].info()["planes"] else "k_gemm"
+            else:
+                r["frac_hbm"] = round(byts / us / 1e3 / hbm_gbs, 4)
+                r["kernel"] = "k_gemv"
+            out.append(r)
+            del x, y
+        for mm in mats:
+            mm.release()
+        del codes, scl
+        torch.cuda.empty_cache()
+    return out
 
 
 def measure_batch(m, cfg, B, K, W, seed, max_over_ranks):
@@ -474,8 +534,12 @@ def run_spb(args):
                "peak_tops": round(int8_peak, 1),
                "peak_source": ("2 x measured" if bf16 else "2 x fallback") + " bf16 dense TF/s (int8 dense = 2 x bf16)",
                "frac": round(prefill_ops / prefill_dev_s / 1e12 / int8_peak, 4),
-               "kernel": "k_gemm (mma.sync m16n8k32 int8 with a per-32-column int64 block-scale epilogue); "
-                         "CUDA events around spb_session_prefill on the session stream"}
+               "kernel": "k_gemm_tc (tcgen05.mma kind::i8 over 8-bit digit planes of the block-scaled weights, "
+                         "TMA-staged activations, 256-row prefill chunks); CUDA events around "
+                         "spb_session_prefill on the session stream (attention, norms and the rest included)"}
+    sweep = None
+    if not args.no_sweep and world == 1:
+        sweep = gemm_sweep(spb, torch.device("cuda", local), stream, int8_peak, peaks()[0])
     line = {
         "metric": METRIC, "value": round(world * K / (ms / 1e3), 3), "unit": "tokens/s",
         "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": round(ms / K, 4),
@@ -493,6 +557,7 @@ def run_spb(args):
         "config1": config1,
         "b64": b64,
         "prefill": prefill,
+        "config2_sweep": sweep,
     }
     if tpr:
         line["tp"] = tpr

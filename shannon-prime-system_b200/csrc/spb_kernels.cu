@@ -125,9 +125,11 @@ k_gemv(DevQ4B w, DevQ4B w2, DevAct act, float *__restrict__ y, int ldy, uint32_t
   const int gstride = gridDim.x * (GEMV_WARPS / KS);
   int g = blockIdx.x * (GEMV_WARPS / KS) + pair;
 
-  uint4 cw[NM][RPW][NCHW];
-  uint32_t hw[NM][RPW][NCHW];
-  auto load_group = [&](int grp) {
+  typedef uint4 CodeBuf[NM][RPW][NCHW];
+  typedef uint32_t ScaleBuf[NM][RPW][NCHW];
+  CodeBuf cw;
+  ScaleBuf hw;
+  auto load_into = [&](int grp, CodeBuf &cw, ScaleBuf &hw) {
 #pragma unroll
     for (int r = 0; r < RPW; r++) {
       const int row = grp * RPW + r;
@@ -150,7 +152,7 @@ k_gemv(DevQ4B w, DevQ4B w2, DevAct act, float *__restrict__ y, int ldy, uint32_t
     }
   };
   pdl_trigger();
-  if (g < ngroups) load_group(g);   // weight loads are in flight while the predecessor drains
+  if (g < ngroups) load_into(g, cw, hw);   // weight loads are in flight while the predecessor drains
   pdl_wait();
 
   {
@@ -196,8 +198,9 @@ k_gemv(DevQ4B w, DevQ4B w2, DevAct act, float *__restrict__ y, int ldy, uint32_t
     npend = 0;
   };
 
-  for (; g < ngroups; g += gstride) {
-    int64_t acc[NM][RPW][NT];
+  typedef int64_t AccBuf[NM][RPW][NT];
+  // the group's exact int32 block sums, scaled and accumulated in int64
+  auto dots = [&](const CodeBuf &cw, const ScaleBuf &hw, AccBuf &acc) {
 #pragma unroll
     for (int m = 0; m < NM; m++)
 #pragma unroll
@@ -221,8 +224,9 @@ k_gemv(DevQ4B w, DevQ4B w2, DevAct act, float *__restrict__ y, int ldy, uint32_t
         }
       }
     }
-    const int g0 = g;
-    if (g + gstride < ngroups) load_group(g + gstride);   // next group's loads overlap the reduction
+  };
+  // warp reduction (and the pair's exchange), then the deferred epilogue's bookkeeping
+  auto finish = [&](int g0, AccBuf &acc) {
 #pragma unroll
     for (int r = 0; r < RPW; r++) {
       const int row = g0 * RPW + r;
@@ -250,6 +254,13 @@ k_gemv(DevQ4B w, DevQ4B w2, DevAct act, float *__restrict__ y, int ldy, uint32_t
         if (++npend == 32) flush();
       }
     }
+  };
+
+  for (; g < ngroups; g += gstride) {
+    AccBuf acc;
+    dots(cw, hw, acc);
+    if (g + gstride < ngroups) load_into(g + gstride, cw, hw);   // next group's loads overlap the reduction
+    finish(g, acc);
   }
   flush();
   if (ymax) {   // per-token max |y| of this CTA -> one atomic per token
@@ -662,6 +673,17 @@ static bool splitk_enabled() {
   return on != 0;
 }
 
+// token rows from which a batch runs the tcgen05 GEMM (SPB_TC_MIN; SPB_TC=0 never)
+static int tc_min_tokens() {
+  static int n = -1;
+  if (n < 0) {
+    const char *e = getenv("SPB_TC_MIN");
+    n = e ? atoi(e) : 128;
+    if (n < 1) n = 1;
+  }
+  return n;
+}
+
 // SPB_GEMM=0 keeps token batches on the dp4a k_gemv (comparisons; results are identical)
 static bool gemm_enabled() {
   static int on = -1;
@@ -680,6 +702,28 @@ cudaError_t launch_gemv(const DevQ4B &w, const DevQ4B *w2, const DevAct &act, in
   if (epi_pair(epi) && (!w2 || w2->rows != w.rows || w2->cols != w.cols)) return cudaErrorInvalidValue;
   if (epi == EPI_I64 && (ymax || amax)) return cudaErrorInvalidValue;
   const size_t yb = (size_t)epi_bytes(epi);   // y row offsets below are in elements of this size
+  // large token batches: the tcgen05 GEMM over digit planes, K split into parts when the
+  // (row tile x token tile) grid would leave most SMs idle
+  if (ntok >= tc_min_tokens() && grid_limit == 0 && gemm_enabled() && gemm_tc_covers(w, w2, epi, ntok)) {
+    const int P = gemm_tc_covers(w, w2, epi, ntok);
+    const int N = P * (epi_pair(epi) ? 2 : 1) == 2 ? 256 : P * (epi_pair(epi) ? 2 : 1) == 3 ? 160
+                : P * (epi_pair(epi) ? 2 : 1) == 4 ? 128 : 80;
+    const long tiles = (long)((ntok + N - 1) / N) * ((w.rows + 127) / 128);
+    const int nk = w.cols / 128;
+    int ks = 1;
+    if (epi == EPI_STORE && !ymax && !amax && ws && splitk_enabled())
+      while (ks < 4 && tiles * ks * 2 <= 148 && nk % (ks * 2) == 0 && nk / (ks * 2) >= 8 &&
+             (size_t)(ks * 2) * ntok * w.rows <= ws_elems)
+        ks *= 2;
+    if (ks > 1) {
+      cudaError_t e = launch_gemm_tc(w, w2, act, ntok, reinterpret_cast<float *>(ws), w.rows, EPI_I64, err, st, nullptr,
+                                     nullptr, ks, pdl_enabled() != 0);
+      if (e == cudaSuccess)
+        e = launch_scale_i64(ws, act.scale, ntok, w.rows, y, ldy, st, ks, (size_t)ntok * w.rows);
+      return e;
+    }
+    return launch_gemm_tc(w, w2, act, ntok, y, ldy, epi, err, st, ymax, amax, 1, pdl_enabled() != 0);
+  }
   // token batches (and row counts the k_gemv templates do not cover): the tensor-core GEMM
   const bool odd = ntok > 1 && (ntok & (ntok - 1)) != 0;
   if ((ntok >= 16 || odd) && grid_limit == 0 && (w.cols & 255) == 0 && (gemm_enabled() || odd)) {

@@ -75,6 +75,14 @@ cudaError_t launch_gemv(const DevQ4B &w, const DevQ4B *w2, const DevAct &act, in
                         uint32_t *ymax = nullptr, unsigned long long *amax = nullptr, int64_t *ws = nullptr,
                         size_t ws_elems = 0);
 
+// The token-batch GEMM on the tcgen05 tensor cores (spb_gemm_tc.cu), from the digit planes of
+// the described block scales (DevQ4B::shift / planes). covers: the planes it would run with, 0
+// when it does not take this matrix (or pair). ks > 1 (EPI_I64 only) splits K into ks parts,
+// part p writing its exact partial sums to y + p * ntok * ldy (int64 elements).
+int gemm_tc_covers(const DevQ4B &w, const DevQ4B *w2, int epi, int ntok);
+cudaError_t launch_gemm_tc(const DevQ4B &w, const DevQ4B *w2, const DevAct &act, int ntok, float *y, int ldy, int epi,
+                           uint32_t *err, cudaStream_t st, uint32_t *ymax, unsigned long long *amax, int ks, bool pdl);
+
 // y[t][j] = (float)(acc[t][j] * (scale[t] / 127 * 2^-24)), the GEMV epilogue's rounding, for
 // n outputs of ntok rows (acc row stride n, y row stride ldy); with parts > 1, acc is the exact
 // sum of the parts at acc + p * part_stride

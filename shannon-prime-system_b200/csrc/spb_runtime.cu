@@ -552,7 +552,8 @@ extern "C" void spb_model_free(spb_model *m) {
 extern "C" int64_t spb_model_weight_bytes(const spb_model *m) { return m ? m->stream_bytes : 0; }
 
 // ------------------------------------------------------------------------------ session
-constexpr int NT_MAX = 64;   // token rows per schedule pass (prefill chunk)
+constexpr int NT_MAX = 256;   // token rows per schedule pass (a prefill chunk without logits)
+constexpr int LG_MAX = 64;    // token rows of a pass that produces logits (and of a decode batch)
 
 struct spb_session {
   spb_model *m;
@@ -574,10 +575,10 @@ struct spb_session {
   int32_t *h_argmax = nullptr;    // pinned [NT_MAX] batch argmaxes
   cudaGraphExec_t step_graph = nullptr;
   // tensor parallel: int64 partial sums of the K-split matrices [NT_MAX][E], this rank's LM-head
-  // logits [NT_MAX][V] and the all-gathered slices [world][NT_MAX][V]
+  // logits [LG_MAX][V] and the all-gathered slices [world][LG_MAX][V]
   int64_t *y64 = nullptr;
   float *logits_l = nullptr, *logits_g = nullptr;
-  int64_t *ws = nullptr;          // split-K workspace of the token-batch GEMM [2][NT_MAX][E]
+  int64_t *ws = nullptr;          // split-K workspace of the token-batch GEMMs [4][NT_MAX][E]
   size_t ws_elems = 0;
 };
 
@@ -599,11 +600,11 @@ extern "C" int spb_session_open(spb_model *m, int pmax, spb_session **out) {
   const size_t o_x = take((size_t)NT_MAX * E * 4), o_qkv = take((size_t)NT_MAX * QKV * 4);
   const size_t o_ao = take((size_t)NT_MAX * m->QD * 4), o_ap = take((size_t)NT_MAX * E * 4);
   const size_t o_gg = take((size_t)NT_MAX * m->FF * 4), o_dn = take((size_t)NT_MAX * E * 4);
-  const size_t o_lg = take((size_t)NT_MAX * m->Vfull * 4), o_qi = take((size_t)NT_MAX * m->QD * 4);
+  const size_t o_lg = take((size_t)LG_MAX * m->Vfull * 4), o_qi = take((size_t)NT_MAX * m->QD * 4);
   const size_t o_y64 = m->tp ? take((size_t)NT_MAX * E * 8) : 0;
-  const size_t o_ws = take((size_t)2 * NT_MAX * E * 8);
-  const size_t o_lgl = m->tp ? take((size_t)NT_MAX * m->V * 4) : 0;
-  const size_t o_lgg = m->tp ? take((size_t)NT_MAX * m->Vfull * 4) : 0;
+  const size_t o_ws = take((size_t)4 * NT_MAX * E * 8);
+  const size_t o_lgl = m->tp ? take((size_t)LG_MAX * m->V * 4) : 0;
+  const size_t o_lgg = m->tp ? take((size_t)LG_MAX * m->Vfull * 4) : 0;
   const size_t o_aq = take((size_t)NT_MAX * maxK), o_ab = take((size_t)NT_MAX * (maxK / 32) * 4);
   const size_t o_as = take(NT_MAX * 4), o_pos = take(4), o_tok = take(NT_MAX * 4), o_am = take(NT_MAX * 4);
   const size_t o_hist = take((size_t)pmax * 4), o_err = take(4), o_slots = take(2 * NT_MAX * 4);
@@ -623,7 +624,7 @@ extern "C" int spb_session_open(spb_model *m, int pmax, spb_session **out) {
   s->amax_keys = (unsigned long long *)(B + o_keys);
   s->rows_dev = (BatchRow *)(B + o_rows);
   s->ws = (int64_t *)(B + o_ws);
-  s->ws_elems = (size_t)2 * NT_MAX * E;
+  s->ws_elems = (size_t)4 * NT_MAX * E;
   if (m->tp) {
     s->y64 = (int64_t *)(B + o_y64);
     s->logits_l = (float *)(B + o_lgl);
@@ -790,7 +791,7 @@ extern "C" int spb_session_prefill(spb_session *s, const int32_t *tokens, int n_
   if (rc) return rc;
   int done = 0;
   while (done < n_tok) {
-    int nt = NT_MAX;
+    int nt = logits ? LG_MAX : NT_MAX;   // the logits buffer holds LG_MAX rows
     while (nt > n_tok - done) nt >>= 1;
     memcpy(s->h_pinned, tokens + done, (size_t)nt * 4);
     CU(cudaMemcpyAsync(s->tok_dev, s->h_pinned, (size_t)nt * 4, cudaMemcpyHostToDevice, s->st));
@@ -853,7 +854,7 @@ extern "C" int spb_session_decode_step(spb_session *s, int32_t token, float *log
 // become the token-batch GEMM. ss[0] leads: its stream and scratch rows run the step.
 extern "C" int spb_batch_decode_step(spb_session *const *ss, int B, const int32_t *tokens, float *logits,
                                      int32_t *argmax) {
-  if (!ss || !tokens || B <= 0 || B > NT_MAX) return set_err(SPB_EBADARG, "spb_batch_decode_step: B in [1, %d]", NT_MAX);
+  if (!ss || !tokens || B <= 0 || B > LG_MAX) return set_err(SPB_EBADARG, "spb_batch_decode_step: B in [1, %d]", LG_MAX);
   spb_session *lead = ss[0];
   if (!lead) return set_err(SPB_EBADARG, "spb_batch_decode_step: null session");
   int Pmax = 0;
