@@ -65,6 +65,9 @@ def parse():
                    help="sessions decoded together for the b64 figure (0: skip it)")
     p.add_argument("--batch-steps", type=int, default=16)
     p.add_argument("--no-sweep", action="store_true", help="skip the isolated matmul sweep (configs[1])")
+    p.add_argument("--spec-sessions", type=int, default=8,
+                   help="speculative-decode sessions per GPU (configs[4]: 64 over 8 GPUs); 0 skips it")
+    p.add_argument("--spec-steps", type=int, default=8)
     p.add_argument("--tp", action="store_true",
                    help="N>1: also time one session tensor-parallel over all N GPUs (strong scaling), "
                         "reported as the line's 'tp' object")
@@ -355,6 +358,68 @@ def measure_batch(m, cfg, B, K, W, seed, max_over_ranks):
                       "B argmaxes D2H per step)", "prefill_s_untimed": round(prefill_s, 2)}
 
 
+SPEC_PG = 128
+
+
+def measure_spec(m, cfg, S, steps, seed, max_over_ranks, barrier):
+    """BASELINE configs[4], one GPU's share: S sessions (the 64 sessions spread over 8 GPUs are 8
+    per GPU) with seeded ragged contexts U[128, 8192] in a paged, copy-on-write K/V pool. Each
+    step: clone every session (O(1): the clone shares the pages), draft 4 greedy tokens on the
+    clones as 4 batched decode steps (the first write into a shared page copies it), rewind a
+    seeded 0-4 rejected tokens, close the parent. Timed: `steps` such steps, wall clock from the
+    host (the clones, rewinds and closes included), max over ranks."""
+    import torch
+    import spb200
+    import spmodel
+    rng = np.random.default_rng(seed + 4242)
+    ctx = rng.integers(128, 8193, size=S)
+    pmax = int(ctx.max()) + 4 * (steps + 2) + 8
+    need = sum(-(-(int(c) + 4 * (steps + 2) + 8) // SPEC_PG) for c in ctx) + 2 * S
+    pool = spb200.KvPool(m, SPEC_PG, need)
+    t0 = time.perf_counter()
+    sess, nxt = [], []
+    for i in range(S):
+        s = pool.session(pmax)
+        t = spmodel.gen_tokens(seed + 5000 + i, int(ctx[i]), cfg.n_vocab)
+        s.prefill(t, logits=False)
+        sess.append(s)
+        nxt.append(int(t[-1]))
+    prefill_s = time.perf_counter() - t0
+
+    def spec_step(sess, nxt):
+        clones = [s.clone() for s in sess]
+        toks, outs = list(nxt), []
+        for _ in range(4):
+            _, am = spb200.batch_decode(clones, toks, logits=False)
+            outs.append([int(a) for a in am])
+            toks = outs[-1]
+        rej = rng.integers(0, 5, size=S)
+        for i in range(S):
+            clones[i].rewind(int(rej[i]))
+            if rej[i] < 4:
+                nxt[i] = outs[3 - int(rej[i])][i]
+            sess[i].close()
+        return clones, int((4 - rej).sum())
+
+    sess, _ = spec_step(sess, nxt)            # warm-up step
+    barrier()
+    t0 = time.perf_counter()
+    accepted = 0
+    for _ in range(steps):
+        sess, a = spec_step(sess, nxt)
+        accepted += a
+    dt = max_over_ranks((time.perf_counter() - t0) * 1e3) / 1e3
+    for s in sess:
+        s.close()
+    pool.free()
+    return {"value": round(accepted / dt, 2), "unit": "accepted tokens/s (this GPU's sessions)",
+            "drafted_tokens_per_s": round(4 * S * steps / dt, 2), "sessions": S, "steps": steps,
+            "ms_per_step": round(dt / steps * 1e3, 3), "ctx": "seeded U[128, 8192] tokens per session",
+            "kv": f"paged pool, {SPEC_PG}-position pages, copy-on-write; {need} pages",
+            "timing": "wall clock around the steps (clone + 4 batched draft steps + rewind + close)",
+            "prefill_s_untimed": round(prefill_s, 2)}
+
+
 def measure_tp(cfg, args, rank, local, world, max_over_ranks, barrier, p2p=True):
     """One session of the model split over the group (spb_model_synthetic_tp): K greedy steps
     timed with CUDA events on the session stream, max over ranks; every rank produces the
@@ -490,6 +555,13 @@ def run_spb(args):
         b64 = measure_batch(m, cfg, args.batch, args.batch_steps, 3, args.seed + rank, max_over_ranks)
         b64["value"] = round(world * b64["value"], 3)
 
+    spec = None
+    if args.spec_sessions > 0:
+        spec = measure_spec(m, cfg, args.spec_sessions, args.spec_steps, args.seed + rank, max_over_ranks, barrier)
+        spec["value"] = round(world * spec["value"], 2)
+        spec["unit"] = "accepted tokens/s (all GPUs' sessions)"
+        spec["sessions_total"] = world * args.spec_sessions
+
     tpr = None
     if args.tp and world > 1:
         tpr = measure_tp(cfg, args, rank, local, world, max_over_ranks, barrier, p2p=True)
@@ -556,6 +628,7 @@ def run_spb(args):
         "cpu_baseline": cpu,
         "config1": config1,
         "b64": b64,
+        "spec": spec,
         "prefill": prefill,
         "config2_sweep": sweep,
     }

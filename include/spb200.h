@@ -109,7 +109,24 @@ int  spb_batch_decode_step(spb_session *const *ss, int B, const int32_t *tokens,
                            int32_t *argmax);
 int  spb_session_rewind(spb_session *s, int n);          /* O(1): position -= n */
 int  spb_session_position(const spb_session *s);         /* -1 on NULL */
-int  spb_session_clone(const spb_session *s, spb_session **out);   /* deep KV copy */
+/* sp_session_clone (sp_session.c:773-816): a session at the same position with the same cache.
+ * A paged session's clone shares its pages (no K/V copied: O(pages) host work); a page is
+ * copied only when one of the sessions holding it writes into it. An unpaged session's clone
+ * is a deep copy of its cache on the device. */
+int  spb_session_clone(const spb_session *s, spb_session **out);
+
+/* ---- paged, copy-on-write K/V (for forks: speculative decode, beam search) --------------
+ * A pool of pages on the model's device, each holding page_positions (a multiple of 128)
+ * positions of every layer's K and V rows: n_pages * page_positions * n_layers * n_head_kv *
+ * head_dim * 8 bytes in all. Paged sessions take pages as they write positions; a page two
+ * sessions share (after a clone) is copied before either writes into it. SPB_EOOM when the
+ * pool has no free page left. Close every session of a pool before freeing it. */
+typedef struct spb_kvpool spb_kvpool;
+int  spb_kvpool_create(spb_model *m, int page_positions, int n_pages, spb_kvpool **out);
+void spb_kvpool_free(spb_kvpool *p);
+int  spb_kvpool_free_pages(spb_kvpool *p);                 /* pages not held by any session */
+/* spb_session_open with the K/V rows in pool pages (same verbs and bytes as an unpaged session) */
+int  spb_session_open_paged(spb_kvpool *p, int pmax, spb_session **out);
 void spb_session_close(spb_session *s);
 /* readback of one cached K (which=0) or V (which=1) row: [n_head_kv*head_dim] int32 */
 int  spb_session_kv_read(const spb_session *s, int layer, int pos, int which, int32_t *out);

@@ -43,10 +43,31 @@ void *spb_l1_backend(void);
  * decode (sp_l1.h:381-384, 436-441). */
 const struct sp_kvdecode_dispatch_fn *spb_l1_kvdecode_table(void);
 
-/* Append-only extension proposed for the section-6b table (sp_l1.h:450-452 allows new
- * rows at the end): fork a resident cache (deep KV copy on the device), the missing
- * piece for speculative decode -- sp_session_clone drops section-6b (sp_session.c:792-799). */
+/* Append-only extension of the section-6b table (sp_l1.h:450-452 allows new rows at the
+ * end): fork a resident cache, the missing piece for speculative decode --
+ * sp_session_clone drops section-6b (sp_session.c:792-799). With a page pool (below) the
+ * fork shares the cache's pages and copies a page only when one side writes into it; without
+ * one it is a deep copy of the cache on the device. */
 int spb_l1_kvdecode_clone(const struct sp_kvdecode_handle *h, struct sp_kvdecode_handle **out);
+
+/* The table with that row appended: its first member is the frozen table, so a caller that
+ * knows only sp_l1.h reads the same six rows; one that knows the extension finds `clone`
+ * after `close`. spb_l1_kvdecode_table() returns &spb_l1_kvdecode_table_ext()->base.
+ * (Complete type only where sp/sp_l1.h is included before this header.) */
+#ifdef SP_L1_H
+struct spb_kvdecode_dispatch_ext {
+    struct sp_kvdecode_dispatch_fn base;
+    int (*clone)(const struct sp_kvdecode_handle *h, struct sp_kvdecode_handle **out);
+};
+#else
+struct spb_kvdecode_dispatch_ext;
+#endif
+const struct spb_kvdecode_dispatch_ext *spb_l1_kvdecode_table_ext(void);
+
+/* Caches of models uploaded after this call live in a per-model page pool of n_pages pages of
+ * page_positions (a multiple of 128) positions, so forks are O(1); 0, 0 (default) = each
+ * cache its own allocation. */
+int spb_l1_set_kv_pool(int page_positions, int n_pages);
 
 /* Device used for models uploaded after this call (default 0). */
 int spb_l1_set_device(int device);

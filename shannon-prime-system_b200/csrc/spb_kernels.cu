@@ -1290,27 +1290,22 @@ __global__ void k_rope_kv(RopeArgs a) {
   const int head = blockIdx.x, t = blockIdx.y;
   const int HD = a.HD, half = HD >> 1, QD = a.NH * HD, KVD = a.NKV * HD;
   const float *row = a.qkv + (size_t)t * (QD + 2 * KVD);
-  int p, P;
-  int32_t *kc, *vc;
+  int p;
+  KvPages kv;
   if (a.rows) {   // row t of a multi-session batch: its own session's position and cache
     const BatchRow br = a.rows[t];
     p = br.pos;
-    P = br.P;
-    const size_t lo = (size_t)a.layer * a.NKV * P * HD;
-    kc = br.kc + lo;
-    vc = br.vc + lo;
+    kv = br.kv;
   } else {
     p = a.pos_dev[0] + t;
-    P = a.P;
-    kc = a.kc;
-    vc = a.vc;
+    kv = a.kv;
   }
   const int i = threadIdx.x;   // pair index, blockDim.x == half
   if (a.zero_slot && head == 0 && i == 0) a.zero_slot[t] = 0u;
   if (head >= a.NH + a.NKV) {  // V head: quantize to the 2^16 grid
     const int g = head - a.NH - a.NKV;
     const float *src = row + QD + KVD + g * HD;
-    int32_t *dst = vc + ((size_t)g * P + p) * HD;
+    int32_t *dst = kv.v + kv_elem(kv, a.NL, a.NKV, HD, a.layer, g, p);
 #pragma unroll
     for (int r = 0; r < 2; r++) {
       const float v = src[i + r * half];
@@ -1336,7 +1331,7 @@ __global__ void k_rope_kv(RopeArgs a) {
   const uint64_t phase = (uint64_t)(int64_t)p * a.W[i];
   int32_t oa, ob;
   cordic_rotate(vals[i], vals[i + half], phase, a.T, a.gain, oa, ob, a.err);
-  int32_t *dst = is_q ? a.qi + (size_t)t * QD + hh * HD : kc + ((size_t)hh * P + p) * HD;
+  int32_t *dst = is_q ? a.qi + (size_t)t * QD + hh * HD : kv.k + kv_elem(kv, a.NL, a.NKV, HD, a.layer, hh, p);
   dst[i] = oa;
   dst[i + half] = ob;
 }
@@ -1395,20 +1390,15 @@ __global__ void __launch_bounds__(ATTN_THREADS, 2) k_attn(AttnArgs a, int cmax, 
   if (CL > 1) asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
   const int g = blockIdx.y, t = blockIdx.z;
   const int QD = a.NH * HD;
-  int p, P;
-  const int32_t *kcl, *vcl;
+  int p;
+  KvPages kv;
   if (a.rows) {   // row t of a multi-session batch: its own session's position and cache
     const BatchRow br = a.rows[t];
     p = br.pos;
-    P = br.P;
-    const size_t lo = (size_t)a.layer * a.NKV * P * HD;
-    kcl = br.kc + lo;
-    vcl = br.vc + lo;
+    kv = br.kv;
   } else {
     p = a.pos_dev[0] + t;
-    P = a.P;
-    kcl = a.kc;
-    vcl = a.vc;
+    kv = a.kv;
   }
   const int s0 = (a.win >= 0 && p - a.win + 1 > 0) ? p - a.win + 1 : 0;
   const int n = p - s0 + 1;
@@ -1418,18 +1408,26 @@ __global__ void __launch_bounds__(ATTN_THREADS, 2) k_attn(AttnArgs a, int cmax, 
   const int cn = max(c1 - c0, 0);
   const int nsub = (cn + SUB - 1) / SUB;
   const int total = 2 * nsub;                 // K slices, then V slices
-  const int32_t *kbase = kcl + (size_t)g * P * HD;
-  const int32_t *vbase = vcl + (size_t)g * P * HD;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  // this (layer, KV head)'s K or V row of position q
+  auto kv_at = [&](bool isv, int q) -> int32_t * {
+    return (isv ? kv.v : kv.k) + kv_elem(kv, a.NL, a.NKV, HD, a.layer, g, q);
+  };
 
-  auto issue = [&](int i) {                   // one bulk copy: slice i -> ring stage i % STAGES
-    const int j = i < nsub ? i : i - nsub;
+  // slice i -> ring stage i % STAGES: one bulk copy, or two where the slice crosses a page
+  // boundary (a slice of SUB <= 128 positions spans at most two pages of >= 128)
+  auto issue = [&](int i) {
+    const bool isv = i >= nsub;
+    const int j = isv ? i - nsub : i;
     const int pos = c0 + j * SUB;
     const int len = min(SUB, c1 - pos);
     const uint32_t bytes = (uint32_t)len * HD * 4;
     uint64_t *bar = &full[i % ATTN_STAGES];
     mbar_arrive_expect_tx(bar, bytes);
-    bulk_g2s(ring + (i % ATTN_STAGES) * SUB * HD, (i < nsub ? kbase : vbase) + (size_t)pos * HD, bytes, bar);
+    int32_t *dst = ring + (i % ATTN_STAGES) * SUB * HD;
+    const int first = min(len, kv.pg - pos % kv.pg);
+    bulk_g2s(dst, kv_at(isv, pos), (uint32_t)first * HD * 4, bar);
+    if (first < len) bulk_g2s(dst + (size_t)first * HD, kv_at(isv, pos + first), (uint32_t)(len - first) * HD * 4, bar);
   };
 
   // K/V rows before this launch's first new position were written by earlier steps, so a
@@ -1500,7 +1498,7 @@ __global__ void __launch_bounds__(ATTN_THREADS, 2) k_attn(AttnArgs a, int cmax, 
         dst[i] = oa;
         dst[i + HALF] = ob;
         if (is_k) {
-          int32_t *kr = const_cast<int32_t *>(kbase) + (size_t)p * HD;
+          int32_t *kr = kv_at(false, p);
           kr[i] = oa;
           kr[i + HALF] = ob;
         }
@@ -1508,7 +1506,7 @@ __global__ void __launch_bounds__(ATTN_THREADS, 2) k_attn(AttnArgs a, int cmax, 
     }
     if (own) {   // the new V row on the 2^16 grid
       const float *src = row + QD + KVD + g * HD;
-      int32_t *vr = const_cast<int32_t *>(vbase) + (size_t)p * HD;
+      int32_t *vr = kv_at(true, p);
       for (int d = threadIdx.x; d < HD; d += ATTN_THREADS) {
         const float v = src[d];
         int32_t q = 0;

@@ -104,17 +104,36 @@ cudaError_t launch_norm(float *x, const float *add, const float *add_w, const fl
                         int ntok, const DevAct &act, float *nx_out, uint32_t *err, cudaStream_t st,
                         uint32_t *zero_slot = nullptr);
 
-// One token row of a multi-session batch: its session's K/V cache base (layer 0,
-// [NL][NKV][P][HD]), the row's position and the session's capacity P.
+// Where one session's cached K/V rows live: pages of `pg` positions, the session's page j at
+// physical page ptab[j] of a pool whose pages are laid out [NL][NKV][pg][HD] int32 (K and V in
+// separate pools, the same page index in both). ptab == nullptr: the session's own single page,
+// pg = its capacity, i.e. the contiguous [NL][NKV][P][HD] cache.
+struct KvPages {
+  int32_t *k, *v;
+  const int32_t *ptab;
+  int pg;
+};
+
+// element offset of (layer L, KV head g, position p) in k or v; the page table is read where it
+// lives (device code: device tables; host code: a host copy)
+__host__ __device__ inline size_t kv_elem(const KvPages &kv, int NL, int NKV, int HD, int L, int g, int p) {
+  const int j = p / kv.pg;
+  const size_t page = kv.ptab ? (size_t)kv.ptab[j] : 0;
+  return ((page * NL + L) * NKV + g) * (size_t)kv.pg * HD + (size_t)(p - j * kv.pg) * HD;
+}
+
+// One token row of a multi-session batch: its session's K/V pages, the row's position and the
+// session's capacity P.
 struct BatchRow {
-  int32_t *kc, *vc;
+  KvPages kv;
   int32_t pos, P;
 };
 
 struct RopeArgs {
   const float *qkv;        // [ntok][QD + 2*KVD] projections
   int32_t *qi;             // [ntok][QD] rotated q on the 2^16 grid
-  int32_t *kc, *vc;        // this layer's cache [NKV][P][HD]
+  KvPages kv;              // the session's K/V pages (unused with rows)
+  int NL;                  // layers (the page layout's stride)
   const float *q_norm, *k_norm;  // nullable when the model has no QK-norm
   const uint64_t *W;       // turn table [HD/2]
   const uint64_t *T;       // CORDIC arctangent table [30]
@@ -123,23 +142,24 @@ struct RopeArgs {
   int NH, NKV, HD, P, ntok;
   uint32_t *err;
   uint32_t *zero_slot;     // nullable: per-row max slots cleared for the attention output
-  const BatchRow *rows;    // nullable: rows of different sessions (kc, vc, P, pos_dev unused)
-  int layer;               // with rows: the layer whose cache rows are written
+  const BatchRow *rows;    // nullable: rows of different sessions (kv, P, pos_dev unused)
+  int layer;               // the layer whose cache rows are written
 };
 cudaError_t launch_rope_kv(const RopeArgs &a, cudaStream_t st);
 
 struct AttnArgs {
   const int32_t *qi;       // [ntok][NH*HD]
-  const int32_t *kc, *vc;  // this layer's cache [NKV][P][HD]
+  KvPages kv;              // the session's K/V pages (unused with rows)
+  int NL;                  // layers (the page layout's stride)
   float *ao;               // [ntok][NH*HD]
   const int32_t *pos_dev;  // position of token row 0
   int NH, NKV, HD, P, win, ntok;
   float ascale;
   uint32_t *err;
   uint32_t *ao_max;        // nullable: per-row atomicMax of the f32 bits of max |ao|
-  const BatchRow *rows;    // nullable: rows of different sessions (kc, vc, pos_dev unused;
+  const BatchRow *rows;    // nullable: rows of different sessions (kv, pos_dev unused;
                            // P = the largest capacity, sizes the shared memory)
-  int layer;               // with rows: the layer whose cache rows are read
+  int layer;               // the layer whose cache rows are read
   // fused QK-norm + RoPE + K/V store, for rows whose only new position is their own (decode
   // rows, batch rows): with qkv set, every CTA normalises and rotates its query heads itself
   // (qi unused) and the CTA whose position slice ends at the new position stores that

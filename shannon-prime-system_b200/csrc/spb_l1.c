@@ -25,8 +25,9 @@
 #define SPB_L1_MAX_MODELS 32
 
 static pthread_mutex_t g_mu = PTHREAD_MUTEX_INITIALIZER;
-static struct { const void *qm; spb_model *m; } g_models[SPB_L1_MAX_MODELS];
+static struct { const void *qm; spb_model *m; spb_kvpool *pool; } g_models[SPB_L1_MAX_MODELS];
 static int g_device = 0;
+static int g_pool_pg = 0, g_pool_pages = 0;   /* spb_l1_set_kv_pool: 0 = unpaged caches */
 static int g_backend_tag;
 
 static int fail(const char *what) {
@@ -103,24 +104,41 @@ static spb_model *upload(const qwen3_model *qm) {
     return m;
 }
 
-static spb_model *model_for(const void *qm_opaque) {
+static spb_model *model_for(const void *qm_opaque, spb_kvpool **pool) {
     if (!qm_opaque) { sp_set_error("spb200: null model"); return NULL; }
     spb_model *m = NULL;
+    if (pool) *pool = NULL;
     pthread_mutex_lock(&g_mu);
+    int slot = -1;
     for (int i = 0; i < SPB_L1_MAX_MODELS; i++)
-        if (g_models[i].qm == qm_opaque) { m = g_models[i].m; break; }
+        if (g_models[i].qm == qm_opaque) { m = g_models[i].m; slot = i; break; }
     if (!m) {
-        int slot = -1;
         for (int i = 0; i < SPB_L1_MAX_MODELS; i++)
             if (!g_models[i].qm) { slot = i; break; }
         if (slot < 0) sp_set_error("spb200: too many resident models");
         else if ((m = upload((const qwen3_model *)qm_opaque)) != NULL) {
             g_models[slot].qm = qm_opaque;
             g_models[slot].m = m;
+            g_models[slot].pool = NULL;
+            if (g_pool_pg > 0 && spb_kvpool_create(m, g_pool_pg, g_pool_pages, &g_models[slot].pool) != SPB_OK) {
+                fail("kv pool");
+                spb_model_free(m);
+                g_models[slot].qm = NULL;
+                g_models[slot].m = m = NULL;
+            }
         }
     }
+    if (m && pool) *pool = g_models[slot].pool;
     pthread_mutex_unlock(&g_mu);
     return m;
+}
+
+int spb_l1_set_kv_pool(int page_positions, int n_pages) {
+    if (page_positions < 0 || n_pages < 0 || (page_positions > 0 && (page_positions % 128 || n_pages == 0)))
+        return SPB_EBADARG;
+    g_pool_pg = page_positions;
+    g_pool_pages = n_pages;
+    return SPB_OK;
 }
 
 int spb_l1_set_device(int device) {
@@ -133,9 +151,11 @@ void spb_l1_release_model(const void *qm_opaque) {
     pthread_mutex_lock(&g_mu);
     for (int i = 0; i < SPB_L1_MAX_MODELS; i++)
         if (g_models[i].qm == qm_opaque) {
+            spb_kvpool_free(g_models[i].pool);
             spb_model_free(g_models[i].m);
             g_models[i].qm = NULL;
             g_models[i].m = NULL;
+            g_models[i].pool = NULL;
         }
     pthread_mutex_unlock(&g_mu);
 }
@@ -144,7 +164,7 @@ void *spb_l1_backend(void) { return &g_backend_tag; }
 
 int spb_l1_forward(void *handle, const void *qm_opaque, const int32_t *tokens, int n_tok, float *logits) {
     (void)handle;
-    spb_model *m = model_for(qm_opaque);
+    spb_model *m = model_for(qm_opaque, NULL);
     if (!m) return 1;
     if (spb_forward(m, tokens, n_tok, logits) != SPB_OK) return fail("forward");
     return 0;
@@ -154,10 +174,12 @@ int spb_l1_forward(void *handle, const void *qm_opaque, const int32_t *tokens, i
 static int kv_open(const void *qm_opaque, int pmax, sp_kvdecode_handle **out) {
     if (!out) { sp_set_error("spb200: open: null out"); return 1; }
     *out = NULL;
-    spb_model *m = model_for(qm_opaque);
+    spb_kvpool *pool = NULL;
+    spb_model *m = model_for(qm_opaque, &pool);
     if (!m) return 1;
     spb_session *s = NULL;
-    if (spb_session_open(m, pmax, &s) != SPB_OK) return fail("open");
+    const int rc = pool ? spb_session_open_paged(pool, pmax, &s) : spb_session_open(m, pmax, &s);
+    if (rc != SPB_OK) return fail("open");
     *out = (sp_kvdecode_handle *)s;
     return 0;
 }
@@ -183,11 +205,6 @@ static int kv_position(const sp_kvdecode_handle *h) {
 
 static void kv_close(sp_kvdecode_handle *h) { spb_session_close((spb_session *)h); }
 
-static const sp_kvdecode_dispatch_fn g_table = {kv_open, kv_prefill, kv_decode_step,
-                                                kv_rewind, kv_position, kv_close};
-
-const struct sp_kvdecode_dispatch_fn *spb_l1_kvdecode_table(void) { return &g_table; }
-
 int spb_l1_kvdecode_clone(const struct sp_kvdecode_handle *h, struct sp_kvdecode_handle **out) {
     spb_session *c = NULL;
     if (!h || !out) { sp_set_error("spb200: clone: null arg"); return 1; }
@@ -195,3 +212,10 @@ int spb_l1_kvdecode_clone(const struct sp_kvdecode_handle *h, struct sp_kvdecode
     *out = (sp_kvdecode_handle *)c;
     return 0;
 }
+
+/* the frozen six rows (sp_l1.h:403-410) followed by the appended clone row */
+static const struct spb_kvdecode_dispatch_ext g_table = {
+    {kv_open, kv_prefill, kv_decode_step, kv_rewind, kv_position, kv_close}, spb_l1_kvdecode_clone};
+
+const struct sp_kvdecode_dispatch_fn *spb_l1_kvdecode_table(void) { return &g_table.base; }
+const struct spb_kvdecode_dispatch_ext *spb_l1_kvdecode_table_ext(void) { return &g_table; }

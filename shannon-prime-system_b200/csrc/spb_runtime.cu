@@ -552,6 +552,20 @@ extern "C" void spb_model_free(spb_model *m) {
 extern "C" int64_t spb_model_weight_bytes(const spb_model *m) { return m ? m->stream_bytes : 0; }
 
 // ------------------------------------------------------------------------------ session
+// A pool of K/V pages for the paged sessions of one model: page i holds `pg` positions of every
+// layer and KV head, [NL][NKV][pg][HD] int32 for K at k + i * page_elems and for V likewise. A
+// page is shared by the sessions whose page tables name it (refs) and copied before one of them
+// writes into it while another still holds it (copy-on-write), so a clone costs its page table.
+struct spb_kvpool {
+  spb_model *m = nullptr;
+  int pg = 0, npages = 0;
+  size_t page_elems = 0;
+  int32_t *k = nullptr, *v = nullptr;
+  std::mutex mu;
+  std::vector<int32_t> refs;        // sessions holding each page
+  std::vector<int32_t> free_list;
+};
+
 constexpr int NT_MAX = 256;   // token rows per schedule pass (a prefill chunk without logits)
 constexpr int LG_MAX = 64;    // token rows of a pass that produces logits (and of a decode batch)
 
@@ -560,8 +574,11 @@ struct spb_session {
   int pmax;
   int pos;                        // host mirror of pos_dev
   cudaStream_t st = nullptr;
-  uint8_t *buf = nullptr;         // one allocation for cache + scratch
-  int32_t *kc, *vc;               // [NL][NKV][pmax][HD]
+  uint8_t *buf = nullptr;         // one allocation for cache (unpaged) + scratch
+  KvPages kv{};                   // where the K/V rows live: its own [NL][NKV][pmax][HD], or pool pages
+  spb_kvpool *pool = nullptr;     // paged: the pool its pages come from
+  std::vector<int32_t> pages;     // paged: host copy of its page table (-1: no page yet)
+  int32_t *ptab_dev = nullptr;    // paged: the device page table [pages.size()]
   float *x, *qkv, *ao, *ap, *gg, *dn, *logits;
   int32_t *qi;
   DevAct act;
@@ -584,7 +601,7 @@ struct spb_session {
 
 static size_t kv_layer_elems(const spb_model *m, int pmax) { return (size_t)m->NKV * pmax * m->HD; }
 
-extern "C" int spb_session_open(spb_model *m, int pmax, spb_session **out) {
+static int session_open(spb_model *m, int pmax, spb_kvpool *pool, spb_session **out) {
   if (!m || !out || pmax <= 0) return set_err(SPB_EBADARG, "spb_session_open: bad arg");
   *out = nullptr;
   CU(cudaSetDevice(m->device));
@@ -592,11 +609,14 @@ extern "C" int spb_session_open(spb_model *m, int pmax, spb_session **out) {
   s->m = m;
   s->pmax = pmax;
   s->pos = 0;
+  s->pool = pool;
+  const int npg = pool ? (pmax + pool->pg - 1) / pool->pg : 0;
+  if (pool) s->pages.assign((size_t)npg, -1);
   const int E = m->E, QKV = m->QD + 2 * m->KVD, maxK = std::max(std::max(E, m->QD), m->FF);
   size_t off = 0;
   auto take = [&](size_t n) { size_t o = off; off = (off + n + 255) & ~(size_t)255; return o; };
-  const size_t kvn = (size_t)m->NL * kv_layer_elems(m, pmax);
-  const size_t o_kc = take(kvn * 4), o_vc = take(kvn * 4);
+  const size_t kvn = pool ? 0 : (size_t)m->NL * kv_layer_elems(m, pmax);
+  const size_t o_kc = take(kvn * 4), o_vc = take(kvn * 4), o_ptab = take((size_t)npg * 4);
   const size_t o_x = take((size_t)NT_MAX * E * 4), o_qkv = take((size_t)NT_MAX * QKV * 4);
   const size_t o_ao = take((size_t)NT_MAX * m->QD * 4), o_ap = take((size_t)NT_MAX * E * 4);
   const size_t o_gg = take((size_t)NT_MAX * m->FF * 4), o_dn = take((size_t)NT_MAX * E * 4);
@@ -613,7 +633,12 @@ extern "C" int spb_session_open(spb_model *m, int pmax, spb_session **out) {
   cudaError_t e = cudaMalloc(&s->buf, off);
   if (e != cudaSuccess) { delete s; return set_err(SPB_EOOM, "spb_session_open: cudaMalloc(%zu): %s", off, cudaGetErrorString(e)); }
   uint8_t *B = s->buf;
-  s->kc = (int32_t *)(B + o_kc); s->vc = (int32_t *)(B + o_vc);
+  if (pool) {
+    s->ptab_dev = (int32_t *)(B + o_ptab);
+    s->kv = KvPages{pool->k, pool->v, s->ptab_dev, pool->pg};
+  } else {
+    s->kv = KvPages{(int32_t *)(B + o_kc), (int32_t *)(B + o_vc), nullptr, pmax};
+  }
   s->x = (float *)(B + o_x); s->qkv = (float *)(B + o_qkv); s->ao = (float *)(B + o_ao);
   s->ap = (float *)(B + o_ap); s->gg = (float *)(B + o_gg); s->dn = (float *)(B + o_dn);
   s->logits = (float *)(B + o_lg); s->qi = (int32_t *)(B + o_qi);
@@ -641,10 +666,102 @@ extern "C" int spb_session_open(spb_model *m, int pmax, spb_session **out) {
   return SPB_OK;
 }
 
+extern "C" int spb_session_open(spb_model *m, int pmax, spb_session **out) { return session_open(m, pmax, nullptr, out); }
+
+extern "C" int spb_session_open_paged(spb_kvpool *pool, int pmax, spb_session **out) {
+  if (!pool) return set_err(SPB_EBADARG, "spb_session_open_paged: null pool");
+  return session_open(pool->m, pmax, pool, out);
+}
+
+// give back this session's pages (after its stream has drained)
+static void release_pages(spb_session *s) {
+  if (!s->pool) return;
+  std::lock_guard<std::mutex> lk(s->pool->mu);
+  for (int32_t &pg : s->pages) {
+    if (pg >= 0 && --s->pool->refs[pg] == 0) s->pool->free_list.push_back(pg);
+    pg = -1;
+  }
+}
+
+// Make positions [pos, pos + n) writable: every page they touch becomes this session's alone (a
+// fresh page, or a copy of a page another session still holds), then the device page table
+// follows. A copy is waited for before the other holder may write its page in place again.
+static int prepare_write(spb_session *s, int pos, int n) {
+  spb_kvpool *pool = s->pool;
+  if (!pool || n <= 0) return SPB_OK;
+  if (pos < 0 || pos + n > s->pmax) return set_err(SPB_ECONTEXT_FULL, "spb: context full");
+  bool changed = false, copied = false;
+  {
+    std::lock_guard<std::mutex> lk(pool->mu);
+    for (int j = pos / pool->pg; j <= (pos + n - 1) / pool->pg; j++) {
+      const int cur = s->pages[j];
+      if (cur >= 0 && pool->refs[cur] == 1) continue;
+      if (pool->free_list.empty()) return set_err(SPB_EOOM, "spb: the KV page pool has no free page");
+      const int np = pool->free_list.back();
+      pool->free_list.pop_back();
+      pool->refs[np] = 1;
+      if (cur >= 0) {   // shared: copy before writing
+        const size_t bytes = pool->page_elems * 4;
+        CU(cudaMemcpyAsync(pool->k + (size_t)np * pool->page_elems, pool->k + (size_t)cur * pool->page_elems, bytes,
+                           cudaMemcpyDeviceToDevice, s->st));
+        CU(cudaMemcpyAsync(pool->v + (size_t)np * pool->page_elems, pool->v + (size_t)cur * pool->page_elems, bytes,
+                           cudaMemcpyDeviceToDevice, s->st));
+        pool->refs[cur]--;
+        copied = true;
+      }
+      s->pages[j] = np;
+      changed = true;
+    }
+  }
+  if (changed)
+    CU(cudaMemcpyAsync(s->ptab_dev, s->pages.data(), s->pages.size() * 4, cudaMemcpyHostToDevice, s->st));
+  if (copied) CU(cudaStreamSynchronize(s->st));
+  return SPB_OK;
+}
+
+extern "C" int spb_kvpool_create(spb_model *m, int page_positions, int n_pages, spb_kvpool **out) {
+  if (!m || !out || n_pages <= 0 || page_positions < 128 || (page_positions % 128))
+    return set_err(SPB_EBADARG, "spb_kvpool_create: page_positions a positive multiple of 128, n_pages > 0");
+  *out = nullptr;
+  CU(cudaSetDevice(m->device));
+  spb_kvpool *p = new spb_kvpool();
+  p->m = m;
+  p->pg = page_positions;
+  p->npages = n_pages;
+  p->page_elems = (size_t)m->NL * m->NKV * page_positions * m->HD;
+  const size_t bytes = p->page_elems * 4 * (size_t)n_pages;
+  cudaError_t e = cudaMalloc(&p->k, bytes);
+  if (e == cudaSuccess) e = cudaMalloc(&p->v, bytes);
+  if (e != cudaSuccess) {
+    cudaFree(p->k);
+    delete p;
+    return set_err(SPB_EOOM, "spb_kvpool_create: cudaMalloc(2 x %zu): %s", bytes, cudaGetErrorString(e));
+  }
+  p->refs.assign((size_t)n_pages, 0);
+  for (int i = n_pages - 1; i >= 0; i--) p->free_list.push_back(i);
+  *out = p;
+  return SPB_OK;
+}
+
+extern "C" void spb_kvpool_free(spb_kvpool *p) {
+  if (!p) return;
+  cudaSetDevice(p->m->device);
+  cudaFree(p->k);
+  cudaFree(p->v);
+  delete p;
+}
+
+extern "C" int spb_kvpool_free_pages(spb_kvpool *p) {
+  if (!p) return -1;
+  std::lock_guard<std::mutex> lk(p->mu);
+  return (int)p->free_list.size();
+}
+
 extern "C" void spb_session_close(spb_session *s) {
   if (!s) return;
   cudaSetDevice(s->m->device);
   if (s->st) cudaStreamSynchronize(s->st);
+  release_pages(s);
   if (s->step_graph) cudaGraphExecDestroy(s->step_graph);
   if (s->st) cudaStreamDestroy(s->st);
   cudaFreeHost(s->h_pinned);
@@ -698,7 +815,6 @@ static cudaError_t enqueue_rows(spb_session *s, int nt, bool want_logits, const 
     if (r == cudaSuccess) r = launch_scale_i64(s->y64, s->act.scale, nt, E, y, E, st);
     return r;
   };
-  const size_t kvl = kv_layer_elems(m, s->pmax);
   for (int L = 0; L < m->NL; L++) {
     const DevLayer &d = m->layers[L];
     // the attention norm also clears the attention output's max slots (filled by k_attn)
@@ -712,7 +828,7 @@ static cudaError_t enqueue_rows(spb_session *s, int nt, bool want_logits, const 
     K(launch_gemv(d.qkv, nullptr, s->act, nt, s->qkv, QKV, EPI_STORE, s->err_dev, st));
     RopeArgs ra{};
     ra.rows = rows; ra.layer = L;
-    ra.qkv = s->qkv; ra.qi = s->qi; ra.kc = s->kc + (size_t)L * kvl; ra.vc = s->vc + (size_t)L * kvl;
+    ra.qkv = s->qkv; ra.qi = s->qi; ra.kv = s->kv; ra.NL = m->NL;
     ra.q_norm = d.q_norm; ra.k_norm = d.k_norm;
     ra.W = m->tabs + 32 + (d.global ? 0 : m->HD / 2);
     ra.T = m->tabs; ra.gain = m->gain; ra.pos_dev = s->pos_dev;
@@ -721,7 +837,7 @@ static cudaError_t enqueue_rows(spb_session *s, int nt, bool want_logits, const 
     if (!fuse_rope) K(launch_rope_kv(ra, st));
     AttnArgs aa{};
     aa.rows = rows; aa.layer = L;
-    aa.qi = s->qi; aa.kc = ra.kc; aa.vc = ra.vc; aa.ao = s->ao; aa.pos_dev = s->pos_dev;
+    aa.qi = s->qi; aa.kv = s->kv; aa.NL = m->NL; aa.ao = s->ao; aa.pos_dev = s->pos_dev;
     aa.NH = m->NH; aa.NKV = m->NKV; aa.HD = m->HD; aa.P = rows ? Pmax : s->pmax; aa.win = d.win; aa.ntok = nt;
     aa.ascale = ascale; aa.err = s->err_dev; aa.ao_max = s->ao_max;
     if (fuse_rope) {
@@ -787,7 +903,9 @@ extern "C" int spb_session_prefill(spb_session *s, const int32_t *tokens, int n_
   if (n_tok > s->pmax - s->pos) return set_err(SPB_ECONTEXT_FULL, "spb_session_prefill: context full");
   CU(cudaSetDevice(s->m->device));
   const int pos0 = s->pos;
-  int rc = sync_pos(s);
+  int rc = prepare_write(s, s->pos, n_tok);
+  if (rc) return rc;
+  rc = sync_pos(s);
   if (rc) return rc;
   int done = 0;
   while (done < n_tok) {
@@ -831,7 +949,9 @@ extern "C" int spb_session_decode_step_argmax(spb_session *s, int32_t token, flo
   if (!s) return set_err(SPB_EBADARG, "spb_session_decode_step: null session");
   if (s->pos >= s->pmax) return set_err(SPB_ECONTEXT_FULL, "spb_session_decode_step: context full");
   CU(cudaSetDevice(s->m->device));
-  int rc = ensure_step_graph(s);
+  int rc = prepare_write(s, s->pos, 1);
+  if (rc) return rc;
+  rc = ensure_step_graph(s);
   if (rc) return rc;
   s->h_pinned[0] = token;
   CU(cudaMemcpyAsync(s->tok_dev, s->h_pinned, 4, cudaMemcpyHostToDevice, s->st));
@@ -867,10 +987,14 @@ extern "C" int spb_batch_decode_step(spb_session *const *ss, int B, const int32_
     Pmax = std::max(Pmax, s->pmax);
   }
   CU(cudaSetDevice(lead->m->device));
+  for (int i = 0; i < B; i++) {   // every row's new position writable (copy-on-write on its own stream)
+    const int rc = prepare_write(ss[i], ss[i]->pos, 1);
+    if (rc) return rc;
+  }
   for (int i = 1; i < B; i++) CU(cudaStreamSynchronize(ss[i]->st));   // their caches are settled
   for (int i = 0; i < B; i++) {
     lead->h_pinned[i] = tokens[i];
-    lead->h_rows[i] = BatchRow{ss[i]->kc, ss[i]->vc, ss[i]->pos, ss[i]->pmax};
+    lead->h_rows[i] = BatchRow{ss[i]->kv, ss[i]->pos, ss[i]->pmax};
   }
   CU(cudaMemcpyAsync(lead->tok_dev, lead->h_pinned, (size_t)B * 4, cudaMemcpyHostToDevice, lead->st));
   CU(cudaMemcpyAsync(lead->rows_dev, lead->h_rows, (size_t)B * sizeof(BatchRow), cudaMemcpyHostToDevice, lead->st));
@@ -895,7 +1019,9 @@ extern "C" int spb_session_decode_greedy(spb_session *s, int32_t token, int n_st
   if (n_steps > s->pmax - s->pos) return set_err(SPB_ECONTEXT_FULL, "spb_session_decode_greedy: context full");
   if (n_steps == 0) return SPB_OK;
   CU(cudaSetDevice(s->m->device));
-  int rc = ensure_step_graph(s);
+  int rc = prepare_write(s, s->pos, n_steps);
+  if (rc) return rc;
+  rc = ensure_step_graph(s);
   if (rc) return rc;
   s->h_pinned[0] = token;
   CU(cudaMemcpyAsync(s->tok_dev, s->h_pinned, 4, cudaMemcpyHostToDevice, s->st));
@@ -923,15 +1049,29 @@ extern "C" int spb_session_rewind(spb_session *s, int n) {
   return SPB_OK;
 }
 
+// sp_session_clone semantics (sp_session.c:773-816): the clone continues from the same
+// position with the same history and cache. Paged: the clone takes the same pages (O(pages) on
+// the host, no K/V copied; a page is copied later only where one of the two writes into it).
+// Unpaged: a deep copy of the cache on the device.
 extern "C" int spb_session_clone(const spb_session *s, spb_session **out) {
   if (!s || !out) return set_err(SPB_EBADARG, "spb_session_clone: null arg");
-  int rc = spb_session_open(s->m, s->pmax, out);
+  int rc = session_open(s->m, s->pmax, s->pool, out);
   if (rc) return rc;
   spb_session *c = *out;
-  const size_t kvn = (size_t)s->m->NL * kv_layer_elems(s->m, s->pmax);
   CU(cudaStreamSynchronize(s->st));
-  CU(cudaMemcpyAsync(c->kc, s->kc, kvn * 4, cudaMemcpyDeviceToDevice, c->st));
-  CU(cudaMemcpyAsync(c->vc, s->vc, kvn * 4, cudaMemcpyDeviceToDevice, c->st));
+  if (s->pool) {
+    {
+      std::lock_guard<std::mutex> lk(s->pool->mu);
+      for (int32_t pg : s->pages)
+        if (pg >= 0) s->pool->refs[pg]++;
+      c->pages = s->pages;
+    }
+    CU(cudaMemcpyAsync(c->ptab_dev, c->pages.data(), c->pages.size() * 4, cudaMemcpyHostToDevice, c->st));
+  } else {
+    const size_t kvn = (size_t)s->m->NL * kv_layer_elems(s->m, s->pmax);
+    CU(cudaMemcpyAsync(c->kv.k, s->kv.k, kvn * 4, cudaMemcpyDeviceToDevice, c->st));
+    CU(cudaMemcpyAsync(c->kv.v, s->kv.v, kvn * 4, cudaMemcpyDeviceToDevice, c->st));
+  }
   CU(cudaMemcpyAsync(c->hist_dev, s->hist_dev, (size_t)s->pmax * 4, cudaMemcpyDeviceToDevice, c->st));
   c->pos = s->pos;
   rc = sync_pos(c);
@@ -944,10 +1084,15 @@ extern "C" int spb_session_kv_read(const spb_session *s, int layer, int pos, int
   if (!s || !out || layer < 0 || layer >= s->m->NL || pos < 0 || pos >= s->pmax)
     return set_err(SPB_EBADARG, "spb_session_kv_read: bad arg");
   const spb_model *m = s->m;
-  const int32_t *base = (which ? s->vc : s->kc) + (size_t)layer * kv_layer_elems(m, s->pmax);
+  KvPages hk = s->kv;
+  if (s->pool) {
+    if (s->pages[pos / s->pool->pg] < 0) return set_err(SPB_EBADARG, "spb_session_kv_read: position never written");
+    hk.ptab = s->pages.data();   // the host copy of the page table
+  }
+  const int32_t *base = which ? s->kv.v : s->kv.k;
   CU(cudaStreamSynchronize(s->st));
   for (int g = 0; g < m->NKV; g++)
-    CU(cudaMemcpy(out + (size_t)g * m->HD, base + ((size_t)g * s->pmax + pos) * m->HD, (size_t)m->HD * 4,
+    CU(cudaMemcpy(out + (size_t)g * m->HD, base + kv_elem(hk, m->NL, m->NKV, m->HD, layer, g, pos), (size_t)m->HD * 4,
                   cudaMemcpyDeviceToHost));
   return SPB_OK;
 }

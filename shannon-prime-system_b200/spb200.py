@@ -32,10 +32,11 @@ CORE_SYMBOLS = [
     "spb_batch_decode_step", "spb_q4b_prepare", "spb_q4b_release", "spb_q4b_info", "spb_q4b_matmul",
     "spb_tp_shard", "spb_tp_unique_id", "spb_tp_open", "spb_tp_close", "spb_tp_rank", "spb_tp_world",
     "spb_model_synthetic_tp", "spb_model_upload_tp", "spb_tp_p2p_init", "spb_tp_p2p_connect",
-    "spb_tp_p2p_loopback",
+    "spb_tp_p2p_loopback", "spb_kvpool_create", "spb_kvpool_free", "spb_kvpool_free_pages",
+    "spb_session_open_paged",
 ]
 L1_SYMBOLS = ["spb_l1_forward", "spb_l1_backend", "spb_l1_kvdecode_table", "spb_l1_kvdecode_clone",
-              "spb_l1_set_device", "spb_l1_release_model"]
+              "spb_l1_set_device", "spb_l1_release_model", "spb_l1_kvdecode_table_ext", "spb_l1_set_kv_pool"]
 
 
 class SpbError(RuntimeError):
@@ -136,6 +137,9 @@ def load(path: str = CORE_SO):
         "spb_gemv_q4b_noalloc": ([vp, vp, C.c_int, C.c_int, vp, C.c_int, vp, vp], C.c_int),
         "spb_q4b_prepare": ([vp, vp, C.c_int, C.c_int, vp, C.POINTER(vp)], C.c_int),
         "spb_tp_p2p_loopback": ([C.c_int, C.c_uint32, C.c_int, C.c_int], C.c_int),
+        "spb_kvpool_create": ([vp, C.c_int, C.c_int, C.POINTER(vp)], C.c_int),
+        "spb_kvpool_free": ([vp], None), "spb_kvpool_free_pages": ([vp], C.c_int),
+        "spb_session_open_paged": ([vp, C.c_int, C.POINTER(vp)], C.c_int),
         "spb_q4b_release": ([vp], None),
         "spb_q4b_info": ([vp, vp], C.c_int),
         "spb_q4b_matmul": ([vp, vp, C.c_int, vp, vp], C.c_int),
@@ -295,6 +299,28 @@ class Model:
             self.h = None
 
 
+class KvPool:
+    """A pool of paged, copy-on-write K/V pages on the model's device (spb_kvpool_create)."""
+
+    def __init__(self, model, page_positions, n_pages):
+        h = C.c_void_p()
+        check(load().spb_kvpool_create(model.h, page_positions, n_pages, C.byref(h)))
+        self.h, self.model, self.pg, self.n_pages = h, model, page_positions, n_pages
+
+    def session(self, pmax):
+        h = C.c_void_p()
+        check(load().spb_session_open_paged(self.h, pmax, C.byref(h)))
+        return Session(self.model, pmax, handle=h)
+
+    def free_pages(self):
+        return load().spb_kvpool_free_pages(self.h)
+
+    def free(self):
+        if self.h:
+            load().spb_kvpool_free(self.h)
+            self.h = None
+
+
 class Session:
     def __init__(self, model, pmax, handle=None):
         self.model, self.pmax = model, pmax
@@ -404,4 +430,6 @@ def load_l1(path: str = L1_SO):
     L.spb_l1_kvdecode_clone.argtypes = [C.c_void_p, C.POINTER(C.c_void_p)]
     L.spb_l1_set_device.argtypes = [C.c_int]
     L.spb_l1_release_model.argtypes = [C.c_void_p]
+    L.spb_l1_kvdecode_table_ext.restype = C.c_void_p
+    L.spb_l1_set_kv_pool.argtypes = [C.c_int, C.c_int]
     return L

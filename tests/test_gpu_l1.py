@@ -104,3 +104,49 @@ def test_non_q4b_model_rejected(reflib, cuda_ok, tmp_path):
     rc = C.CFUNCTYPE(C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p)(fn.value)(
         None, None, None, 1, None)
     assert rc != 0 and b"null model" in L.sp_last_error()
+
+
+def test_section6b_extended_table_paged_clone(reflib, xr, cuda_ok, tmp_path):
+    """The table with the appended clone row (its first six rows are the frozen table), on a
+    model whose caches live in a page pool: the fork shares pages, both sides stay exact."""
+    cfg = spmodel.CONFIGS["micro_qwen"]
+    T = spmodel.gen_model(cfg, seed=4)
+    mp, tp = str(tmp_path / "m.sp-model"), str(tmp_path / "m.sp-tokenizer")
+    spmodel.write_sp_model(mp, tp, cfg, T)
+    model = reflib.load(mp, tp)
+    l1 = spb200.load_l1()
+    assert l1.spb_l1_set_kv_pool(128, 16) == 0
+    L = reflib.lib
+    s = reflib.session(model, cfg.max_context)
+    qm = L.sp_session_qwen3_model(s)
+    ext = l1.spb_l1_kvdecode_table_ext()
+    assert ext == l1.spb_l1_kvdecode_table()          # the frozen table is the extension's prefix
+    fns = (C.c_void_p * 7).from_address(ext)
+    OPEN = C.CFUNCTYPE(C.c_int, C.c_void_p, C.c_int, C.POINTER(C.c_void_p))
+    PRE = C.CFUNCTYPE(C.c_int, C.c_void_p, C.c_void_p, C.c_int)
+    DEC = C.CFUNCTYPE(C.c_int, C.c_void_p, C.c_int32, C.c_void_p)
+    POS = C.CFUNCTYPE(C.c_int, C.c_void_p)
+    CLOSE = C.CFUNCTYPE(None, C.c_void_p)
+    CLONE = C.CFUNCTYPE(C.c_int, C.c_void_p, C.POINTER(C.c_void_p))
+    h = C.c_void_p()
+    assert OPEN(fns[0])(qm, cfg.max_context, C.byref(h)) == 0
+    toks = spmodel.gen_tokens(35, 40, cfg.n_vocab)
+    assert PRE(fns[1])(h, toks.ctypes.data, toks.size) == 0
+    xs = xr.session(xref.build_desc(cfg, T), cfg.max_context)
+    xs.prefill(toks, all_logits=False)
+    h2 = C.c_void_p()
+    assert CLONE(fns[6])(h, C.byref(h2)) == 0
+    xc = xs.clone()
+    lg = np.empty(cfg.n_vocab, np.float32)
+    for tok_a, tok_b in ((3, 8), (4, 9), (5, 10)):
+        assert DEC(fns[2])(h, tok_a, lg.ctypes.data) == 0
+        assert np.array_equal(u32(lg), u32(xs.step(tok_a)))
+        assert DEC(fns[2])(h2, tok_b, lg.ctypes.data) == 0
+        assert np.array_equal(u32(lg), u32(xc.step(tok_b)))
+    assert POS(fns[4])(h) == POS(fns[4])(h2) == 43
+    CLOSE(fns[5])(h2)
+    CLOSE(fns[5])(h)
+    L.sp_session_destroy(s)
+    l1.spb_l1_release_model(qm)
+    assert l1.spb_l1_set_kv_pool(0, 0) == 0
+    reflib.lib.sp_model_unload(model)
