@@ -68,9 +68,10 @@ def parse():
     p.add_argument("--spec-sessions", type=int, default=8,
                    help="speculative-decode sessions per GPU (configs[4]: 64 over 8 GPUs); 0 skips it")
     p.add_argument("--spec-steps", type=int, default=8)
-    p.add_argument("--tp", action="store_true",
-                   help="N>1: also time one session tensor-parallel over all N GPUs (strong scaling), "
-                        "reported as the line's 'tp' object")
+    p.add_argument("--q8-prefill", type=int, default=4096, help="configs[3] prefill tokens (0 skips configs[3])")
+    p.add_argument("--q8-steps", type=int, default=512)
+    p.add_argument("--no-tp", action="store_true", help="N>1: skip the tensor-parallel objects")
+    p.add_argument("--tp", action="store_true", help="(default with N>1) the tensor-parallel objects")
     return p.parse_args()
 
 
@@ -358,6 +359,49 @@ def measure_batch(m, cfg, B, K, W, seed, max_over_ranks):
                       "B argmaxes D2H per step)", "prefill_s_untimed": round(prefill_s, 2)}
 
 
+def measure_qwen8b(args, local, rank, max_over_ranks, barrier, hbm_gbs):
+    """BASELINE configs[3] on one GPU: the Qwen3-8B shape (36 layers, d 4096, 32/8 heads of 128,
+    SwiGLU FFN 12288, vocab 151936, CORDIC-RoPE), random-init OK_Q4B from a seed; prefill
+    --q8-prefill tokens (CUDA events), then --q8-steps greedy decode steps on the device (CUDA
+    events on the session stream). frac: the bytes a decode token must read (every OK_Q4B
+    weight, and the K/V rows of every layer at the step's context) over the step time, against
+    the measured HBM peak."""
+    import torch
+    import spb200
+    import spmodel
+    cfg = spmodel.CONFIGS["qwen8b"]
+    P, K = args.q8_prefill, args.q8_steps
+    m = spb200.Model.synthetic(cfg, seed=args.seed + 8 + rank, device=local)
+    s = m.session(P + K + 8)
+    stream = torch.cuda.ExternalStream(s.stream(), device=torch.device("cuda", local))
+    toks = spmodel.gen_tokens(args.seed + 300 + rank, P, cfg.n_vocab)
+    e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+    e0.record(stream)
+    s.prefill(toks, logits=False)
+    e1.record(stream)
+    s.greedy(int(toks[-1]), 4)                          # warm-up (builds the step graph)
+    barrier()
+    e2.record(stream)
+    s.greedy(int(toks[-1]), K)
+    e3 = torch.cuda.Event(enable_timing=True)
+    e3.record(stream)
+    e3.synchronize()
+    pre_s = e0.elapsed_time(e1) / 1e3
+    ms = max_over_ranks(e2.elapsed_time(e3))
+    wbytes = m.weight_bytes()
+    ctx_mean = P + 4 + K / 2.0
+    kv_bytes = 2 * cfg.n_layers * cfg.n_head_kv * cfg.head_dim * 4 * ctx_mean
+    step_s = ms / K / 1e3
+    s.close()
+    m.free()
+    return {"workload": f"qwen8b: prefill {P} + {K} greedy decode steps, B=1 (BASELINE configs[3])",
+            "decode_tokens_per_s": round(K / (ms / 1e3), 2), "ms_per_step": round(ms / K, 4),
+            "prefill_s": round(pre_s, 4), "prefill_tokens_per_s": round(P / pre_s, 1),
+            "bytes_per_token": {"weights": wbytes, "kv_mean": int(kv_bytes)},
+            "frac_hbm": round((wbytes + kv_bytes) / step_s / 1e9 / hbm_gbs, 4),
+            "timing": "CUDA events on the session stream; inputs resident (device greedy loop)"}
+
+
 SPEC_PG = 128
 
 
@@ -450,7 +494,7 @@ def measure_tp(cfg, args, rank, local, world, max_over_ranks, barrier, p2p=True)
     s.close()
     m.free()
     tp.close()
-    return {"value": round(K / (ms / 1e3), 3), "unit": "tokens/s", "n_gpus": world, "steps": K,
+    return {"model": cfg.name, "value": round(K / (ms / 1e3), 3), "unit": "tokens/s", "n_gpus": world, "steps": K,
             "ms_per_step": round(ms / K, 4), "scaling": "strong",
             "parallelism": f"tp{world}: heads, FFN columns and LM-head rows split; int64 all-reduce after "
                            f"the attention output and FFN down projections, quantizer-max and argmax-key "
@@ -562,10 +606,19 @@ def run_spb(args):
         spec["unit"] = "accepted tokens/s (all GPUs' sessions)"
         spec["sessions_total"] = world * args.spec_sessions
 
+    q8 = None
+    if args.q8_prefill > 0:
+        q8 = measure_qwen8b(args, local, rank, max_over_ranks, barrier, peaks()[0])
+        q8["decode_tokens_per_s_all_gpus"] = round(world * q8["decode_tokens_per_s"], 2)
+
     tpr = None
-    if args.tp and world > 1:
+    if world > 1 and not args.no_tp:
         tpr = measure_tp(cfg, args, rank, local, world, max_over_ranks, barrier, p2p=True)
         tpr["nccl_only"] = measure_tp(cfg, args, rank, local, world, max_over_ranks, barrier, p2p=False)
+        if args.q8_prefill > 0:
+            import spmodel
+            tpr["qwen8b"] = measure_tp(spmodel.CONFIGS["qwen8b"], args, rank, local, world, max_over_ranks,
+                                       barrier, p2p=True)
 
     cpu = None
     config1 = None
@@ -629,6 +682,7 @@ def run_spb(args):
         "config1": config1,
         "b64": b64,
         "spec": spec,
+        "qwen8b": q8,
         "prefill": prefill,
         "config2_sweep": sweep,
     }

@@ -1928,10 +1928,16 @@ __global__ void k_synth_codes(uint64_t *dst, size_t nwords, uint64_t key) {
     dst[i] = splitmix64(i + key);
 }
 
+// one generated block scale: the matrix's exponent field, the word's low 10 bits as mantissa and
+// its bit 10 as sign (the host generator's rule, spmodel.gen_bscale)
+__device__ __forceinline__ uint16_t synth_scale_bits(uint64_t w, int exp_field) {
+  return (uint16_t)(((uint32_t)exp_field << 10) | (uint32_t)(w & 0x3FFull) | ((uint32_t)((w >> 10) & 1ull) << 15));
+}
+
 __global__ void k_synth_scales(uint16_t *dst, int rows, int nblk, int exp_field, uint64_t key) {
   const size_t n = (size_t)rows * nblk;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
-    dst[i] = (uint16_t)(((uint32_t)exp_field << 10) | (uint32_t)(splitmix64(i + key) & 0x3FFull));
+    dst[i] = synth_scale_bits(splitmix64(i + key), exp_field);
 }
 
 __global__ void k_synth_norm(float *dst, int n, uint64_t key) {
@@ -1970,7 +1976,7 @@ __global__ void k_synth_scales_cols(uint16_t *dst, int rows, int nblk_dst, int n
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
     const size_t r = i / nblk_dst, j = i - r * nblk_dst;
     const uint64_t w = splitmix64(r * (size_t)nblk_src + (size_t)blk_off + j + key);
-    dst[i] = (uint16_t)(((uint32_t)exp_field << 10) | (uint32_t)(w & 0x3FFull));
+    dst[i] = synth_scale_bits(w, exp_field);
   }
 }
 

@@ -11,8 +11,13 @@ CUDA library): every tensor owns a stream id; word(seed, stream, i) is a 64-bit
 splitmix64 hash, so any element can be produced independently.
   * codes   : byte j of a Q4B matrix = byte (j % 8) of word(seed, stream, j // 8)
               -> every nibble uniform over all 16 values (-8..7)
-  * bscale  : f16 with exponent e = floor(log2(1 / (8 * sqrt(cols)))) and a uniform
-              random 10-bit mantissa, i.e. uniform in [2^e, 2^(e+1))
+  * bscale  : f16 with exponent e = floor(log2(1 / (8 * sqrt(cols)))), a uniform random
+              10-bit mantissa and a random sign (bit 10 of the word), i.e. +-uniform in
+              [2^e, 2^(e+1)). The sign matters: uniform nibbles have mean -1/2, so with
+              positive scales every row shares a common-mode component, the gate and up
+              products share it too, and a model without sandwich norms (Qwen3) carries a
+              coherent offset into its residual stream that leaves the exact range within
+              three layers at the 8B width; random signs remove the common mode
   * norms   : (7549747 + (word >> 40) % 1677722) * 2^-23, i.e. in [0.9, 1.1)
   * tokens  : word % n_vocab
 """
@@ -129,7 +134,8 @@ def gen_bscale(seed, stream, rows, cols):
     nblk = (cols + 31) // 32
     e = scale_exponent(cols)
     w = words(seed, stream, rows * nblk)
-    bits = (np.uint64((e + 15) << 10) | (w & np.uint64(0x3FF))).astype(np.uint16)
+    bits = (np.uint64((e + 15) << 10) | (w & np.uint64(0x3FF)) |
+            (((w >> np.uint64(10)) & np.uint64(1)) << np.uint64(15))).astype(np.uint16)
     return bits.reshape(rows, nblk)
 
 

@@ -71,6 +71,8 @@ def test_generator_is_deterministic_and_uniform():
     s = spmodel.gen_bscale(0, 11, 64, 512).astype(np.uint32)
     e = (s >> 10) & 31
     assert np.all(e == spmodel.scale_exponent(512) + 15)
+    neg = (s >> 15) & 1                                  # random signs: no common-mode row offset
+    assert 0.45 < neg.mean() < 0.55
     w = spmodel.gen_norm(0, 12, 1000)
     assert w.min() >= 0.9 and w.max() < 1.1
 
