@@ -557,7 +557,9 @@ def run_spb(args):
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
+    torch.cuda.nvtx.range_push("decode_steps")   # selects these launches for an ncu launch list
     generated = s.greedy(tok, K)
+    torch.cuda.nvtx.range_pop()
     e1.record(stream)
     e1.synchronize()
     ms = max_over_ranks(e0.elapsed_time(e1))

@@ -1381,8 +1381,7 @@ __global__ void __launch_bounds__(ATTN_THREADS, 2) k_attn(AttnArgs a, int cmax, 
   __shared__ int32_t mx_in[16][G];        // CL > 1: each rank's score maximum, pushed by that rank
   __shared__ int64_t s_in[16][G];         // CL > 1: each rank's exponential sum
   __shared__ float fred[33];
-  __shared__ acc128 gred[ATTN_THREADS / 32];   // fused: per-warp QK-norm sums of squares
-  __shared__ uint64_t ginv[ATTN_THREADS / 32]; // fused: inverse rms per head group
+  __shared__ uint64_t ginv[9];                  // fused: inverse rms of each rotated head (G + 1 <= 9)
 
   const int rank = CL > 1 ? (int)cluster.block_rank() : 0;
   // the partials are pushed into the owning rank's shared memory (no remote loads): this
@@ -1446,27 +1445,35 @@ __global__ void __launch_bounds__(ATTN_THREADS, 2) k_attn(AttnArgs a, int cmax, 
   if (!fused) {
     for (int i = threadIdx.x; i < G * HD; i += ATTN_THREADS) qs[i] = a.qi[(size_t)t * QD + (size_t)g * G * HD + i];
   } else {
-    // QK-norm + CORDIC-RoPE of the G query heads (and, for the owner, the new K row), HD/2
-    // threads per head, one pair each, the same island steps as k_rope_kv
-    constexpr int HALF = HD / 2, GPP = ATTN_THREADS / HALF, WPG = HALF / 32;
+    // QK-norm + CORDIC-RoPE of the G query heads (and, for the owner, the new K row): item x =
+    // pair x % HALF of rotated head x / HALF, thread tid takes items tid, tid + 256, ...; every
+    // head's sum of squares is reduced in the same pass (a warp's items share one head), the
+    // inverse rms of the heads is found by one thread each, then every item is normalised and
+    // rotated -- the same island steps as k_rope_kv, in one pass however many heads rotate
+    constexpr int HALF = HD / 2, WPH = HALF / 32;   // warps per head in one item round
+    constexpr int NIT = ((G + 1) * HALF + ATTN_THREADS - 1) / ATTN_THREADS;
+    constexpr int NW = ATTN_THREADS / 32;
+    static_assert(NIT * NW * (int)sizeof(acc128) <= G * HD * 4, "norm partials fit the q staging");
+    acc128 *part = reinterpret_cast<acc128 *>(qs);   // [NIT][NW] per-warp sums, before qs is written
     const int KVD = a.NKV * HD;
     const float *row = a.qkv + (size_t)t * (QD + 2 * KVD);
-    const int gi = threadIdx.x / HALF, i = threadIdx.x % HALF;
-    const int nrot = G + (own ? 1 : 0);
-    const uint64_t phase = (uint64_t)(int64_t)p * a.W[i];
-    for (int j0 = 0; j0 < nrot; j0 += GPP) {
-      const int j = j0 + gi;
-      const bool act = j < nrot, is_k = j == G;
-      const float *src = row + (is_k ? QD + g * HD : (g * G + j) * HD);
-      float x0 = act ? src[i] : 0.0f, x1 = act ? src[i + HALF] : 0.0f;
-      if (a.q_norm) {
+    const int nrot = G + (own ? 1 : 0), nitems = nrot * HALF;
+    float x0[NIT], x1[NIT];
+#pragma unroll
+    for (int k = 0; k < NIT; k++) {
+      const int item = threadIdx.x + k * ATTN_THREADS, j = item / HALF, i = item % HALF;
+      const bool act = item < nitems;
+      const float *src = row + (j == G ? QD + g * HD : (g * G + j) * HD);
+      x0[k] = act ? src[i] : 0.0f;
+      x1[k] = act ? src[i + HALF] : 0.0f;
+      if (a.q_norm && k * ATTN_THREADS < nitems) {   // (warp-uniform: whole rounds of items)
         acc128 ss{0ull, 0ll};
         bool bad = false;
         if (act) {
-          if (!(fabsf(x0) < 32768.0f)) bad = true;
-          else { const int64_t xi = q16_round(x0); acc128_add(ss, xi * xi); }
-          if (!(fabsf(x1) < 32768.0f)) bad = true;
-          else { const int64_t xi = q16_round(x1); acc128_add(ss, xi * xi); }
+          if (!(fabsf(x0[k]) < 32768.0f)) bad = true;
+          else { const int64_t xi = q16_round(x0[k]); acc128_add(ss, xi * xi); }
+          if (!(fabsf(x1[k]) < 32768.0f)) bad = true;
+          else { const int64_t xi = q16_round(x1[k]); acc128_add(ss, xi * xi); }
         }
         if (bad) raise_err(a.err, ERR_NORM_RANGE);
 #pragma unroll
@@ -1476,32 +1483,40 @@ __global__ void __launch_bounds__(ATTN_THREADS, 2) k_attn(AttnArgs a, int cmax, 
           r.hi = __shfl_xor_sync(0xffffffffu, ss.hi, o);
           acc128_add(ss, r);
         }
-        if (lane == 0) gred[warp] = ss;
-        __syncthreads();
-        if (act && i == 0) {
-          acc128 tot = gred[gi * WPG];
-          for (int w = 1; w < WPG; w++) acc128_add(tot, gred[gi * WPG + w]);
-          ginv[gi] = rms_inv(tot, HD, a.err);
-        }
-        __syncthreads();
-        if (act) {
-          const float *nw = is_k ? a.k_norm : a.q_norm;
-          const uint64_t inv = ginv[gi];
-          x0 = rms_apply(x0, nw[i], inv, a.err);
-          x1 = rms_apply(x1, nw[i + HALF], inv, a.err);
-        }
+        if (lane == 0) part[k * NW + warp] = ss;
       }
-      if (act) {
-        int32_t oa, ob;
-        cordic_rotate(x0, x1, phase, a.T, a.gain, oa, ob, a.err);
-        int32_t *dst = is_k ? kvn : qs + j * HD;
-        dst[i] = oa;
-        dst[i + HALF] = ob;
-        if (is_k) {
-          int32_t *kr = kv_at(false, p);
-          kr[i] = oa;
-          kr[i + HALF] = ob;
-        }
+    }
+    if (a.q_norm) {
+      __syncthreads();
+      if (threadIdx.x < nrot) {   // head h's items h HALF .. + HALF: round (h HALF) / 256, WPH warps
+        const int h = threadIdx.x, k = (h * HALF) / ATTN_THREADS, w0 = ((h * HALF) % ATTN_THREADS) / 32;
+        acc128 tot = part[k * NW + w0];
+        for (int w = 1; w < WPH; w++) acc128_add(tot, part[k * NW + w0 + w]);
+        ginv[h] = rms_inv(tot, HD, a.err);
+      }
+      __syncthreads();   // (the partials in qs are read: qs may be written from here)
+    }
+#pragma unroll
+    for (int k = 0; k < NIT; k++) {
+      const int item = threadIdx.x + k * ATTN_THREADS, j = item / HALF, i = item % HALF;
+      if (item >= nitems) continue;
+      const bool is_k = j == G;
+      float v0 = x0[k], v1 = x1[k];
+      if (a.q_norm) {
+        const float *nw = is_k ? a.k_norm : a.q_norm;
+        const uint64_t inv = ginv[j];
+        v0 = rms_apply(v0, nw[i], inv, a.err);
+        v1 = rms_apply(v1, nw[i + HALF], inv, a.err);
+      }
+      int32_t oa, ob;
+      cordic_rotate(v0, v1, (uint64_t)(int64_t)p * a.W[i], a.T, a.gain, oa, ob, a.err);
+      int32_t *dst = is_k ? kvn : qs + j * HD;
+      dst[i] = oa;
+      dst[i + HALF] = ob;
+      if (is_k) {
+        int32_t *kr = kv_at(false, p);
+        kr[i] = oa;
+        kr[i + HALF] = ob;
       }
     }
     if (own) {   // the new V row on the 2^16 grid
