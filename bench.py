@@ -589,8 +589,18 @@ def run_spb(args):
         shapes, tot_b, tot_us, gl = gemv_roofline(cfg, spb, torch.device("cuda", local), stream)
         peak, peak_kind = peaks()
         achieved = tot_b / tot_us / 1e3
+        # DRAM bytes per launch from one ncu capture of the 12B-width decode GEMVs
+        # (profiles/k_gemv_decode_gemma12b_width.md); the LM head was not in that capture and is
+        # counted at its algorithmic bytes. Per token, like `achieved`.
+        traffic = None
+        if cfg.name == "gemma12b":
+            per_launch = {"qkv": 17.72e6, "o": 8.87e6, "gate_up": 66.70e6, "down": 33.22e6}
+            traffic = int(sum(per_launch[n] * k for n, r, c, g, k in gemv_shapes(cfg) if n in per_launch) +
+                          gemv_bytes(cfg.n_vocab, cfg.n_embd, False))
         roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                "frac": round(achieved / peak, 4), "traffic": None,
+                "frac": round(achieved / peak, 4), "traffic": traffic,
+                "traffic_source": "ncu dram bytes per launch (profiles/k_gemv_decode_gemma12b_width.md), "
+                                  "x launches per token; LM head at its algorithmic bytes",
                 "peak_source": f"{peak_kind} hbm_gbs (burst copy)", "kernel": "k_gemv (OK_Q4B dequant-GEMV, M=1)",
                 "algorithmic_bytes_per_token": int(tot_b), "gemv_us_per_token": round(tot_us, 1),
                 "per_shape": shapes}
