@@ -526,7 +526,9 @@ def run_spb(args):
     t0 = time.perf_counter()
     p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     p0.record(stream)
+    torch.cuda.nvtx.range_push("prefill")   # selects these launches for an ncu launch list
     s.prefill(toks, logits=False)
+    torch.cuda.nvtx.range_pop()
     p1.record(stream)
     p1.synchronize()
     prefill_s = time.perf_counter() - t0

@@ -45,10 +45,12 @@ constexpr int TC_THREADS = 32 * (2 + TC_CONV_WARPS);
 constexpr int TC_PLANE = TC_BM * TC_BK;   // bytes of one plane tile
 constexpr int TC_SMEM_BUDGET = 225 * 1024;
 
-template <int P, int NM>
+// SN: the 64-token tile for batches of at most 64 rows (the multi-session decode step), where the
+// larger tiles would mostly multiply zero rows
+template <int P, int NM, bool SN = false>
 struct TcShape {
   static constexpr int PM = P * NM;
-  static constexpr int N = PM == 2 ? 256 : PM == 3 ? 160 : PM == 4 ? 128 : 80;   // token rows per CTA
+  static constexpr int N = SN ? 64 : PM == 2 ? 256 : PM == 3 ? 160 : PM == 4 ? 128 : 80;   // token rows per CTA
   static constexpr int COLS = PM * N;                                             // tensor-memory columns used
   static constexpr int TMEM_COLS = COLS <= 256 ? 256 : 512;
   static constexpr int A_BYTES = PM * TC_PLANE;
@@ -183,12 +185,13 @@ __device__ __forceinline__ void convert_block(const uint4 cw, int32_t mult, uint
   }
 }
 
-template <int P, int NM, int EPI, int PF>
+template <int P, int NM, int EPI, bool SN>
 __global__ void __launch_bounds__(TC_THREADS, 1)
 k_gemm_tc(const __grid_constant__ CUtensorMap tmb, DevQ4B w, DevQ4B w2, DevAct act, int ntok, int ks, float *y,
           int ldy, uint32_t *err, uint32_t *ymax, unsigned long long *amax) {
-  using SH = TcShape<P, NM>;
+  using SH = TcShape<P, NM, SN>;
   constexpr int N = SH::N, S = SH::S;
+  constexpr int PF = 2;   // stages of codes and scales in flight in the converters' registers
   extern __shared__ uint8_t tsm_raw[];
   __shared__ __align__(8) uint64_t full_a[S], full_b[S], empty[S], tfull;
   __shared__ uint32_t tmem_base_sh;
@@ -457,11 +460,11 @@ bool tc_enabled() {
   return on != 0;
 }
 
-template <int P, int NM, int EPI, int PF>
-cudaError_t tc_launch_pf(const DevQ4B &w, const DevQ4B &w2, const DevAct &act, int ntok, float *y, int ldy, uint32_t *err,
+template <int P, int NM, int EPI, bool SN>
+cudaError_t tc_launch_sn(const DevQ4B &w, const DevQ4B &w2, const DevAct &act, int ntok, float *y, int ldy, uint32_t *err,
                       uint32_t *ymax, unsigned long long *amax, cudaStream_t st, int ks, bool pdl) {
-  using SH = TcShape<P, NM>;
-  auto kern = k_gemm_tc<P, NM, EPI, PF>;
+  using SH = TcShape<P, NM, SN>;
+  auto kern = k_gemm_tc<P, NM, EPI, SN>;
   static bool configured = false;
   if (!configured) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SH::SMEM);
@@ -496,25 +499,11 @@ cudaError_t tc_launch_pf(const DevQ4B &w, const DevQ4B &w2, const DevAct &act, i
   return cudaLaunchKernelEx(&cfg, kern, tm, w, w2, act, ntok, ks, y, ldy, err, ymax, amax);
 }
 
-// converter prefetch depth in stages (SPB_TC_PF: 1, 2 or 3; default 2)
-int tc_prefetch() {
-  static int n = -1;
-  if (n < 0) {
-    const char *e = getenv("SPB_TC_PF");
-    n = e ? atoi(e) : 2;
-    if (n < 1 || n > 3) n = 2;
-  }
-  return n;
-}
-
 template <int P, int NM, int EPI>
 cudaError_t tc_launch(const DevQ4B &w, const DevQ4B &w2, const DevAct &act, int ntok, float *y, int ldy, uint32_t *err,
                       uint32_t *ymax, unsigned long long *amax, cudaStream_t st, int ks, bool pdl) {
-  switch (tc_prefetch()) {
-    case 1: return tc_launch_pf<P, NM, EPI, 1>(w, w2, act, ntok, y, ldy, err, ymax, amax, st, ks, pdl);
-    case 3: return tc_launch_pf<P, NM, EPI, 3>(w, w2, act, ntok, y, ldy, err, ymax, amax, st, ks, pdl);
-    default: return tc_launch_pf<P, NM, EPI, 2>(w, w2, act, ntok, y, ldy, err, ymax, amax, st, ks, pdl);
-  }
+  if (ntok <= 64) return tc_launch_sn<P, NM, EPI, true>(w, w2, act, ntok, y, ldy, err, ymax, amax, st, ks, pdl);
+  return tc_launch_sn<P, NM, EPI, false>(w, w2, act, ntok, y, ldy, err, ymax, amax, st, ks, pdl);
 }
 
 template <int EPI>

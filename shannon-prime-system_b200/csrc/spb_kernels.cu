@@ -673,12 +673,13 @@ static bool splitk_enabled() {
   return on != 0;
 }
 
-// token rows from which a batch runs the tcgen05 GEMM (SPB_TC_MIN; SPB_TC=0 never)
+// token rows from which a batch runs the tcgen05 GEMM (SPB_TC_MIN; SPB_TC=0 never): 16, where its
+// 64-token tile already beats the mma.sync GEMM (64-session batch 3367 -> 3724 tok/s)
 static int tc_min_tokens() {
   static int n = -1;
   if (n < 0) {
     const char *e = getenv("SPB_TC_MIN");
-    n = e ? atoi(e) : 128;
+    n = e ? atoi(e) : 16;
     if (n < 1) n = 1;
   }
   return n;
@@ -706,8 +707,8 @@ cudaError_t launch_gemv(const DevQ4B &w, const DevQ4B *w2, const DevAct &act, in
   // (row tile x token tile) grid would leave most SMs idle
   if (ntok >= tc_min_tokens() && grid_limit == 0 && gemm_enabled() && gemm_tc_covers(w, w2, epi, ntok)) {
     const int P = gemm_tc_covers(w, w2, epi, ntok);
-    const int N = P * (epi_pair(epi) ? 2 : 1) == 2 ? 256 : P * (epi_pair(epi) ? 2 : 1) == 3 ? 160
-                : P * (epi_pair(epi) ? 2 : 1) == 4 ? 128 : 80;
+    const int PM = P * (epi_pair(epi) ? 2 : 1);   // token tile of the GEMM's launch (TcShape::N)
+    const int N = ntok <= 64 ? 64 : PM == 2 ? 256 : PM == 3 ? 160 : PM == 4 ? 128 : 80;
     const long tiles = (long)((ntok + N - 1) / N) * ((w.rows + 127) / 128);
     const int nk = w.cols / 128;
     int ks = 1;
