@@ -1734,6 +1734,361 @@ __global__ void __launch_bounds__(ATTN_THREADS, 2) k_attn(AttnArgs a, int cmax, 
 }
 
 
+// ---- prefill rows in tiles: the rows of one prefill chunk are consecutive positions of one
+// session and read the same K/V rows, so one CTA takes ATILE_QV query vectors of one KV head
+// (TQ = ATILE_QV / G consecutive rows x the G query heads that share it) and every staged K/V
+// slice serves all of them, where the per-row kernel streams it once per row. Scores of the
+// union of the rows' windows, each query's maximum, the island's exponentials with their exact
+// int64 sums, then the 128-bit V-sums. ST (stored): the scores stay in shared memory between the
+// K pass and the V pass; otherwise (a union too long for shared memory) a second K pass
+// recomputes them slice by slice, K and V slices alternating through the ring. A position
+// outside a row's own window (a later position of the chunk, or one before the row's sliding
+// window) weighs exactly 0, so every integer is the per-row kernel's.
+constexpr int ATILE_QV = 16;
+constexpr int ATILE_STAGES = 3;
+
+template <int HD>
+struct AttnTile {
+  static constexpr int SUB = 4096 / HD;                       // positions per ring stage (16 KB)
+  static constexpr int V4 = HD / 32;                          // int4 columns per lane of an 8-lane group
+  static constexpr int QG = SUB >= 32 ? 1 : 32 / SUB;         // query subsets over the 32 groups
+  static constexpr int NPG = 32 / QG;                         // position slots per subset
+  static constexpr int PPG = SUB > NPG ? SUB / NPG : 1;       // positions per group per slice
+  static constexpr int QPG = ATILE_QV / QG;                   // query vectors per group
+  static constexpr int KEEP = QPG / 8;                        // scores each lane keeps per position
+  static constexpr int GROUPS = ATTN_THREADS / HD;            // position groups of the V-sum
+  static constexpr size_t RING = (size_t)ATILE_STAGES * SUB * HD * 4;
+  // + the scores of the whole union when stored, else the exponentials of one slice
+  static constexpr size_t BASE = RING + (size_t)ATILE_QV * HD * 4;
+  static size_t smem(bool st, int cmax) { return BASE + (size_t)ATILE_QV * (st ? cmax : SUB) * 4; }
+  static_assert(NPG * PPG == SUB && QPG % 8 == 0, "every (query, position) of a slice has one group");
+  static_assert(16 * GROUPS == SUB, "each V-sum thread folds two runs of 8 positions per slice");
+  static_assert((size_t)(GROUPS - 1) * ATILE_QV * HD * sizeof(acc128) <= RING, "V-sum partials fit the ring");
+};
+
+template <int HD, int G, bool ST>
+__global__ void __launch_bounds__(ATTN_THREADS, ST ? 1 : 2) k_attn_tile(AttnArgs a, int cmax) {
+  using AT = AttnTile<HD>;
+  constexpr int SUB = AT::SUB, V4 = AT::V4, NPG = AT::NPG, PPG = AT::PPG, QPG = AT::QPG, KEEP = AT::KEEP;
+  constexpr int GROUPS = AT::GROUPS, QV = ATILE_QV, TQ = ATILE_QV / G, S = ATILE_STAGES;
+  extern __shared__ __align__(128) uint8_t at_raw[];
+  int32_t *ring = reinterpret_cast<int32_t *>(at_raw);   // [S][SUB][HD]
+  int32_t *qs = ring + S * SUB * HD;                       // [QV][HD] rotated queries
+  int32_t *es = qs + QV * HD;                              // [QV][ST ? cmax : SUB] scores -> exponentials
+  const int estride = ST ? cmax : SUB;
+  __shared__ __align__(8) uint64_t full[S];
+  __shared__ int32_t mx[QV];
+  __shared__ unsigned long long ssum[QV];
+  __shared__ uint32_t omx[TQ];
+
+  const int g = blockIdx.y, t0 = blockIdx.x * TQ, tid = threadIdx.x, lane = tid & 31;
+  const int QD = a.NH * HD;
+  const int nrow = min(TQ, a.ntok - t0);
+  pdl_trigger();
+  if (tid == 0) {
+    for (int s = 0; s < S; s++) mbar_init(&full[s], 1);
+    mbar_init_fence();
+  }
+  if (tid < QV) { mx[tid] = INT32_MIN; ssum[tid] = 0ull; }
+  if (tid < TQ) omx[tid] = 0u;
+  pdl_wait();
+  const int pbase = a.pos_dev[0] + t0;   // position of the tile's first row
+  auto wstart = [&](int p) { return (a.win >= 0 && p - a.win + 1 > 0) ? p - a.win + 1 : 0; };
+  const int u0 = wstart(pbase), u1 = pbase + nrow;   // the union of the rows' windows: [u0, u1)
+  const int ulen = u1 - u0;
+  if (ST && ulen > cmax) {   // (the launch sized cmax for every tile; never taken)
+    if (tid == 0) raise_err(a.err, ERR_SCORE_RANGE);
+    return;
+  }
+  const int nsl = (ulen + SUB - 1) / SUB;
+  const int total = (ST ? 2 : 3) * nsl;
+  auto kv_at = [&](bool isv, int q) -> int32_t * {
+    return (isv ? a.kv.v : a.kv.k) + kv_elem(a.kv, a.NL, a.NKV, HD, a.layer, g, q);
+  };
+  // item i -> (slice, K or V): ST: the K slices, then the V slices; otherwise pass A's K slices,
+  // then pass B's K and V slices alternating
+  auto item = [&](int i, int &sl) -> bool {
+    if (i < nsl) { sl = i; return false; }
+    if (ST) { sl = i - nsl; return true; }
+    sl = (i - nsl) >> 1;
+    return ((i - nsl) & 1) != 0;
+  };
+  // a slice of SUB <= 64 positions spans at most two pages of >= 128
+  auto issue = [&](int i) {
+    int sl;
+    const bool isv = item(i, sl);
+    const int pos = u0 + sl * SUB;
+    const int len = min(SUB, u1 - pos);
+    uint64_t *bar = &full[i % S];
+    mbar_arrive_expect_tx(bar, (uint32_t)len * HD * 4);
+    int32_t *dst = ring + (i % S) * SUB * HD;
+    const int first = min(len, a.kv.pg - pos % a.kv.pg);
+    bulk_g2s(dst, kv_at(isv, pos), (uint32_t)first * HD * 4, bar);
+    if (first < len) bulk_g2s(dst + (size_t)first * HD, kv_at(isv, pos + first), (uint32_t)(len - first) * HD * 4, bar);
+  };
+  for (int i = tid; i < QV * HD; i += ATTN_THREADS) {
+    const int qv = i / HD, d = i - qv * HD, r = qv / G, h = qv - r * G;
+    qs[i] = r < nrow ? a.qi[(size_t)(t0 + r) * QD + (size_t)(g * G + h) * HD + d] : 0;
+  }
+  __syncthreads();   // barriers initialised, queries staged
+  if (tid == 0)
+    for (int i = 0; i < min(S, total); i++) issue(i);
+  auto next = [&](int i) {   // after the __syncthreads that freed item i's stage
+    if (tid == 0 && i + S < total) {
+      fence_proxy_async_smem();
+      issue(i + S);
+    }
+  };
+
+  // scores: 8-lane group gi takes slot gi % NPG of query subset gi / NPG; lane j of the group
+  // holds the int4 columns 4j + 32v of the position's K row; after the three-level butterfly
+  // lane (l % 8) keeps the raw score of the group's query l, and the conversions run once all
+  // queries are reduced, every lane busy
+  const int gi = tid >> 3, gj = tid & 7, qsub = gi / NPG, pslot = gi % NPG;
+  auto valid_at = [&](int qv, int jpos) {
+    const int r = qv / G;
+    const int p = pbase + r;
+    return r < nrow && jpos <= p && jpos >= wstart(p);
+  };
+  auto to_grid = [&](int64_t sv, bool ok) -> int32_t {
+    float z = __fmul_rn(__double2float_rn(__dmul_rn(__ll2double_rn(sv), 0x1p-32)), a.ascale);
+    if (!(fabsf(z) < 131072.0f)) {
+      if (ok) raise_err(a.err, ERR_SCORE_RANGE);
+      z = 0.0f;
+    }
+    return (int32_t)llround_d((double)z * 16384.0);
+  };
+  auto score = [&](const int32_t *buf, int sl, int len, auto &&use) {
+#pragma unroll 1
+    for (int r = 0; r < PPG; r++) {
+      const int pp = pslot + r * NPG;
+      const bool inb = pp < len;
+      const int32_t *kr = buf + (inb ? pp : 0) * HD + 4 * gj;
+      int4 kv[V4];
+#pragma unroll
+      for (int v = 0; v < V4; v++) kv[v] = *reinterpret_cast<const int4 *>(kr + 32 * v);
+      int64_t kept[KEEP];
+#pragma unroll
+      for (int l = 0; l < QPG; l++) {
+        const int32_t *qr = qs + (qsub * QPG + l) * HD + 4 * gj;
+        int64_t acc = 0;
+#pragma unroll
+        for (int v = 0; v < V4; v++) {
+          const int4 q = *reinterpret_cast<const int4 *>(qr + 32 * v);
+          acc += (int64_t)q.x * kv[v].x;
+          acc += (int64_t)q.y * kv[v].y;
+          acc += (int64_t)q.z * kv[v].z;
+          acc += (int64_t)q.w * kv[v].w;
+        }
+        acc += __shfl_xor_sync(0xffffffffu, acc, 4);
+        acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+        acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+        if ((l & 7) == gj) kept[l >> 3] = acc;
+      }
+#pragma unroll
+      for (int k = 0; k < KEEP; k++) {
+        const int qv = qsub * QPG + gj + 8 * k;
+        use(k, qv, pp, kept[k], inb && valid_at(qv, u0 + sl * SUB + pp));
+      }
+    }
+  };
+  int64_t lsum[KEEP];
+#pragma unroll
+  for (int k = 0; k < KEEP; k++) lsum[k] = 0;
+  auto exps_into = [&](int k, int qv, int idx, int32_t zi, bool ok) {
+    int64_t e = 0;
+    if (ok) e = exp_fixed((((int64_t)zi - (int64_t)mx[qv]) * ONE) >> 14);
+    es[qv * estride + idx] = (int32_t)e;
+    lsum[k] += e;
+  };
+
+  // ---- K pass: each query's maximum over its own window (ST: and its scores)
+  int32_t lmax[KEEP];
+#pragma unroll
+  for (int k = 0; k < KEEP; k++) lmax[k] = INT32_MIN;
+  for (int i = 0; i < nsl; i++) {
+    const int stage = i % S;
+    mbar_wait(&full[stage], (uint32_t)(i / S) & 1u, a.err);
+    score(ring + stage * SUB * HD, i, min(SUB, u1 - (u0 + i * SUB)), [&](int k, int qv, int pp, int64_t sv, bool ok) {
+      if (ok) {
+        const int32_t zi = to_grid(sv, true);
+        lmax[k] = max(lmax[k], zi);
+        if (ST) es[qv * estride + i * SUB + pp] = zi;
+      }
+    });
+    __syncthreads();
+    next(i);
+  }
+#pragma unroll
+  for (int k = 0; k < KEEP; k++) {   // the warp's four groups hold the same queries
+    int32_t m = lmax[k];
+    m = max(m, __shfl_xor_sync(0xffffffffu, m, 8));
+    m = max(m, __shfl_xor_sync(0xffffffffu, m, 16));
+    if (lane < 8 && m != INT32_MIN) atomicMax(&mx[qsub * QPG + gj + 8 * k], m);
+  }
+  __syncthreads();
+  if (ST) {   // exponentials of the stored scores: thread tid takes positions tid, tid + 256, ...
+    for (int q = 0; q < QV; q++) {
+      int64_t sm = 0;
+      for (int j = tid; j < ulen; j += ATTN_THREADS) {
+        int64_t e = 0;
+        if (valid_at(q, u0 + j)) e = exp_fixed((((int64_t)es[q * estride + j] - (int64_t)mx[q]) * ONE) >> 14);
+        es[q * estride + j] = (int32_t)e;
+        sm += e;
+      }
+      sm = warp_sum_i64(sm);
+      if (lane == 0 && sm) atomicAdd(&ssum[q], (unsigned long long)sm);
+    }
+    __syncthreads();
+  }
+
+  // ---- V pass (not ST: K slices again for the exponentials, alternating with the V slices):
+  // thread (d, grp) folds the run of 16 positions grp * 16 .. of each slice, eight per fold
+  // into 128 bits (e <= 2^30 and |v| < 2^30, so 8 |e v| < 2^63); positions past len weigh 0
+  const int d = tid % HD, grp = tid / HD;
+  acc128 acc[QV];
+#pragma unroll
+  for (int q = 0; q < QV; q++) acc[q] = acc128{0ull, 0ll};
+  for (int i = nsl; i < total; i++) {
+    const int stage = i % S;
+    mbar_wait(&full[stage], (uint32_t)(i / S) & 1u, a.err);
+    const int32_t *buf = ring + stage * SUB * HD;
+    int sl;
+    const bool isv = item(i, sl);
+    const int len = min(SUB, u1 - (u0 + sl * SUB));
+    if (!isv) {
+      score(buf, sl, len, [&](int k, int qv, int pp, int64_t sv, bool ok) {
+        exps_into(k, qv, pp, ok ? to_grid(sv, false) : 0, ok);
+      });
+    } else {
+      const int32_t *eb = es + (ST ? sl * SUB : 0);
+#pragma unroll
+      for (int f = 0; f < 2; f++) {
+        const int pb = grp * 16 + f * 8;
+        if (pb < len) {
+          int64_t v[8];
+#pragma unroll
+          for (int u = 0; u < 8; u++) v[u] = pb + u < len ? (int64_t)buf[(pb + u) * HD + d] : 0;
+#pragma unroll
+          for (int q = 0; q < QV; q++) {
+            const int4 e0 = *reinterpret_cast<const int4 *>(eb + q * estride + pb);
+            const int4 e1 = *reinterpret_cast<const int4 *>(eb + q * estride + pb + 4);
+            int64_t part = (int64_t)e0.x * v[0] + (int64_t)e0.y * v[1] + (int64_t)e0.z * v[2] +
+                           (int64_t)e0.w * v[3] + (int64_t)e1.x * v[4] + (int64_t)e1.y * v[5] +
+                           (int64_t)e1.z * v[6] + (int64_t)e1.w * v[7];
+            acc128_add(acc[q], part);
+          }
+        }
+      }
+    }
+    __syncthreads();
+    next(i);
+  }
+  if (!ST) {
+#pragma unroll
+    for (int k = 0; k < KEEP; k++) {
+      int64_t sm = lsum[k];
+      sm += __shfl_xor_sync(0xffffffffu, sm, 8);
+      sm += __shfl_xor_sync(0xffffffffu, sm, 16);
+      if (lane < 8 && sm) atomicAdd(&ssum[qsub * QPG + gj + 8 * k], (unsigned long long)sm);
+    }
+  }
+  if (GROUPS > 1) {   // the ring is idle now: it holds the other position groups' partials
+    acc128 *red = reinterpret_cast<acc128 *>(ring);
+    if (grp > 0)
+#pragma unroll
+      for (int q = 0; q < QV; q++) red[((grp - 1) * QV + q) * HD + d] = acc[q];
+    __syncthreads();
+    if (grp == 0)
+      for (int r = 1; r < GROUPS; r++)
+#pragma unroll
+        for (int q = 0; q < QV; q++) acc128_add(acc[q], red[((r - 1) * QV + q) * HD + d]);
+  }
+  __syncthreads();   // the exponential sums are complete
+
+  // ---- finalize: thread d of group 0 writes head dim d of every query
+  if (grp == 0) {
+    float rm[TQ];
+#pragma unroll
+    for (int r = 0; r < TQ; r++) rm[r] = 0.0f;
+#pragma unroll
+    for (int q = 0; q < QV; q++) {
+      const int r = q / G, h = q % G;
+      if (r < nrow) {
+        const acc128 N = acc[q];
+        const int64_t hi = (int64_t)(((uint64_t)N.hi << 16) | (N.lo >> 48));   // N * 2^16, |N| < 2^78
+        const uint64_t lo = N.lo << 16;
+        const int64_t qd = floordiv_s128(hi, lo, (uint64_t)ssum[q]);
+        const float o = __double2float_rn(__dmul_rn(__ll2double_rn(qd), 0x1p-32));
+        a.ao[(size_t)(t0 + r) * QD + ((size_t)g * G + h) * HD + d] = o;
+        rm[r] = fmaxf(rm[r], fabsf(o));
+      }
+    }
+    if (a.ao_max) {
+#pragma unroll
+      for (int r = 0; r < TQ; r++) {
+        const float m = warp_max_f(rm[r]);
+        if (lane == 0 && r < nrow) atomicMax(&omx[r], __float_as_uint(m));
+      }
+    }
+  }
+  if (a.ao_max) {
+    __syncthreads();
+    if (tid < nrow) atomicMax(a.ao_max + t0 + tid, omx[tid]);
+  }
+}
+
+constexpr size_t ATILE_SMEM_MAX = 220 * 1024;
+
+// SPB_ATTN_TILE_STORE=0 always recomputes the scores in a second K pass (comparisons)
+static bool attn_tile_store_enabled() {
+  static int on = -1;
+  if (on < 0) {
+    const char *e = getenv("SPB_ATTN_TILE_STORE");
+    on = (e && e[0] == '0') ? 0 : 1;
+  }
+  return on != 0;
+}
+
+template <int HD, int G>
+static cudaError_t attn_tile(const AttnArgs &a, cudaStream_t st) {
+  using AT = AttnTile<HD>;
+  constexpr int TQ = ATILE_QV / G;
+  // the longest union of a tile's windows: the window plus TQ - 1 rows, at most the capacity
+  const int span = a.win >= 0 ? std::min(a.P, a.win + TQ - 1) : a.P;
+  const int cmax = (span + AT::SUB - 1) / AT::SUB * AT::SUB;   // the V pass reads whole slices of it
+  const dim3 grid((a.ntok + TQ - 1) / TQ, a.NKV);
+  if (attn_tile_store_enabled() && AT::smem(true, cmax) <= ATILE_SMEM_MAX) {
+    auto kern = k_attn_tile<HD, G, true>;
+    static bool set = false;
+    if (!set) {
+      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ATILE_SMEM_MAX);
+      if (e != cudaSuccess) return e;
+      set = true;
+    }
+    return launch_k(kern, grid, dim3(ATTN_THREADS), AT::smem(true, cmax), st, 1, a, cmax);
+  }
+  auto kern = k_attn_tile<HD, G, false>;
+  static bool set = false;
+  if (!set) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)AT::smem(false, 0));
+    if (e != cudaSuccess) return e;
+    set = true;
+  }
+  return launch_k(kern, grid, dim3(ATTN_THREADS), AT::smem(false, 0), st, 1, a, 0);
+}
+
+// token rows of one session from which attention runs in row tiles (SPB_ATTN_TILE; 0 never)
+static int attn_tile_min() {
+  static int n = -1;
+  if (n < 0) {
+    const char *e = getenv("SPB_ATTN_TILE");
+    n = e ? atoi(e) : 16;
+    if (n < 0) n = 0;
+  }
+  return n;
+}
+
 template <int HD, int G>
 static size_t attn_smem(int cmax, int cl, bool fused) {
   constexpr int SUB = AttnSub<HD>::SUB, GROUPS = ATTN_THREADS / HD;
@@ -1793,8 +2148,10 @@ static cudaError_t attn_cl(const AttnArgs &a, cudaStream_t st) {
 cudaError_t launch_attn(const AttnArgs &a, cudaStream_t st) {
   const int G = a.NH / a.NKV;
   if (a.NH % a.NKV || a.P <= 0) return cudaErrorInvalidValue;
+  // prefill chunks (rows of one session, K/V already stored by k_rope_kv): row tiles
+  const bool tile = !a.rows && !a.qkv && attn_tile_min() > 0 && a.ntok >= attn_tile_min();
 #define SPB_ATTN_CASE(HDV, GV) \
-  if (a.HD == HDV && G == GV) return attn_cl<HDV, GV>(a, st);
+  if (a.HD == HDV && G == GV) return tile ? attn_tile<HDV, GV>(a, st) : attn_cl<HDV, GV>(a, st);
   SPB_ATTN_CASE(64, 1) SPB_ATTN_CASE(64, 2) SPB_ATTN_CASE(64, 4) SPB_ATTN_CASE(64, 8)
   SPB_ATTN_CASE(128, 1) SPB_ATTN_CASE(128, 2) SPB_ATTN_CASE(128, 4) SPB_ATTN_CASE(128, 8)
   SPB_ATTN_CASE(256, 1) SPB_ATTN_CASE(256, 2) SPB_ATTN_CASE(256, 4) SPB_ATTN_CASE(256, 8)

@@ -176,3 +176,30 @@ def test_prefill_k_not_multiple_of_256(xr, cuda_ok, name):
     want = xr.session(xref.build_desc(cfg, T), cfg.max_context).prefill(toks)
     m.free()
     assert np.array_equal(u32(got), u32(want))
+
+
+@pytest.mark.parametrize("hd,nh,nkv,win", [(256, 4, 2, 40), (128, 8, 2, 300), (64, 8, 8, 24)])
+def test_prefill_row_tiles_long_context(xr, cuda_ok, hd, nh, nkv, win):
+    """Prefill chunks of 256 rows run attention in row tiles (16 query vectors of one KV head
+    per CTA, each K/V slice staged once for all of them): 600 positions in chunks of 256 + 256
+    + 88 rows, sliding windows shorter than a chunk (rows of one tile start their windows at
+    different positions) on the local layers, the full context on the global one, then decode
+    steps; every logit and K/V row == XREF."""
+    cfg = dataclasses.replace(spmodel.CONFIGS["micro_gemma"], n_layers=6, head_dim=hd, n_head=nh,
+                              n_head_kv=nkv, sliding_window=win, max_context=640)
+    T = spmodel.gen_model(cfg, seed=13)
+    m = spb200.Model.upload(cfg, T)
+    toks = spmodel.gen_tokens(34, 600, cfg.n_vocab)
+    s = m.session(cfg.max_context)
+    want_s = xr.session(xref.build_desc(cfg, T), cfg.max_context)
+    s.prefill(toks, logits=False)
+    want_s.prefill(toks, all_logits=False)
+    for L in (0, 5):
+        for p in (0, 255, 256, 511, 599):
+            for w in (0, 1):
+                assert np.array_equal(s.kv(L, p, w), want_s.kv(L, p, w)), (L, p, w)
+    for t in spmodel.gen_tokens(35, 3, cfg.n_vocab):
+        assert np.array_equal(u32(s.step(int(t))), u32(want_s.step(int(t))))
+    s.close()
+    want_s.close()
+    m.free()
