@@ -70,6 +70,8 @@ def parse():
     p.add_argument("--spec-steps", type=int, default=8)
     p.add_argument("--q8-prefill", type=int, default=4096, help="configs[3] prefill tokens (0 skips configs[3])")
     p.add_argument("--q8-steps", type=int, default=512)
+    p.add_argument("--spinor", type=int, default=1,
+                   help="also time B=1 decode on a Spinor-block K/V session (SPB_KV_SPINOR); 0 skips it")
     p.add_argument("--no-tp", action="store_true", help="N>1: skip the tensor-parallel objects")
     p.add_argument("--tp", action="store_true", help="(default with N>1) the tensor-parallel objects")
     return p.parse_args()
@@ -464,6 +466,60 @@ def measure_spec(m, cfg, S, steps, seed, max_over_ranks, barrier):
             "prefill_s_untimed": round(prefill_s, 2)}
 
 
+def kv_bytes_per_token(cfg, ctx, row_bytes):
+    """K+V bytes one decode token reads at context ctx: every layer's window of positions x KV
+    heads x 2 rows of row_bytes (sliding-window layers read at most the window)."""
+    tot = 0
+    for L in range(cfg.n_layers):
+        glob = cfg.arch != spmodel_arch_gemma() or cfg.sliding_window <= 0 or (L % cfg.swa_period) == cfg.swa_period - 1
+        n = ctx if glob else min(ctx, cfg.sliding_window)
+        tot += n * cfg.n_head_kv * 2 * row_bytes
+    return tot
+
+
+def spmodel_arch_gemma():
+    import spmodel
+    return spmodel.ARCH_GEMMA3
+
+
+def measure_spinor(m, cfg, args, max_over_ranks, barrier, hbm_gbs):
+    """B=1 greedy decode with the K/V cache kept as Spinor blocks (SPB_KV_SPINOR): the same
+    prefill length (its attention per row: the row tiles read int32 rows only) and K timed steps."""
+    import torch
+    import spmodel
+    K, W = args.steps, args.warmup
+    s = m.session(args.prefill + W + K + 8, spinor=True)
+    stream = torch.cuda.ExternalStream(s.stream())
+    toks = spmodel.gen_tokens(args.seed + 300, args.prefill, cfg.n_vocab)
+    p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    p0.record(stream)
+    s.prefill(toks, logits=False)
+    p1.record(stream)
+    p1.synchronize()
+    tok = int(toks[-1])
+    s.greedy(tok, W)
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    s.greedy(tok, K)
+    e1.record(stream)
+    e1.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1))
+    barrier()
+    s.close()
+    hd = cfg.head_dim
+    rb = (1 if hd <= 55 else (hd + 54) // 55) * 63
+    ctx = args.prefill + W + K // 2
+    kv_spin, kv_i32 = kv_bytes_per_token(cfg, ctx, rb), kv_bytes_per_token(cfg, ctx, hd * 4)
+    step_b = m.weight_bytes() + kv_spin
+    return {"value": round(K / (ms / 1e3), 3), "unit": "tokens/s (B=1, K/V as Spinor blocks)",
+            "ms_per_step": round(ms / K, 4), "prefill_s": round(p0.elapsed_time(p1) / 1e3, 4),
+            "kv_row_bytes": rb, "kv_row_bytes_int32": hd * 4, "ctx_mid": ctx,
+            "kv_bytes_per_token": kv_spin, "kv_bytes_per_token_int32": kv_i32,
+            "step_bytes_frac_of_hbm": round(step_b / (ms / K / 1e3) / 1e9 / hbm_gbs, 4),
+            "note": "every K/V row encoded by the kernel producing it, decoded inside the attention"}
+
+
 def measure_tp(cfg, args, rank, local, world, max_over_ranks, barrier, p2p=True):
     """One session of the model split over the group (spb_model_synthetic_tp): K greedy steps
     timed with CUDA events on the session stream, max over ranks; every rank produces the
@@ -620,6 +676,11 @@ def run_spb(args):
         spec["unit"] = "accepted tokens/s (all GPUs' sessions)"
         spec["sessions_total"] = world * args.spec_sessions
 
+    spin = None
+    if args.spinor:
+        spin = measure_spinor(m, cfg, args, max_over_ranks, barrier, peaks()[0])
+        spin["value"] = round(world * spin["value"], 3)
+
     q8 = None
     if args.q8_prefill > 0:
         q8 = measure_qwen8b(args, local, rank, max_over_ranks, barrier, peaks()[0])
@@ -697,6 +758,7 @@ def run_spb(args):
         "b64": b64,
         "spec": spec,
         "qwen8b": q8,
+        "spinor_kv": spin,
         "prefill": prefill,
         "config2_sweep": sweep,
     }

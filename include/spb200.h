@@ -91,6 +91,15 @@ int64_t spb_model_weight_bytes(const spb_model *m);   /* OK_Q4B bytes streamed p
 
 /* ---- resident KV session (the section-6b verbs, sp_l1.h:386-410) ------------ */
 int  spb_session_open(spb_model *m, int pmax, spb_session **out);
+/* Compressed K/V (sp_l1.h:156 SP_KV_SPINOR; the reference's kv_mode 1, sp_session.c:233-244,
+ * 298-313): every K and V head row is kept as ceil(head_dim / 55) frozen 63-byte Spinor blocks
+ * (include/sp/spinor_block.h:93-97), 315 bytes per row at head_dim 256 against 1024 for the
+ * int32 grid. A K row is encoded from its 2^16-grid values times 2^-16, a V row from its float
+ * projections; attention reads lrintf(decoded * 65536). Unpaged sessions with head_dim 64,
+ * 128 or 256 (else SPB_EUNSUPPORTED); not in spb_batch_decode_step. Clone, rewind and prefill
+ * keep their meaning. */
+#define SPB_KV_SPINOR 1u
+int  spb_session_open_ex(spb_model *m, int pmax, unsigned flags, spb_session **out);
 /* ingest n_tok tokens at the live position; logits [n_tok][n_vocab] (host) or NULL */
 int  spb_session_prefill(spb_session *s, const int32_t *tokens, int n_tok, float *logits);
 /* one token; writes the next position's full-vocab logits (host buffer) */
@@ -128,8 +137,12 @@ int  spb_kvpool_free_pages(spb_kvpool *p);                 /* pages not held by 
 /* spb_session_open with the K/V rows in pool pages (same verbs and bytes as an unpaged session) */
 int  spb_session_open_paged(spb_kvpool *p, int pmax, spb_session **out);
 void spb_session_close(spb_session *s);
-/* readback of one cached K (which=0) or V (which=1) row: [n_head_kv*head_dim] int32 */
+/* readback of one cached K (which=0) or V (which=1) row: [n_head_kv*head_dim] int32
+ * (SPB_EUNSUPPORTED for a Spinor session) */
 int  spb_session_kv_read(const spb_session *s, int layer, int pos, int which, int32_t *out);
+/* a Spinor session's cached K or V blocks of one layer and position: n_head_kv rows of
+ * ceil(head_dim / 55) * 63 bytes */
+int  spb_session_kv_bytes(const spb_session *s, int layer, int pos, int which, uint8_t *out);
 /* device stream the session enqueues on (cudaStream_t) */
 void *spb_session_stream(spb_session *s);
 

@@ -118,6 +118,22 @@ int     xref_clone(const xref_session *s, xref_session **out);
 int     xref_kv_read(const xref_session *s, int layer, int pos, int which, int32_t *out);
 int     xref_argmax(const float *v, int n);
 
+/* ---- Spinor KV blocks (xref_spinor.c; the reference's frozen 63-byte codec) ---- */
+#define XREF_SPINOR_BODY 55
+#define XREF_SPINOR_BYTES 63
+#define XREF_KV_SPINOR 1u        /* session flag: K/V rows kept as Spinor blocks (SP_KV_SPINOR) */
+uint8_t xref_crc8(const uint8_t *data, int len);
+int     xref_spinor_blocks_for(int k);
+void    xref_spinor_encode(const float *v, int len, uint8_t out[XREF_SPINOR_BYTES]);
+int     xref_spinor_decode(const uint8_t in[XREF_SPINOR_BYTES], float *v, int len);
+void    xref_spinor_encode_vec(const float *v, int k, uint8_t *blocks);
+int     xref_spinor_decode_vec(const uint8_t *blocks, int k, float *v);
+int     xref_spinor_kv_row(const int32_t *kg, const float *vf, int hd, uint8_t *blocks, int32_t *grid);
+/* a session whose cache holds Spinor blocks (flags = XREF_KV_SPINOR; 0 = xref_session_create) */
+int     xref_session_create_ex(const xref_model *m, int max_ctx, unsigned flags, xref_session **out);
+/* the cached blocks of one layer at one position: n_head_kv * blocks_for(head_dim) * 63 bytes */
+int     xref_kv_bytes(const xref_session *s, int layer, int pos, int which, uint8_t *out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -111,6 +111,41 @@ class Xref:
         L.xref_cordic_gain_q62.restype = C.c_uint64
         L.xref_attn_head.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int,
                                      C.c_int, C.c_int, C.c_float, C.c_void_p]
+        L.xref_session_create_ex.argtypes = [C.c_void_p, C.c_int, C.c_uint, C.POINTER(C.c_void_p)]
+        L.xref_kv_bytes.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p]
+        L.xref_crc8.argtypes = [C.c_void_p, C.c_int]
+        L.xref_crc8.restype = C.c_uint8
+        L.xref_spinor_encode_vec.argtypes = [C.c_void_p, C.c_int, C.c_void_p]
+        L.xref_spinor_decode_vec.argtypes = [C.c_void_p, C.c_int, C.c_void_p]
+        L.xref_spinor_kv_row.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]
+
+    # ---- Spinor KV blocks
+    @staticmethod
+    def spinor_blocks_for(k):
+        return 1 if k <= 55 else (k + 54) // 55
+
+    def spinor_encode(self, v):
+        v = np.ascontiguousarray(v, np.float32)
+        o = np.zeros(self.spinor_blocks_for(v.size) * 63, np.uint8)
+        self.lib.xref_spinor_encode_vec(v.ctypes.data, v.size, o.ctypes.data)
+        return o
+
+    def spinor_decode(self, blocks, k):
+        blocks = np.ascontiguousarray(blocks, np.uint8)
+        o = np.zeros(k, np.float32)
+        rc = self.lib.xref_spinor_decode_vec(blocks.ctypes.data, k, o.ctypes.data)
+        return o, rc
+
+    def spinor_kv_row(self, hd, kg=None, vf=None):
+        """(blocks, grid, rc) of one head row: a K row on the 2^16 grid, or a V row of floats."""
+        blocks = np.zeros(self.spinor_blocks_for(hd) * 63, np.uint8)
+        grid = np.zeros(hd, np.int32)
+        kp = np.ascontiguousarray(kg, np.int32) if kg is not None else None
+        vp = np.ascontiguousarray(vf, np.float32) if vf is not None else None
+        rc = self.lib.xref_spinor_kv_row(kp.ctypes.data if kp is not None else None,
+                                         vp.ctypes.data if vp is not None else None, hd,
+                                         blocks.ctypes.data, grid.ctypes.data)
+        return blocks, grid, rc
 
     # ---- elementwise helpers on numpy arrays
     def rmsnorm(self, x, w):
@@ -166,17 +201,17 @@ class Xref:
         return o, rc
 
     # ---- sessions
-    def session(self, desc, max_ctx):
-        return XrefSession(self, desc, max_ctx)
+    def session(self, desc, max_ctx, spinor=False):
+        return XrefSession(self, desc, max_ctx, flags=1 if spinor else 0)
 
 
 class XrefSession:
-    def __init__(self, xr, desc, max_ctx, handle=None):
-        self.xr, self.desc, self.max_ctx = xr, desc, max_ctx
+    def __init__(self, xr, desc, max_ctx, handle=None, flags=0):
+        self.xr, self.desc, self.max_ctx, self.flags = xr, desc, max_ctx, flags
         self.V = desc.cfg.n_vocab
         if handle is None:
             h = C.c_void_p()
-            rc = xr.lib.xref_session_create(C.byref(desc), max_ctx, C.byref(h))
+            rc = xr.lib.xref_session_create_ex(C.byref(desc), max_ctx, flags, C.byref(h))
             if rc:
                 raise RuntimeError(f"xref_session_create rc={rc}")
             handle = h
@@ -216,7 +251,16 @@ class XrefSession:
         rc = self.xr.lib.xref_clone(self.h, C.byref(h))
         if rc:
             raise RuntimeError(f"xref_clone rc={rc}")
-        return XrefSession(self.xr, self.desc, self.max_ctx, handle=h)
+        return XrefSession(self.xr, self.desc, self.max_ctx, handle=h, flags=self.flags)
+
+    def kv_bytes(self, layer, pos, which):
+        """Spinor sessions: the cached blocks of one layer at one position."""
+        c = self.desc.cfg
+        o = np.zeros(c.n_head_kv * self.xr.spinor_blocks_for(c.head_dim) * 63, np.uint8)
+        rc = self.xr.lib.xref_kv_bytes(self.h, layer, pos, which, o.ctypes.data)
+        if rc:
+            raise RuntimeError(f"xref_kv_bytes rc={rc}")
+        return o
 
     def kv(self, layer, pos, which):
         c = self.desc.cfg

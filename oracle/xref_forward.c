@@ -36,6 +36,8 @@ struct xref_session {
     const xref_model *m;
     int max_ctx, pos;
     int32_t *kc, *vc;          /* [n_layers][max_ctx][n_head_kv*head_dim], 2^16 grid */
+    unsigned flags;            /* XREF_KV_SPINOR: the rows above are the decoded Spinor blocks */
+    uint8_t *kb, *vb;          /* spinor: [n_layers][max_ctx][n_head_kv][nblk * 63] */
     uint64_t *wg, *wl;         /* RoPE turn tables, [head_dim/2] */
     float *x, *nx, *q, *k, *v, *ao, *ap, *g, *u, *dn, *t;
     int32_t *qi;
@@ -95,15 +97,29 @@ int xref_attn_head(const int32_t *q, const int32_t *K, const int32_t *V, int str
     return rc;
 }
 
+static size_t spin_row_bytes(const xref_config *c) {
+    return (size_t)c->n_head_kv * (size_t)xref_spinor_blocks_for(c->head_dim) * XREF_SPINOR_BYTES;
+}
+
 int xref_session_create(const xref_model *m, int max_ctx, xref_session **out) {
-    if (!m || !out || max_ctx <= 0) return XREF_EBADARG;
+    return xref_session_create_ex(m, max_ctx, 0u, out);
+}
+
+int xref_session_create_ex(const xref_model *m, int max_ctx, unsigned flags, xref_session **out) {
+    if (!m || !out || max_ctx <= 0 || (flags & ~XREF_KV_SPINOR)) return XREF_EBADARG;
     const xref_config *c = &m->cfg;
     const int E = c->n_embd, HD = c->head_dim, KVD = c->n_head_kv * HD, QD = c->n_head * HD;
     const int FF = c->n_ff;
     if (c->n_head % c->n_head_kv) return XREF_EBADARG;
     xref_session *s = (xref_session *)calloc(1, sizeof *s);
     if (!s) return XREF_ENOMEM;
-    s->m = m; s->max_ctx = max_ctx;
+    s->m = m; s->max_ctx = max_ctx; s->flags = flags;
+    if (flags & XREF_KV_SPINOR) {
+        const size_t nb = (size_t)c->n_layers * (size_t)max_ctx * spin_row_bytes(c);
+        s->kb = (uint8_t *)calloc(nb, 1);
+        s->vb = (uint8_t *)calloc(nb, 1);
+        if (!s->kb || !s->vb) { xref_session_destroy(s); return XREF_ENOMEM; }
+    }
     size_t kvn = (size_t)c->n_layers * (size_t)max_ctx * (size_t)KVD;
     s->kc = (int32_t *)calloc(kvn, sizeof(int32_t));
     s->vc = (int32_t *)calloc(kvn, sizeof(int32_t));
@@ -129,7 +145,7 @@ int xref_session_create(const xref_model *m, int max_ctx, xref_session **out) {
 
 void xref_session_destroy(xref_session *s) {
     if (!s) return;
-    free(s->kc); free(s->vc); free(s->wg); free(s->wl);
+    free(s->kc); free(s->vc); free(s->kb); free(s->vb); free(s->wg); free(s->wl);
     free(s->x); free(s->nx); free(s->q); free(s->k); free(s->v); free(s->ao); free(s->ap);
     free(s->g); free(s->u); free(s->dn); free(s->t); free(s->qi);
     free(s);
@@ -181,9 +197,20 @@ int xref_decode_step(xref_session *s, int32_t tok, float *logits) {
             if (c->has_qk_norm) { CHK(norm(kh, ly->k_norm, HD, s->t)); memcpy(kh, s->t, (size_t)HD * 4); }
             CHK(xref_rope_cordic(kh, HD, pos, W, kcl + (size_t)pos * KVD + (size_t)h * HD));
         }
-        for (int i = 0; i < KVD; i++) {
-            if (!(fabsf(s->v[i]) < 16384.0f)) return XREF_ERANGE;
-            vcl[(size_t)pos * KVD + i] = (int32_t)lrintf(s->v[i] * 65536.0f);
+        if (s->flags & XREF_KV_SPINOR) {   /* K/V rows through the Spinor codec (sp_session.c:298-313) */
+            const size_t rbh = (size_t)xref_spinor_blocks_for(HD) * XREF_SPINOR_BYTES, rb = spin_row_bytes(c);
+            uint8_t *kb = s->kb + ((size_t)L * P + pos) * rb, *vb = s->vb + ((size_t)L * P + pos) * rb;
+            for (int h = 0; h < NKV; h++) {
+                int32_t *kr = kcl + (size_t)pos * KVD + (size_t)h * HD;
+                CHK(xref_spinor_kv_row(kr, NULL, HD, kb + h * rbh, kr));
+                CHK(xref_spinor_kv_row(NULL, s->v + (size_t)h * HD, HD, vb + h * rbh,
+                                       vcl + (size_t)pos * KVD + (size_t)h * HD));
+            }
+        } else {
+            for (int i = 0; i < KVD; i++) {
+                if (!(fabsf(s->v[i]) < 16384.0f)) return XREF_ERANGE;
+                vcl[(size_t)pos * KVD + i] = (int32_t)lrintf(s->v[i] * 65536.0f);
+            }
         }
         for (int h = 0; h < NH; h++) {
             const int g = h / group;
@@ -237,11 +264,16 @@ int xref_rewind(xref_session *s, int n) {
 int xref_position(const xref_session *s) { return s ? s->pos : -1; }
 
 int xref_clone(const xref_session *s, xref_session **out) {
-    CHK(xref_session_create(s->m, s->max_ctx, out));
+    CHK(xref_session_create_ex(s->m, s->max_ctx, s->flags, out));
     const xref_config *c = &s->m->cfg;
     size_t kvn = (size_t)c->n_layers * (size_t)s->max_ctx * (size_t)(c->n_head_kv * c->head_dim);
     memcpy((*out)->kc, s->kc, kvn * sizeof(int32_t));
     memcpy((*out)->vc, s->vc, kvn * sizeof(int32_t));
+    if (s->flags & XREF_KV_SPINOR) {
+        const size_t nb = (size_t)c->n_layers * (size_t)s->max_ctx * spin_row_bytes(c);
+        memcpy((*out)->kb, s->kb, nb);
+        memcpy((*out)->vb, s->vb, nb);
+    }
     (*out)->pos = s->pos;
     return XREF_OK;
 }
@@ -252,5 +284,14 @@ int xref_kv_read(const xref_session *s, int layer, int pos, int which, int32_t *
     if (layer < 0 || layer >= c->n_layers || pos < 0 || pos >= s->max_ctx) return XREF_EBADARG;
     const int32_t *src = (which ? s->vc : s->kc) + ((size_t)layer * s->max_ctx + pos) * KVD;
     memcpy(out, src, (size_t)KVD * sizeof(int32_t));
+    return XREF_OK;
+}
+
+int xref_kv_bytes(const xref_session *s, int layer, int pos, int which, uint8_t *out) {
+    const xref_config *c = &s->m->cfg;
+    if (!(s->flags & XREF_KV_SPINOR) || layer < 0 || layer >= c->n_layers || pos < 0 || pos >= s->max_ctx)
+        return XREF_EBADARG;
+    const size_t rb = spin_row_bytes(c);
+    memcpy(out, (which ? s->vb : s->kb) + ((size_t)layer * s->max_ctx + pos) * rb, rb);
     return XREF_OK;
 }

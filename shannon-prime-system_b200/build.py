@@ -29,7 +29,7 @@ REF_INCLUDE = os.environ.get("SPB_REF_INCLUDE",
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVFLAGS = ["-std=c++17", "-O3", "-lineinfo", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr"] + ARCH
 CU_SRCS = ["spb_kernels.cu", "spb_gemm_tc.cu", "spb_runtime.cu", "spb_noalloc.cu", "spb_tp.cu"]
-HDRS = ["spb_exact.cuh", "spb_kernels.cuh", "spb_async.cuh", "spb_device.cuh", "spb_tp.cuh"]
+HDRS = ["spb_exact.cuh", "spb_kernels.cuh", "spb_async.cuh", "spb_device.cuh", "spb_tp.cuh", "spb_spinor.cuh"]
 
 
 def _newer(out, deps):

@@ -29,6 +29,7 @@
 #include "spb_device.cuh"
 #include "spb_exact.cuh"
 #include "spb_kernels.cuh"
+#include "spb_spinor.cuh"
 
 #include <algorithm>
 #include <cooperative_groups.h>
@@ -1303,6 +1304,23 @@ __global__ void k_rope_kv(RopeArgs a) {
   }
   const int i = threadIdx.x;   // pair index, blockDim.x == half
   if (a.zero_slot && head == 0 && i == 0) a.zero_slot[t] = 0u;
+  // Spinor-block cache: K and V rows are stored as 63-byte blocks (CRC tables, per-warp block
+  // images and the rotated K row after the two f32 rows in shared memory)
+  const bool spin = kv.rb > 0 && head >= a.NH;
+  uint8_t *tab = reinterpret_cast<uint8_t *>(rsm + 2 * HD);
+  uint8_t *imgs = tab + 1024;
+  int32_t *krow = reinterpret_cast<int32_t *>(imgs + 64 * ((half + 31) / 32));
+  if (spin) {
+    crc8_tables_build(tab, threadIdx.x, blockDim.x);
+    __syncthreads();
+  }
+  if (head >= a.NH + a.NKV && spin) {   // V head: Spinor blocks of the float projections
+    const int g = head - a.NH - a.NKV;
+    spin_encode_row(row + QD + KVD + g * HD, false, HD,
+                    reinterpret_cast<uint8_t *>(kv.v) + kv_spin_off(kv, a.NKV, a.layer, g, p), nullptr, imgs, tab,
+                    a.err);
+    return;
+  }
   if (head >= a.NH + a.NKV) {  // V head: quantize to the 2^16 grid
     const int g = head - a.NH - a.NKV;
     const float *src = row + QD + KVD + g * HD;
@@ -1332,6 +1350,14 @@ __global__ void k_rope_kv(RopeArgs a) {
   const uint64_t phase = (uint64_t)(int64_t)p * a.W[i];
   int32_t oa, ob;
   cordic_rotate(vals[i], vals[i + half], phase, a.T, a.gain, oa, ob, a.err);
+  if (spin) {   // K head: Spinor blocks of the rotated grid row
+    krow[i] = oa;
+    krow[i + half] = ob;
+    __syncthreads();
+    spin_encode_row(krow, true, HD, reinterpret_cast<uint8_t *>(kv.k) + kv_spin_off(kv, a.NKV, a.layer, hh, p),
+                    nullptr, imgs, tab, a.err);
+    return;
+  }
   int32_t *dst = is_q ? a.qi + (size_t)t * QD + hh * HD : kv.k + kv_elem(kv, a.NL, a.NKV, HD, a.layer, hh, p);
   dst[i] = oa;
   dst[i + half] = ob;
@@ -1339,8 +1365,12 @@ __global__ void k_rope_kv(RopeArgs a) {
 
 cudaError_t launch_rope_kv(const RopeArgs &a, cudaStream_t st) {
   if (a.HD & 1 || a.HD / 2 > 1024) return cudaErrorInvalidValue;
+  if (a.kv.rb > 0 && (a.rows || a.kv.ptab || a.HD < 64 || a.kv.rb != spin_row_bytes(a.HD))) return cudaErrorInvalidValue;
   dim3 grid(a.NH + 2 * a.NKV, a.ntok);
-  return launch_k(k_rope_kv, grid, dim3(a.HD / 2), 2 * a.HD * sizeof(float), st, 1, a);
+  // Spinor caches: + CRC tables, a 64-byte block image per warp, the rotated K row
+  const size_t smem = 2 * a.HD * sizeof(float) +
+                      (a.kv.rb > 0 ? 1024 + 64 * (size_t)((a.HD / 2 + 31) / 32) + (size_t)a.HD * 4 : 0);
+  return launch_k(k_rope_kv, grid, dim3(a.HD / 2), smem, st, 1, a);
 }
 
 // ------------------------------------------------------------------------------ attention
@@ -1413,6 +1443,19 @@ __global__ void __launch_bounds__(ATTN_THREADS, 2) k_attn(AttnArgs a, int cmax, 
   auto kv_at = [&](bool isv, int q) -> int32_t * {
     return (isv ? kv.v : kv.k) + kv_elem(kv, a.NL, a.NKV, HD, a.layer, g, q);
   };
+  // Spinor-block cache (kv.rb > 0): a slice's blocks are copied (16-byte aligned around them)
+  // into the tail of its ring stage, SOFF bytes in, and decoded into the stage's int32 rows;
+  // the first half of the rows lands below SOFF, so only the second half waits on a barrier
+  const bool spin = kv.rb > 0;
+  using SG = SpinGeom<HD>;
+  constexpr int SOFF = SUB * HD * 4 - ((SUB * SG::RB + 32 + 15) & ~15);
+  static_assert(SOFF >= SUB / 2 * HD * 4, "the decoded first half stays below the copied blocks");
+  auto spin_src = [&](bool isv, int q) -> const uint8_t * {
+    return reinterpret_cast<const uint8_t *>(isv ? kv.v : kv.k) + kv_spin_off(kv, a.NKV, a.layer, g, q);
+  };
+  // CRC tables and per-(row, chunk) decode multipliers after the exchange buffers
+  uint8_t *spin_tab = reinterpret_cast<uint8_t *>(gat + (CL > 1 ? G * HD : 0));
+  float *smul = reinterpret_cast<float *>(spin_tab + 1024);
 
   // slice i -> ring stage i % STAGES: one bulk copy, or two where the slice crosses a page
   // boundary (a slice of SUB <= 128 positions spans at most two pages of >= 128)
@@ -1423,11 +1466,51 @@ __global__ void __launch_bounds__(ATTN_THREADS, 2) k_attn(AttnArgs a, int cmax, 
     const int len = min(SUB, c1 - pos);
     const uint32_t bytes = (uint32_t)len * HD * 4;
     uint64_t *bar = &full[i % ATTN_STAGES];
-    mbar_arrive_expect_tx(bar, bytes);
     int32_t *dst = ring + (i % ATTN_STAGES) * SUB * HD;
+    if (spin) {
+      const uintptr_t A = (uintptr_t)spin_src(isv, pos), A0 = A & ~(uintptr_t)15;
+      const uintptr_t A1 = (A + (uintptr_t)len * SG::RB + 15) & ~(uintptr_t)15;
+      mbar_arrive_expect_tx(bar, (uint32_t)(A1 - A0));
+      bulk_g2s(reinterpret_cast<uint8_t *>(dst) + SOFF, reinterpret_cast<const void *>(A0), (uint32_t)(A1 - A0), bar);
+      return;
+    }
+    mbar_arrive_expect_tx(bar, bytes);
     const int first = min(len, kv.pg - pos % kv.pg);
     bulk_g2s(dst, kv_at(isv, pos), (uint32_t)first * HD * 4, bar);
     if (first < len) bulk_g2s(dst + (size_t)first * HD, kv_at(isv, pos + first), (uint32_t)(len - first) * HD * 4, bar);
+  };
+
+  // decode slice i's blocks (landed in its stage) into the stage's int32 rows [0, len)
+  auto spin_decode = [&](int i, int32_t *buf, int len) {
+    const bool isv = i >= nsub;
+    const int pos = c0 + (isv ? i - nsub : i) * SUB;
+    const uint8_t *src = reinterpret_cast<const uint8_t *>(buf) + SOFF + ((uintptr_t)spin_src(isv, pos) & 15);
+    for (int x = threadIdx.x; x < len * SG::NB; x += ATTN_THREADS)
+      smul[x] = spin_block_mul(src + (x / SG::NB) * SG::RB + (x % SG::NB) * SPIN_BYTES);
+    __syncthreads();
+    constexpr int NV = SUB / 2 * HD / ATTN_THREADS, RSTEP = ATTN_THREADS / HD;
+    const int d = threadIdx.x % HD, r0 = threadIdx.x / HD;
+    int cb, ci;
+    SG::locate(d, cb, ci);
+    const int bo = cb * SPIN_BYTES + 7 + (17 * ci) % SPIN_BODY;
+#pragma unroll
+    for (int k = 0; k < NV; k++) {
+      const int r = r0 + k * RSTEP;
+      if (r < len) buf[r * HD + d] = spin_grid(src[r * SG::RB + bo], smul[r * SG::NB + cb]);
+    }
+    int32_t hv[NV];
+#pragma unroll
+    for (int k = 0; k < NV; k++) {
+      const int r = SUB / 2 + r0 + k * RSTEP;
+      hv[k] = r < len ? spin_grid(src[r * SG::RB + bo], smul[r * SG::NB + cb]) : 0;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < NV; k++) {
+      const int r = SUB / 2 + r0 + k * RSTEP;
+      if (r < len) buf[r * HD + d] = hv[k];
+    }
+    __syncthreads();
   };
 
   // K/V rows before this launch's first new position were written by earlier steps, so a
@@ -1514,13 +1597,21 @@ __global__ void __launch_bounds__(ATTN_THREADS, 2) k_attn(AttnArgs a, int cmax, 
       int32_t *dst = is_k ? kvn : qs + j * HD;
       dst[i] = oa;
       dst[i + HALF] = ob;
-      if (is_k) {
+      if (is_k && !spin) {
         int32_t *kr = kv_at(false, p);
         kr[i] = oa;
         kr[i + HALF] = ob;
       }
     }
-    if (own) {   // the new V row on the 2^16 grid
+    if (own && spin) {   // the new K and V rows as Spinor blocks; kvn takes their decoded grids
+      __syncthreads();
+      crc8_tables_build(spin_tab, threadIdx.x, ATTN_THREADS);
+      __syncthreads();
+      uint8_t *imgs = reinterpret_cast<uint8_t *>(smul);
+      spin_encode_row(kvn, true, HD, const_cast<uint8_t *>(spin_src(false, p)), kvn, imgs, spin_tab, a.err);
+      spin_encode_row(row + QD + KVD + g * HD, false, HD, const_cast<uint8_t *>(spin_src(true, p)), kvn + HD, imgs,
+                      spin_tab, a.err);
+    } else if (own) {   // the new V row on the 2^16 grid
       const float *src = row + QD + KVD + g * HD;
       int32_t *vr = kv_at(true, p);
       for (int d = threadIdx.x; d < HD; d += ATTN_THREADS) {
@@ -1556,6 +1647,7 @@ __global__ void __launch_bounds__(ATTN_THREADS, 2) k_attn(AttnArgs a, int cmax, 
     mbar_wait(&full[stage], (uint32_t)(i / ATTN_STAGES) & 1u, a.err);
     const int32_t *buf = ring + stage * SUB * HD;
     const int len = min(SUB, cn - i * SUB);
+    if (spin) spin_decode(i, ring + stage * SUB * HD, len);
     if (own && i == nsub - 1) {   // the new position (the slice's last) from this kernel's K row
       for (int d = threadIdx.x; d < HD; d += ATTN_THREADS) ring[stage * SUB * HD + (len - 1) * HD + d] = kvn[d];
       __syncthreads();
@@ -1646,6 +1738,7 @@ __global__ void __launch_bounds__(ATTN_THREADS, 2) k_attn(AttnArgs a, int cmax, 
     const int32_t *buf = ring + stage * SUB * HD;
     const int j0 = (i - nsub) * SUB;
     const int len = min(SUB, cn - j0);
+    if (spin) spin_decode(i, ring + stage * SUB * HD, len);
     if (own && i == total - 1) {   // ... and its V row
       for (int d = threadIdx.x; d < HD; d += ATTN_THREADS) ring[stage * SUB * HD + (len - 1) * HD + d] = kvn[HD + d];
       __syncthreads();
@@ -2090,12 +2183,13 @@ static int attn_tile_min() {
 }
 
 template <int HD, int G>
-static size_t attn_smem(int cmax, int cl, bool fused) {
+static size_t attn_smem(int cmax, int cl, bool fused, bool spin = false) {
   constexpr int SUB = AttnSub<HD>::SUB, GROUPS = ATTN_THREADS / HD;
   const bool direct = GROUPS == 1 && cl > 1;
   return (size_t)ATTN_STAGES * SUB * HD * 4 + (size_t)G * HD * 4 + (fused ? (size_t)2 * HD * 4 : 0) +
          (size_t)((G * cmax + 3) & ~3) * 4 +
-         (direct ? 0 : (size_t)GROUPS * G * HD * sizeof(acc128)) + (cl > 1 ? (size_t)G * HD * sizeof(acc128) : 0);
+         (direct ? 0 : (size_t)GROUPS * G * HD * sizeof(acc128)) + (cl > 1 ? (size_t)G * HD * sizeof(acc128) : 0) +
+         (spin ? 2048 : 0);   // Spinor caches: CRC tables, decode multipliers
 }
 
 template <int HD, int G>
@@ -2137,10 +2231,10 @@ static cudaError_t attn_cl(const AttnArgs &a, cudaStream_t st) {
   const int span = a.win >= 0 ? std::min(a.P, a.win) : a.P;
   int cl = 1;
   while (cl < clmax && ((long)a.ntok * a.NKV * cl < 2L * nsm || span > cl * ATTN_SPAN)) cl *= 2;
-  const bool fused = a.qkv != nullptr;
-  while (cl < clmax && attn_smem<HD, G>((a.P + cl - 1) / cl, cl, fused) > 200 * 1024) cl *= 2;
+  const bool fused = a.qkv != nullptr, spin = a.kv.rb > 0;
+  while (cl < clmax && attn_smem<HD, G>((a.P + cl - 1) / cl, cl, fused, spin) > 200 * 1024) cl *= 2;
   const int cmax = (a.P + cl - 1) / cl;
-  const size_t smem = attn_smem<HD, G>(cmax, cl, fused);
+  const size_t smem = attn_smem<HD, G>(cmax, cl, fused, spin);
   if (smem > 200 * 1024) return cudaErrorInvalidValue;
   return launch_k(kern, dim3(cl, a.NKV, a.ntok), dim3(ATTN_THREADS), smem, st, cl, a, cmax, cl);
 }
@@ -2148,8 +2242,10 @@ static cudaError_t attn_cl(const AttnArgs &a, cudaStream_t st) {
 cudaError_t launch_attn(const AttnArgs &a, cudaStream_t st) {
   const int G = a.NH / a.NKV;
   if (a.NH % a.NKV || a.P <= 0) return cudaErrorInvalidValue;
+  // Spinor-block caches: one session's own unpaged cache, head_dim 64 / 128 / 256
+  if (a.kv.rb > 0 && (a.rows || a.kv.ptab || a.HD < 64 || a.kv.rb != spin_row_bytes(a.HD))) return cudaErrorInvalidValue;
   // prefill chunks (rows of one session, K/V already stored by k_rope_kv): row tiles
-  const bool tile = !a.rows && !a.qkv && attn_tile_min() > 0 && a.ntok >= attn_tile_min();
+  const bool tile = !a.rows && !a.qkv && a.kv.rb == 0 && attn_tile_min() > 0 && a.ntok >= attn_tile_min();
 #define SPB_ATTN_CASE(HDV, GV) \
   if (a.HD == HDV && G == GV) return tile ? attn_tile<HDV, GV>(a, st) : attn_cl<HDV, GV>(a, st);
   SPB_ATTN_CASE(64, 1) SPB_ATTN_CASE(64, 2) SPB_ATTN_CASE(64, 4) SPB_ATTN_CASE(64, 8)

@@ -112,7 +112,15 @@ struct KvPages {
   int32_t *k, *v;
   const int32_t *ptab;
   int pg;
+  // rb > 0: the rows are Spinor blocks (rb = ceil(HD / 55) * 63 bytes per position and KV head),
+  // k and v then point at bytes laid out [NL][NKV][pg][rb]; single page only (ptab == nullptr)
+  int rb = 0;
 };
+
+// byte offset of (layer L, KV head g, position p) in a Spinor-block cache (kv.rb > 0)
+__host__ __device__ inline size_t kv_spin_off(const KvPages &kv, int NKV, int L, int g, int p) {
+  return (((size_t)L * NKV + g) * (size_t)kv.pg + (size_t)p) * (size_t)kv.rb;
+}
 
 // element offset of (layer L, KV head g, position p) in k or v; the page table is read where it
 // lives (device code: device tables; host code: a host copy)

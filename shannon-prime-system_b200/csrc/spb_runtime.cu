@@ -11,6 +11,7 @@
 // This mirrors kv_step_gemma3 (sp_session.c:380-464) and kv_step (sp_session.c:274-363).
 #include "../../include/spb200.h"
 #include "spb_kernels.cuh"
+#include "spb_spinor.cuh"
 #include "spb_tp.cuh"
 
 #include <cuda_runtime.h>
@@ -597,13 +598,23 @@ struct spb_session {
   float *logits_l = nullptr, *logits_g = nullptr;
   int64_t *ws = nullptr;          // split-K workspace of the token-batch GEMMs [4][NT_MAX][E]
   size_t ws_elems = 0;
+  unsigned flags = 0;             // SPB_KV_SPINOR: K/V rows kept as Spinor blocks (kv.rb bytes each)
 };
 
 static size_t kv_layer_elems(const spb_model *m, int pmax) { return (size_t)m->NKV * pmax * m->HD; }
 
-static int session_open(spb_model *m, int pmax, spb_kvpool *pool, spb_session **out) {
+// bytes of one layer's Spinor-block K (or V) cache
+static size_t kv_spin_layer_bytes(const spb_model *m, int pmax) {
+  return (size_t)m->NKV * pmax * (size_t)spin_row_bytes(m->HD);
+}
+
+static int session_open(spb_model *m, int pmax, spb_kvpool *pool, spb_session **out, unsigned flags = 0) {
   if (!m || !out || pmax <= 0) return set_err(SPB_EBADARG, "spb_session_open: bad arg");
   *out = nullptr;
+  if (flags & ~(unsigned)SPB_KV_SPINOR) return set_err(SPB_EBADARG, "spb_session_open_ex: unknown flags 0x%x", flags);
+  const bool spin = (flags & SPB_KV_SPINOR) != 0;
+  if (spin && (pool || m->HD < 64 || m->HD > 256 || (m->HD & (m->HD - 1))))
+    return set_err(SPB_EUNSUPPORTED, "spb_session_open_ex: Spinor K/V needs an unpaged session and head_dim 64, 128 or 256");
   CU(cudaSetDevice(m->device));
   spb_session *s = new spb_session();
   s->m = m;
@@ -616,7 +627,9 @@ static int session_open(spb_model *m, int pmax, spb_kvpool *pool, spb_session **
   size_t off = 0;
   auto take = [&](size_t n) { size_t o = off; off = (off + n + 255) & ~(size_t)255; return o; };
   const size_t kvn = pool ? 0 : (size_t)m->NL * kv_layer_elems(m, pmax);
-  const size_t o_kc = take(kvn * 4), o_vc = take(kvn * 4), o_ptab = take((size_t)npg * 4);
+  // Spinor blocks: + 32 bytes, as the attention's bulk copies read 16-byte-aligned spans around a slice
+  const size_t kvb = spin ? (size_t)m->NL * kv_spin_layer_bytes(m, pmax) + 32 : kvn * 4;
+  const size_t o_kc = take(kvb), o_vc = take(kvb), o_ptab = take((size_t)npg * 4);
   const size_t o_x = take((size_t)NT_MAX * E * 4), o_qkv = take((size_t)NT_MAX * QKV * 4);
   const size_t o_ao = take((size_t)NT_MAX * m->QD * 4), o_ap = take((size_t)NT_MAX * E * 4);
   const size_t o_gg = take((size_t)NT_MAX * m->FF * 4), o_dn = take((size_t)NT_MAX * E * 4);
@@ -637,8 +650,9 @@ static int session_open(spb_model *m, int pmax, spb_kvpool *pool, spb_session **
     s->ptab_dev = (int32_t *)(B + o_ptab);
     s->kv = KvPages{pool->k, pool->v, s->ptab_dev, pool->pg};
   } else {
-    s->kv = KvPages{(int32_t *)(B + o_kc), (int32_t *)(B + o_vc), nullptr, pmax};
+    s->kv = KvPages{(int32_t *)(B + o_kc), (int32_t *)(B + o_vc), nullptr, pmax, spin ? spin_row_bytes(m->HD) : 0};
   }
+  s->flags = flags;
   s->x = (float *)(B + o_x); s->qkv = (float *)(B + o_qkv); s->ao = (float *)(B + o_ao);
   s->ap = (float *)(B + o_ap); s->gg = (float *)(B + o_gg); s->dn = (float *)(B + o_dn);
   s->logits = (float *)(B + o_lg); s->qi = (int32_t *)(B + o_qi);
@@ -667,6 +681,10 @@ static int session_open(spb_model *m, int pmax, spb_kvpool *pool, spb_session **
 }
 
 extern "C" int spb_session_open(spb_model *m, int pmax, spb_session **out) { return session_open(m, pmax, nullptr, out); }
+
+extern "C" int spb_session_open_ex(spb_model *m, int pmax, unsigned flags, spb_session **out) {
+  return session_open(m, pmax, nullptr, out, flags);
+}
 
 extern "C" int spb_session_open_paged(spb_kvpool *pool, int pmax, spb_session **out) {
   if (!pool) return set_err(SPB_EBADARG, "spb_session_open_paged: null pool");
@@ -982,6 +1000,7 @@ extern "C" int spb_batch_decode_step(spb_session *const *ss, int B, const int32_
     spb_session *s = ss[i];
     if (!s || s->m != lead->m) return set_err(SPB_EBADARG, "spb_batch_decode_step: sessions must share one model");
     if (s->pos >= s->pmax) return set_err(SPB_ECONTEXT_FULL, "spb_batch_decode_step: session %d context full", i);
+    if (s->kv.rb) return set_err(SPB_EUNSUPPORTED, "spb_batch_decode_step: session %d keeps Spinor K/V (decode it alone)", i);
     for (int j = 0; j < i; j++)
       if (ss[j] == s) return set_err(SPB_EBADARG, "spb_batch_decode_step: session %d repeated", i);
     Pmax = std::max(Pmax, s->pmax);
@@ -1055,7 +1074,7 @@ extern "C" int spb_session_rewind(spb_session *s, int n) {
 // Unpaged: a deep copy of the cache on the device.
 extern "C" int spb_session_clone(const spb_session *s, spb_session **out) {
   if (!s || !out) return set_err(SPB_EBADARG, "spb_session_clone: null arg");
-  int rc = session_open(s->m, s->pmax, s->pool, out);
+  int rc = session_open(s->m, s->pmax, s->pool, out, s->flags);
   if (rc) return rc;
   spb_session *c = *out;
   CU(cudaStreamSynchronize(s->st));
@@ -1068,9 +1087,10 @@ extern "C" int spb_session_clone(const spb_session *s, spb_session **out) {
     }
     CU(cudaMemcpyAsync(c->ptab_dev, c->pages.data(), c->pages.size() * 4, cudaMemcpyHostToDevice, c->st));
   } else {
-    const size_t kvn = (size_t)s->m->NL * kv_layer_elems(s->m, s->pmax);
-    CU(cudaMemcpyAsync(c->kv.k, s->kv.k, kvn * 4, cudaMemcpyDeviceToDevice, c->st));
-    CU(cudaMemcpyAsync(c->kv.v, s->kv.v, kvn * 4, cudaMemcpyDeviceToDevice, c->st));
+    const size_t kvb = s->kv.rb ? (size_t)s->m->NL * kv_spin_layer_bytes(s->m, s->pmax)
+                                : (size_t)s->m->NL * kv_layer_elems(s->m, s->pmax) * 4;
+    CU(cudaMemcpyAsync(c->kv.k, s->kv.k, kvb, cudaMemcpyDeviceToDevice, c->st));
+    CU(cudaMemcpyAsync(c->kv.v, s->kv.v, kvb, cudaMemcpyDeviceToDevice, c->st));
   }
   CU(cudaMemcpyAsync(c->hist_dev, s->hist_dev, (size_t)s->pmax * 4, cudaMemcpyDeviceToDevice, c->st));
   c->pos = s->pos;
@@ -1084,6 +1104,7 @@ extern "C" int spb_session_kv_read(const spb_session *s, int layer, int pos, int
   if (!s || !out || layer < 0 || layer >= s->m->NL || pos < 0 || pos >= s->pmax)
     return set_err(SPB_EBADARG, "spb_session_kv_read: bad arg");
   const spb_model *m = s->m;
+  if (s->kv.rb) return set_err(SPB_EUNSUPPORTED, "spb_session_kv_read: a Spinor session's rows are blocks (spb_session_kv_bytes)");
   KvPages hk = s->kv;
   if (s->pool) {
     if (s->pages[pos / s->pool->pg] < 0) return set_err(SPB_EBADARG, "spb_session_kv_read: position never written");
@@ -1093,6 +1114,19 @@ extern "C" int spb_session_kv_read(const spb_session *s, int layer, int pos, int
   CU(cudaStreamSynchronize(s->st));
   for (int g = 0; g < m->NKV; g++)
     CU(cudaMemcpy(out + (size_t)g * m->HD, base + kv_elem(hk, m->NL, m->NKV, m->HD, layer, g, pos), (size_t)m->HD * 4,
+                  cudaMemcpyDeviceToHost));
+  return SPB_OK;
+}
+
+extern "C" int spb_session_kv_bytes(const spb_session *s, int layer, int pos, int which, uint8_t *out) {
+  if (!s || !out || layer < 0 || layer >= s->m->NL || pos < 0 || pos >= s->pmax)
+    return set_err(SPB_EBADARG, "spb_session_kv_bytes: bad arg");
+  if (!s->kv.rb) return set_err(SPB_EBADARG, "spb_session_kv_bytes: not a Spinor session");
+  const spb_model *m = s->m;
+  const uint8_t *base = reinterpret_cast<const uint8_t *>(which ? s->kv.v : s->kv.k);
+  CU(cudaStreamSynchronize(s->st));
+  for (int g = 0; g < m->NKV; g++)
+    CU(cudaMemcpy(out + (size_t)g * s->kv.rb, base + kv_spin_off(s->kv, m->NKV, layer, g, pos), (size_t)s->kv.rb,
                   cudaMemcpyDeviceToHost));
   return SPB_OK;
 }

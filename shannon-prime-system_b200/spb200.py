@@ -17,6 +17,7 @@ L1_SO = os.path.join(HERE, "libspb200_l1.so")
 
 SPB_OK, SPB_ENOMEM, SPB_EBADARG, SPB_EBADSTATE = 0, -1, -3, -4
 SPB_EUNSUPPORTED, SPB_ECONTEXT_FULL, SPB_ECUDA, SPB_EOOM, SPB_ERANGE = -5, -33, -40, -43, -50
+SPB_KV_SPINOR = 1   # spb_session_open_ex flag: K/V rows as Spinor blocks
 
 # symbols include/spb200.h declares (checked by the CPU test suite)
 CORE_SYMBOLS = [
@@ -33,7 +34,7 @@ CORE_SYMBOLS = [
     "spb_tp_shard", "spb_tp_unique_id", "spb_tp_open", "spb_tp_close", "spb_tp_rank", "spb_tp_world",
     "spb_model_synthetic_tp", "spb_model_upload_tp", "spb_tp_p2p_init", "spb_tp_p2p_connect",
     "spb_tp_p2p_loopback", "spb_kvpool_create", "spb_kvpool_free", "spb_kvpool_free_pages",
-    "spb_session_open_paged",
+    "spb_session_open_paged", "spb_session_open_ex", "spb_session_kv_bytes",
 ]
 L1_SYMBOLS = ["spb_l1_forward", "spb_l1_backend", "spb_l1_kvdecode_table", "spb_l1_kvdecode_clone",
               "spb_l1_set_device", "spb_l1_release_model", "spb_l1_kvdecode_table_ext", "spb_l1_set_kv_pool"]
@@ -140,6 +141,8 @@ def load(path: str = CORE_SO):
         "spb_kvpool_create": ([vp, C.c_int, C.c_int, C.POINTER(vp)], C.c_int),
         "spb_kvpool_free": ([vp], None), "spb_kvpool_free_pages": ([vp], C.c_int),
         "spb_session_open_paged": ([vp, C.c_int, C.POINTER(vp)], C.c_int),
+        "spb_session_open_ex": ([vp, C.c_int, C.c_uint, C.POINTER(vp)], C.c_int),
+        "spb_session_kv_bytes": ([vp, C.c_int, C.c_int, C.c_int, vp], C.c_int),
         "spb_q4b_release": ([vp], None),
         "spb_q4b_info": ([vp, vp], C.c_int),
         "spb_q4b_matmul": ([vp, vp, C.c_int, vp, vp], C.c_int),
@@ -290,8 +293,9 @@ class Model:
         check(load().spb_forward(self.h, tokens.ctypes.data, tokens.size, lg.ctypes.data))
         return lg
 
-    def session(self, pmax):
-        return Session(self, pmax)
+    def session(self, pmax, spinor=False):
+        """A resident-KV session; spinor=True keeps K/V as Spinor blocks (SPB_KV_SPINOR)."""
+        return Session(self, pmax, flags=SPB_KV_SPINOR if spinor else 0)
 
     def free(self):
         if self.h:
@@ -322,12 +326,12 @@ class KvPool:
 
 
 class Session:
-    def __init__(self, model, pmax, handle=None):
-        self.model, self.pmax = model, pmax
+    def __init__(self, model, pmax, handle=None, flags=0):
+        self.model, self.pmax, self.flags = model, pmax, flags
         self.V = model.cfg.n_vocab
         if handle is None:
             handle = C.c_void_p()
-            check(load().spb_session_open(model.h, pmax, C.byref(handle)))
+            check(load().spb_session_open_ex(model.h, pmax, flags, C.byref(handle)))
         self.h = handle
 
     def prefill(self, tokens, logits=True):
@@ -362,12 +366,20 @@ class Session:
     def clone(self):
         h = C.c_void_p()
         check(load().spb_session_clone(self.h, C.byref(h)))
-        return Session(self.model, self.pmax, handle=h)
+        return Session(self.model, self.pmax, handle=h, flags=self.flags)
 
     def kv(self, layer, pos, which):
         c = self.model.cfg
         o = np.empty(c.n_head_kv * c.head_dim, np.int32)
         check(load().spb_session_kv_read(self.h, layer, pos, which, o.ctypes.data))
+        return o
+
+    def kv_bytes(self, layer, pos, which):
+        """A Spinor session's cached blocks of one layer and position (uint8)."""
+        c = self.model.cfg
+        nb = 1 if c.head_dim <= 55 else (c.head_dim + 54) // 55
+        o = np.empty(c.n_head_kv * nb * 63, np.uint8)
+        check(load().spb_session_kv_bytes(self.h, layer, pos, which, o.ctypes.data))
         return o
 
     def stream(self):

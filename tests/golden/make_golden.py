@@ -79,5 +79,54 @@ def main():
     print("wrote", len(out), "arrays")
 
 
+SPINOR_LENS = [1, 7, 43, 54, 55, 56, 64, 110, 111, 128, 200, 256]
+
+
+def spinor_inputs(rng):
+    """Seeded head rows for the Spinor KV codec: float rows at several scales (zeros, exact
+    rounding ties and saturation included), and K rows on the 2^16 score grid."""
+    rows = []
+    for k in SPINOR_LENS:
+        for sc in (1e-3, 1.0, 300.0):
+            rows.append((rng.standard_normal(k) * sc).astype(np.float32))
+        v = rng.integers(-254, 255, k).astype(np.float32) / 2.0   # halves: rounding ties
+        v[0] = 127.0
+        rows.append(v)
+        z = np.zeros(k, np.float32)
+        rows.append(z)
+        if k > 3:
+            z2 = (rng.standard_normal(k) * 5).astype(np.float32)
+            z2[::3] = 0.0
+            z2[1] = -0.0
+            rows.append(z2)
+    grids = [rng.integers(-(1 << 24) + 1, 1 << 24, k).astype(np.int32) for k in (64, 128, 256)]
+    grids += [(rng.standard_normal(256) * 65536 * 3).astype(np.int32)]
+    return rows, grids
+
+
+def spinor():
+    """Spinor blocks from the reference's own codec (core/vht2/spinor_block.c, vht2.c,
+    mobius_reorder.c): encode_vec and decode_vec of every seeded row."""
+    C.CDLL(xref.SPREF_SO, mode=C.RTLD_GLOBAL)
+    L = C.CDLL(xref.SPREF_SO)
+    L.sp_spinor_encode_vec.argtypes = [C.c_void_p, C.c_int, C.c_void_p]
+    L.sp_spinor_decode_vec.argtypes = [C.c_void_p, C.c_int, C.c_void_p]
+    rows, grids = spinor_inputs(np.random.default_rng(20261202))
+    out = {}
+    for i, v in enumerate(rows + [g.astype(np.float32) * np.float32(1.0 / 65536) for g in grids]):
+        nb = 1 if v.size <= 55 else (v.size + 54) // 55
+        blk = np.zeros(nb * 63, np.uint8)
+        L.sp_spinor_encode_vec(v.ctypes.data, v.size, blk.ctypes.data)
+        dec = np.zeros(v.size, np.float32)
+        rc = L.sp_spinor_decode_vec(blk.ctypes.data, v.size, dec.ctypes.data)
+        assert rc == 0
+        out[f"sp{i}_v"], out[f"sp{i}_blocks"], out[f"sp{i}_dec"] = v, blk, dec
+    np.savez_compressed(os.path.join(HERE, "spinor_vectors.npz"), **out)
+    print("wrote", len(out), "arrays")
+
+
 if __name__ == "__main__":
-    main()
+    if sys.argv[1:] == ["spinor"]:
+        spinor()
+    else:
+        main()
