@@ -72,6 +72,10 @@ def parse():
     p.add_argument("--q8-steps", type=int, default=512)
     p.add_argument("--spinor", type=int, default=1,
                    help="also time B=1 decode on a Spinor-block K/V session (SPB_KV_SPINOR); 0 skips it")
+    p.add_argument("--spin-batch", type=int, default=16,
+                   help="sessions of the long-context batch comparison (int32 against Spinor K/V); 0 skips it")
+    p.add_argument("--spin-ctx", type=int, default=4096, help="their shared prefix length")
+    p.add_argument("--spin-batch-steps", type=int, default=8)
     p.add_argument("--no-tp", action="store_true", help="N>1: skip the tensor-parallel objects")
     p.add_argument("--tp", action="store_true", help="(default with N>1) the tensor-parallel objects")
     return p.parse_args()
@@ -520,6 +524,47 @@ def measure_spinor(m, cfg, args, max_over_ranks, barrier, hbm_gbs):
             "note": "every K/V row encoded by the kernel producing it, decoded inside the attention"}
 
 
+def measure_spinor_batch(m, cfg, args, max_over_ranks, hbm_gbs):
+    """Long-context batch decode, K/V as int32 rows against Spinor blocks: one session prefills a
+    --spin-ctx prefix, --spin-batch - 1 clones fork it (a shared prompt), and the sessions decode
+    together through spb_batch_decode_step (distinct tokens per row). At this context the
+    attention reads more bytes than the weights, which is where the 3.25x smaller rows pay."""
+    import torch
+    import spb200
+    import spmodel
+    S, L, K, W = args.spin_batch, args.spin_ctx, args.spin_batch_steps, 2
+    out = {"sessions": S, "ctx": L, "steps": K, "warmup": W,
+           "timing": "wall clock around K synchronous spb_batch_decode_step calls (S tokens H2D, S argmaxes D2H)"}
+    hd = cfg.head_dim
+    rb = (1 if hd <= 55 else (hd + 54) // 55) * 63
+    for name, spin in (("int32", False), ("spinor", True)):
+        s0 = m.session(L + W + K + 8, spinor=spin)
+        toks = spmodel.gen_tokens(args.seed + 400, L, cfg.n_vocab)
+        t0 = time.perf_counter()
+        s0.prefill(toks, logits=False)
+        torch.cuda.synchronize()
+        pre = time.perf_counter() - t0
+        sessions = [s0] + [s0.clone() for _ in range(S - 1)]
+        cur = [int(t) for t in spmodel.gen_tokens(args.seed + 401, S, cfg.n_vocab)]
+        for _ in range(W):
+            _, am = spb200.batch_decode(sessions, cur, logits=False)
+            cur = am
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(K):
+            _, am = spb200.batch_decode(sessions, cur, logits=False)
+            cur = am
+        dt = max_over_ranks((time.perf_counter() - t0) * 1e3) / 1e3
+        for s in sessions:
+            s.close()
+        kvb = S * kv_bytes_per_token(cfg, L + W + K // 2, rb if spin else hd * 4)
+        out[name] = {"value": round(S * K / dt, 2), "unit": "tokens/s", "ms_per_step": round(dt / K * 1e3, 3),
+                     "kv_bytes_per_step": kvb, "prefill_s_untimed": round(pre, 2),
+                     "step_bytes_frac_of_hbm": round((m.weight_bytes() + kvb) / (dt / K) / 1e9 / hbm_gbs, 4)}
+    out["spinor_over_int32"] = round(out["spinor"]["value"] / out["int32"]["value"], 3)
+    return out
+
+
 def measure_tp(cfg, args, rank, local, world, max_over_ranks, barrier, p2p=True):
     """One session of the model split over the group (spb_model_synthetic_tp): K greedy steps
     timed with CUDA events on the session stream, max over ranks; every rank produces the
@@ -681,6 +726,10 @@ def run_spb(args):
         spin = measure_spinor(m, cfg, args, max_over_ranks, barrier, peaks()[0])
         spin["value"] = round(world * spin["value"], 3)
 
+    spin_b = None
+    if args.spin_batch > 0:
+        spin_b = measure_spinor_batch(m, cfg, args, max_over_ranks, peaks()[0])
+
     q8 = None
     if args.q8_prefill > 0:
         q8 = measure_qwen8b(args, local, rank, max_over_ranks, barrier, peaks()[0])
@@ -759,6 +808,7 @@ def run_spb(args):
         "spec": spec,
         "qwen8b": q8,
         "spinor_kv": spin,
+        "spinor_batch_long_ctx": spin_b,
         "prefill": prefill,
         "config2_sweep": sweep,
     }

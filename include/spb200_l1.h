@@ -69,6 +69,12 @@ const struct spb_kvdecode_dispatch_ext *spb_l1_kvdecode_table_ext(void);
  * cache its own allocation. */
 int spb_l1_set_kv_pool(int page_positions, int n_pages);
 
+/* spb_session_open_ex flags of the section-6b caches opened after this call: SPB_KV_SPINOR keeps
+ * their K/V rows as the reference's 63-byte Spinor blocks (its SP_KV_SPINOR session flag,
+ * sp_l1.h:156-157, which the frozen open row cannot carry); 0 (default) = int32 rows. A page pool
+ * set with spb_l1_set_kv_pool takes precedence. No reference counterpart beyond that flag. */
+int spb_l1_set_kv_flags(unsigned flags);
+
 /* Device used for models uploaded after this call (default 0). */
 int spb_l1_set_device(int device);
 

@@ -1365,11 +1365,12 @@ __global__ void k_rope_kv(RopeArgs a) {
 
 cudaError_t launch_rope_kv(const RopeArgs &a, cudaStream_t st) {
   if (a.HD & 1 || a.HD / 2 > 1024) return cudaErrorInvalidValue;
-  if (a.kv.rb > 0 && (a.rows || a.kv.ptab || a.HD < 64 || a.kv.rb != spin_row_bytes(a.HD))) return cudaErrorInvalidValue;
+  if (a.kv.rb > 0 && (a.kv.ptab || a.HD < 64 || a.kv.rb != spin_row_bytes(a.HD))) return cudaErrorInvalidValue;
   dim3 grid(a.NH + 2 * a.NKV, a.ntok);
-  // Spinor caches: + CRC tables, a 64-byte block image per warp, the rotated K row
+  // Spinor caches (or batch rows, each of which may be one): + CRC tables, a 64-byte block image
+  // per warp, the rotated K row
   const size_t smem = 2 * a.HD * sizeof(float) +
-                      (a.kv.rb > 0 ? 1024 + 64 * (size_t)((a.HD / 2 + 31) / 32) + (size_t)a.HD * 4 : 0);
+                      (a.kv.rb > 0 || a.rows ? 1024 + 64 * (size_t)((a.HD / 2 + 31) / 32) + (size_t)a.HD * 4 : 0);
   return launch_k(k_rope_kv, grid, dim3(a.HD / 2), smem, st, 1, a);
 }
 
@@ -1432,9 +1433,26 @@ __global__ void __launch_bounds__(ATTN_THREADS, 2) k_attn(AttnArgs a, int cmax, 
   }
   const int s0 = (a.win >= 0 && p - a.win + 1 > 0) ? p - a.win + 1 : 0;
   const int n = p - s0 + 1;
-  const int c = (n + CL - 1) / CL;
-  const int c0 = s0 + rank * c;
-  const int c1 = min(c0 + c, p + 1);
+  // positions [c0, c1) of this rank: an equal split, except that with the fused QK-norm + RoPE
+  // the last rank (which also normalises, rotates and stores the new K and V rows) takes own_pct
+  // percent of an equal share and the others split the rest
+  int c0, c1;
+  if (a.qkv && CL > 1 && a.own_pct < 100) {
+    const int c = (n + CL - 1) / CL;
+    const int own = max(1, min(n, c * a.own_pct / 100));
+    const int rest = n - own, cr = (rest + CL - 2) / (CL - 1);
+    if (rank < CL - 1) {
+      c0 = s0 + rank * cr;
+      c1 = min(c0 + cr, s0 + rest);
+    } else {
+      c0 = s0 + rest;
+      c1 = p + 1;
+    }
+  } else {
+    const int c = (n + CL - 1) / CL;
+    c0 = s0 + rank * c;
+    c1 = min(c0 + c, p + 1);
+  }
   const int cn = max(c1 - c0, 0);
   const int nsub = (cn + SUB - 1) / SUB;
   const int total = 2 * nsub;                 // K slices, then V slices
@@ -2192,6 +2210,20 @@ static size_t attn_smem(int cmax, int cl, bool fused, bool spin = false) {
          (spin ? 2048 : 0);   // Spinor caches: CRC tables, decode multipliers
 }
 
+// SPB_ATTN_OWN: the share of positions (percent of an equal split) the owning rank of a fused
+// decode row takes (100: an equal split; default 50, measured 3.79 against 3.83-3.86 ms per
+// 12B decode step)
+static int attn_own_pct() {
+  static int v = -1;
+  if (v < 0) {
+    const char *e = getenv("SPB_ATTN_OWN");
+    v = e ? atoi(e) : 50;
+    if (v < 0) v = 0;
+    if (v > 100) v = 100;
+  }
+  return v;
+}
+
 template <int HD, int G>
 static cudaError_t attn_cl(const AttnArgs &a, cudaStream_t st) {
   // Largest cluster: 16 CTAs where the device can co-schedule them (asked once, before any
@@ -2231,19 +2263,23 @@ static cudaError_t attn_cl(const AttnArgs &a, cudaStream_t st) {
   const int span = a.win >= 0 ? std::min(a.P, a.win) : a.P;
   int cl = 1;
   while (cl < clmax && ((long)a.ntok * a.NKV * cl < 2L * nsm || span > cl * ATTN_SPAN)) cl *= 2;
-  const bool fused = a.qkv != nullptr, spin = a.kv.rb > 0;
+  // (batch rows may each keep Spinor blocks: their launches always carry the Spinor scratch)
+  const bool fused = a.qkv != nullptr, spin = a.kv.rb > 0 || a.rows != nullptr;
   while (cl < clmax && attn_smem<HD, G>((a.P + cl - 1) / cl, cl, fused, spin) > 200 * 1024) cl *= 2;
-  const int cmax = (a.P + cl - 1) / cl;
+  // a rank's positions at most (the other ranks' share grows when the owner's shrinks)
+  AttnArgs b = a;
+  b.own_pct = attn_own_pct();
+  const int cmax = (fused && cl > 1 && b.own_pct < 100) ? (a.P + cl - 2) / (cl - 1) : (a.P + cl - 1) / cl;
   const size_t smem = attn_smem<HD, G>(cmax, cl, fused, spin);
   if (smem > 200 * 1024) return cudaErrorInvalidValue;
-  return launch_k(kern, dim3(cl, a.NKV, a.ntok), dim3(ATTN_THREADS), smem, st, cl, a, cmax, cl);
+  return launch_k(kern, dim3(cl, a.NKV, a.ntok), dim3(ATTN_THREADS), smem, st, cl, b, cmax, cl);
 }
 
 cudaError_t launch_attn(const AttnArgs &a, cudaStream_t st) {
   const int G = a.NH / a.NKV;
   if (a.NH % a.NKV || a.P <= 0) return cudaErrorInvalidValue;
-  // Spinor-block caches: one session's own unpaged cache, head_dim 64 / 128 / 256
-  if (a.kv.rb > 0 && (a.rows || a.kv.ptab || a.HD < 64 || a.kv.rb != spin_row_bytes(a.HD))) return cudaErrorInvalidValue;
+  // Spinor-block caches: unpaged caches (a session's own, or each batch row's), head_dim 64 / 128 / 256
+  if (a.kv.rb > 0 && (a.kv.ptab || a.HD < 64 || a.kv.rb != spin_row_bytes(a.HD))) return cudaErrorInvalidValue;
   // prefill chunks (rows of one session, K/V already stored by k_rope_kv): row tiles
   const bool tile = !a.rows && !a.qkv && a.kv.rb == 0 && attn_tile_min() > 0 && a.ntok >= attn_tile_min();
 #define SPB_ATTN_CASE(HDV, GV) \

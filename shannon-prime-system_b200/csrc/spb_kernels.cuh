@@ -176,6 +176,7 @@ struct AttnArgs {
   const float *q_norm, *k_norm;
   const uint64_t *W, *T;
   uint64_t gain;
+  int own_pct;             // set by launch_attn: the owning rank's share of positions (percent)
 };
 cudaError_t launch_attn(const AttnArgs &a, cudaStream_t st);
 

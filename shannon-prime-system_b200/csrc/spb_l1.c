@@ -24,6 +24,7 @@
 
 #define SPB_L1_MAX_MODELS 32
 
+static unsigned g_kv_flags = 0;   /* spb_session_open_ex flags of section-6b caches */
 static pthread_mutex_t g_mu = PTHREAD_MUTEX_INITIALIZER;
 static struct { const void *qm; spb_model *m; spb_kvpool *pool; } g_models[SPB_L1_MAX_MODELS];
 static int g_device = 0;
@@ -162,6 +163,15 @@ void spb_l1_release_model(const void *qm_opaque) {
 
 void *spb_l1_backend(void) { return &g_backend_tag; }
 
+/* K/V kept as Spinor blocks (SPB_KV_SPINOR) for caches opened after this call; the engine-side
+ * counterpart of the reference's SP_KV_SPINOR session flag (sp_l1.h:156), which the frozen
+ * section-6b open row cannot carry. Unpaged caches only (a page pool takes precedence). */
+int spb_l1_set_kv_flags(unsigned flags) {
+    if (flags & ~(unsigned)SPB_KV_SPINOR) { sp_set_error("spb200: set_kv_flags: unknown flags"); return 1; }
+    __atomic_store_n(&g_kv_flags, flags, __ATOMIC_RELAXED);
+    return 0;
+}
+
 int spb_l1_forward(void *handle, const void *qm_opaque, const int32_t *tokens, int n_tok, float *logits) {
     (void)handle;
     spb_model *m = model_for(qm_opaque, NULL);
@@ -178,7 +188,8 @@ static int kv_open(const void *qm_opaque, int pmax, sp_kvdecode_handle **out) {
     spb_model *m = model_for(qm_opaque, &pool);
     if (!m) return 1;
     spb_session *s = NULL;
-    const int rc = pool ? spb_session_open_paged(pool, pmax, &s) : spb_session_open(m, pmax, &s);
+    const unsigned flags = __atomic_load_n(&g_kv_flags, __ATOMIC_RELAXED);
+    const int rc = pool ? spb_session_open_paged(pool, pmax, &s) : spb_session_open_ex(m, pmax, flags, &s);
     if (rc != SPB_OK) return fail("open");
     *out = (sp_kvdecode_handle *)s;
     return 0;

@@ -1000,7 +1000,6 @@ extern "C" int spb_batch_decode_step(spb_session *const *ss, int B, const int32_
     spb_session *s = ss[i];
     if (!s || s->m != lead->m) return set_err(SPB_EBADARG, "spb_batch_decode_step: sessions must share one model");
     if (s->pos >= s->pmax) return set_err(SPB_ECONTEXT_FULL, "spb_batch_decode_step: session %d context full", i);
-    if (s->kv.rb) return set_err(SPB_EUNSUPPORTED, "spb_batch_decode_step: session %d keeps Spinor K/V (decode it alone)", i);
     for (int j = 0; j < i; j++)
       if (ss[j] == s) return set_err(SPB_EBADARG, "spb_batch_decode_step: session %d repeated", i);
     Pmax = std::max(Pmax, s->pmax);

@@ -37,7 +37,8 @@ CORE_SYMBOLS = [
     "spb_session_open_paged", "spb_session_open_ex", "spb_session_kv_bytes",
 ]
 L1_SYMBOLS = ["spb_l1_forward", "spb_l1_backend", "spb_l1_kvdecode_table", "spb_l1_kvdecode_clone",
-              "spb_l1_set_device", "spb_l1_release_model", "spb_l1_kvdecode_table_ext", "spb_l1_set_kv_pool"]
+              "spb_l1_set_device", "spb_l1_release_model", "spb_l1_kvdecode_table_ext", "spb_l1_set_kv_pool",
+              "spb_l1_set_kv_flags"]
 
 
 class SpbError(RuntimeError):

@@ -96,6 +96,45 @@ def test_section6b_decode(reflib, xr, cuda_ok, setup):
     L.sp_session_destroy(s)
 
 
+def test_section6b_spinor_kv(reflib, xr, cuda_ok, setup):
+    """Caches opened through the section-6b table after spb_l1_set_kv_flags(SPB_KV_SPINOR) keep
+    their K/V as Spinor blocks (the reference's SP_KV_SPINOR); the reference's own sp_decode_step
+    then returns XREF's Spinor-session logits byte for byte."""
+    cfg, T, model, l1 = setup
+    L = reflib.lib
+    assert l1.spb_l1_set_kv_flags(2) != 0   # unknown flag refused
+    assert l1.spb_l1_set_kv_flags(spb200.SPB_KV_SPINOR) == 0
+    try:
+        s = reflib.session(model, cfg.max_context)
+        qm = L.sp_session_qwen3_model(s)
+        dt = l1.spb_l1_kvdecode_table()
+        OPEN = C.CFUNCTYPE(C.c_int, C.c_void_p, C.c_int, C.POINTER(C.c_void_p))
+        PRE = C.CFUNCTYPE(C.c_int, C.c_void_p, C.c_void_p, C.c_int)
+        CLOSE = C.CFUNCTYPE(None, C.c_void_p)
+        fns = (C.c_void_p * 6).from_address(dt)
+        h = C.c_void_p()
+        assert OPEN(fns[0])(qm, cfg.max_context, C.byref(h)) == 0
+        toks = spmodel.gen_tokens(35, 16, cfg.n_vocab)
+        xs = xr.session(xref.build_desc(cfg, T), cfg.max_context, spinor=True)
+        lx = xs.prefill(toks)[-1]
+        rc, _ = reflib.prefill(s, toks, cfg.n_vocab)
+        assert rc == 0
+        assert PRE(fns[1])(h, toks.ctypes.data, toks.size) == 0
+        assert L.sp_session_register_kvdecode_backend(s, h, dt) == 0
+        tok = int(lx.argmax())
+        for i in range(8):
+            lx = xs.step(tok)
+            rc, lg = reflib.decode(s, tok, cfg.n_vocab)
+            assert rc == 0, reflib.err()
+            assert np.array_equal(u32(lg), u32(lx)), f"step {i}"
+            tok = int(lg.argmax())
+        L.sp_session_register_kvdecode_backend(s, None, None)
+        CLOSE(fns[5])(h)
+        L.sp_session_destroy(s)
+    finally:
+        assert l1.spb_l1_set_kv_flags(0) == 0
+
+
 def test_non_q4b_model_rejected(reflib, cuda_ok, tmp_path):
     """A model whose weights are not OK_Q4B arena tensors is refused with a clear error."""
     l1 = spb200.load_l1()

@@ -5,7 +5,7 @@ decode step) and decoded inside the attention from the blocks its bulk copies br
 
 Against XREF's Spinor session (oracle/xref_spinor.c, pinned to the reference's compiled codec by
 tests/test_spinor_codec.py): every logit, the greedy tokens, and the cached blocks byte for
-byte; clone and rewind; and the refusals."""
+byte; clone and rewind; batches mixing Spinor and int32 sessions; and the refusals."""
 import ctypes as C
 import dataclasses
 
@@ -125,9 +125,46 @@ def test_spinor_refusals(cuda_ok):
     o = np.zeros(cfg.n_head_kv * cfg.head_dim, np.int32)
     assert L.spb_session_kv_read(s.h, 0, 0, 0, o.ctypes.data) == spb200.SPB_EUNSUPPORTED
     plain = m.session(64)
-    arr = (C.c_void_p * 2)(s.h, plain.h)
-    toks = np.array([1, 2], np.int32)
-    assert L.spb_batch_decode_step(arr, 2, toks.ctypes.data, None, None) == spb200.SPB_EUNSUPPORTED
     b = np.zeros(16, np.uint8)
     assert L.spb_session_kv_bytes(plain.h, 0, 0, 0, b.ctypes.data) == spb200.SPB_EBADARG
     s.close(); plain.close(); m.free()
+
+
+def test_spinor_batch_rows(xr, cuda_ok):
+    """spb_batch_decode_step over sessions at different positions, three keeping Spinor K/V and
+    one int32 rows: every row's logits equal its own XREF session's (Spinor or not)."""
+    cfg = dataclasses.replace(spmodel.CONFIGS["micro_gemma"], head_dim=128, n_head=8, n_head_kv=2,
+                              sliding_window=48, max_context=256)
+    T = spmodel.gen_model(cfg, seed=58)
+    m = spb200.Model.upload(cfg, T)
+    d = xref.build_desc(cfg, T)
+    kinds = [True, False, True, True]
+    lens = [70, 33, 150, 9]
+    ss, xs = [], []
+    for i, (sp, n) in enumerate(zip(kinds, lens)):
+        s = m.session(cfg.max_context, spinor=sp)
+        x = xr.session(d, cfg.max_context, spinor=sp)
+        toks = spmodel.gen_tokens(60 + i, n, cfg.n_vocab)
+        s.prefill(toks, logits=False)
+        x.prefill(toks, all_logits=False)
+        ss.append(s)
+        xs.append(x)
+    L = spb200.load()
+    arr = (C.c_void_p * len(ss))(*[s.h for s in ss])
+    toks = np.array([3, 5, 7, 11], np.int32)
+    for step in range(4):
+        lg = np.empty((len(ss), cfg.n_vocab), np.float32)
+        am = np.empty(len(ss), np.int32)
+        spb200.check(L.spb_batch_decode_step(arr, len(ss), toks.ctypes.data, lg.ctypes.data, am.ctypes.data))
+        for i, x in enumerate(xs):
+            want = x.step(int(toks[i]))
+            assert np.array_equal(u32(lg[i]), u32(want)), (step, i)
+        toks = am.copy()
+    for i, (s, x) in enumerate(zip(ss, xs)):
+        p = lens[i] + 3
+        if kinds[i]:
+            assert np.array_equal(s.kv_bytes(1, p, 0), x.kv_bytes(1, p, 0))
+            assert np.array_equal(s.kv_bytes(0, p, 1), x.kv_bytes(0, p, 1))
+        s.close()
+        x.close()
+    m.free()
