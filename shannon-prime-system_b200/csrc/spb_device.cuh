@@ -35,6 +35,28 @@ __device__ __forceinline__ int32_t block_dot(const uint4 cw, const int4 x0, cons
   return s;
 }
 
+// d = c + sum of the 4 unsigned bytes of a times the 4 signed bytes of b
+__device__ __forceinline__ int32_t dp4a_us(uint32_t a, int32_t b, int32_t c) {
+  int32_t d;
+  asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
+// block_dot(cw, x0, x1) + corr with one mask-and-flip per nibble half and no shift: even columns
+// (w & 0x0F) ^ 0x08 = code + 8 per byte; odd columns (w & 0xF0) ^ 0x80 = 16 (code + 8) per
+// unsigned byte, so that half's sum is exactly 16 times its block sum (an arithmetic shift by 4)
+__device__ __forceinline__ int32_t block_dot_corr(const uint4 cw, const int4 x0, const int4 x1, int32_t corr) {
+  const uint32_t w[4] = {cw.x, cw.y, cw.z, cw.w};
+  const int32_t xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+  int32_t lo = corr, hi = 0;
+#pragma unroll
+  for (int g = 0; g < 4; g++) {
+    lo = dp4a_us((w[g] & 0x0F0F0F0Fu) ^ 0x08080808u, xv[2 * g], lo);
+    hi = dp4a_us((w[g] & 0xF0F0F0F0u) ^ 0x80808080u, xv[2 * g + 1], hi);
+  }
+  return lo + (hi >> 4);
+}
+
 // acc += k * isum with the f16 block scale as k = m * 2^sh (|m| < 2^11, sh < 30):
 // one 32-bit multiply (|m*isum| < 2^26) and one widening multiply-add by 2^sh.
 __device__ __forceinline__ void scale_acc(int64_t &acc, uint32_t h, int32_t isum) {

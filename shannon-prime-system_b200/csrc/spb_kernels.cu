@@ -97,9 +97,16 @@ __device__ __forceinline__ uint4 ld_stream_u4(const uint8_t *p) {
   return v;
 }
 
+// warps sharing one row at batch 1 (KSF: forced, 0 = the default rule)
+template <int NT, int NM, int NCH, int RPW, int KSF>
+__host__ __device__ constexpr int gemv_ks() {
+  return KSF ? KSF : (NT == 1 && RPW == 1 && NCH * NM >= 8) ? 2 : 1;
+}
+
 // NT token rows, epilogue EPI, NCH 16-byte vectors per lane per row (cols <= 1024*NCH),
-// RPW rows per warp group. ymax (nullable): per-token max |y| via atomicMax of f32 bits.
-template <int NT, int EPI, int NCH, int RPW>
+// RPW rows per warp group, KSF warps per row (0: the default rule).
+// ymax (nullable): per-token max |y| via atomicMax of f32 bits.
+template <int NT, int EPI, int NCH, int RPW, int KSF = 0>
 __global__ void __launch_bounds__(GEMV_THREADS)
 k_gemv(DevQ4B w, DevQ4B w2, DevAct act, float *__restrict__ y, int ldy, uint32_t *err, uint32_t *ymax,
        unsigned long long *amax) {
@@ -112,14 +119,14 @@ k_gemv(DevQ4B w, DevQ4B w2, DevAct act, float *__restrict__ y, int ldy, uint32_t
   double *dsc = reinterpret_cast<double *>(xs + ((NT * nblk + 1) & ~1));   // [NT]
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   // KS = 2 (single rows of >= 8 code vectors per lane: the FFN down projection, the gate/up
-  // pair at K > 1024): the two warps of a pair take the
-  // two halves of a row's 32-column blocks, so each holds half the code vectors (half the
-  // registers: twice the resident warps); the odd warp hands its exact int64 half to the even
-  // warp through shared memory under a 64-thread named barrier, and only even warps finish rows
-  constexpr int KS = (NT == 1 && RPW == 1 && NCH * NM >= 8) ? 2 : 1;
+  // pair at K > 1024), or 4 where forced: the KS warps of a group take KS parts of a row's
+  // 32-column blocks, so each holds 1/KS of the code vectors (fewer registers: more resident
+  // warps); the other warps hand their exact int64 parts to the group's first warp through
+  // shared memory under a named barrier of the group, and only first warps finish rows
+  constexpr int KS = gemv_ks<NT, NM, NCH, RPW, KSF>();
   constexpr int NCHW = NCH / KS;   // code vectors per lane per row held by one warp
   const int half = warp % KS, pair = warp / KS;
-  __shared__ int64_t ks_part[GEMV_WARPS / KS][NM];
+  __shared__ int64_t ks_part[GEMV_WARPS / KS][KS][NM];
   const int rows = w.rows;
   const size_t rstride = (size_t)(K >> 1);
   const int ngroups = (rows + RPW - 1) / RPW;
@@ -217,11 +224,15 @@ k_gemv(DevQ4B w, DevQ4B w2, DevAct act, float *__restrict__ y, int ldy, uint32_t
           const int4 *xb = reinterpret_cast<const int4 *>(xw + t * kw + b * 8);
           const int4 x0 = xb[0], x1 = xb[1];
           const int32_t corr = -8 * xs[t * nblk + b];
+          // the leaner block sum where instruction issue bounds the kernel (4 vectors per lane:
+          // Q|K|V, O, gate/up, LM head); the down projection (16) is bound by latency, and
+          // measured slower with it
 #pragma unroll
           for (int m = 0; m < NM; m++)
 #pragma unroll
             for (int r = 0; r < RPW; r++)
-              scale_acc(acc[m][r][t], hw[m][r][j], block_dot(cw[m][r][j], x0, x1) + corr);
+              scale_acc(acc[m][r][t], hw[m][r][j],
+                        NCH <= 4 ? block_dot_corr(cw[m][r][j], x0, x1, corr) : block_dot(cw[m][r][j], x0, x1) + corr);
         }
       }
     }
@@ -235,16 +246,18 @@ k_gemv(DevQ4B w, DevQ4B w2, DevAct act, float *__restrict__ y, int ldy, uint32_t
       for (int t = 0; t < NT; t++) {
 #pragma unroll
         for (int m = 0; m < NM; m++) acc[m][r][t] = warp_sum_i64(acc[m][r][t]);
-        if (KS == 2) {   // (KS = 2 only with RPW = 1, NT = 1)
+        if (KS > 1) {   // (KS > 1 only with RPW = 1, NT = 1)
 #pragma unroll
           for (int m = 0; m < NM; m++)
-            if (half == 1 && lane == 0) ks_part[pair][m] = acc[m][r][t];
-          asm volatile("bar.sync %0, 64;" ::"r"(1 + pair) : "memory");
+            if (half > 0 && lane == 0) ks_part[pair][half][m] = acc[m][r][t];
+          asm volatile("bar.sync %0, %1;" ::"r"(1 + pair), "n"(32 * KS) : "memory");
 #pragma unroll
           for (int m = 0; m < NM; m++)
-            if (half == 0) acc[m][r][t] += ks_part[pair][m];
-          asm volatile("bar.sync %0, 64;" ::"r"(1 + pair) : "memory");   // the slot is free again
-          if (half == 1) continue;
+            if (half == 0)
+#pragma unroll
+              for (int h = 1; h < KS; h++) acc[m][r][t] += ks_part[pair][h][m];
+          asm volatile("bar.sync %0, %1;" ::"r"(1 + pair), "n"(32 * KS) : "memory");   // the slots are free again
+          if (half > 0) continue;
         }
         if (lane == npend && row < rows) {
           pa = acc[0][r][t];
@@ -299,13 +312,13 @@ k_gemv(DevQ4B w, DevQ4B w2, DevAct act, float *__restrict__ y, int ldy, uint32_t
   }
 }
 
-template <int NT, int EPI, int NCH, int RPW>
+template <int NT, int EPI, int NCH, int RPW, int KSF = 0>
 static cudaError_t gemv_launch(const DevQ4B &w, const DevQ4B &w2, const DevAct &act, float *y, int ldy,
                                uint32_t *err, uint32_t *ymax, unsigned long long *amax, cudaStream_t st,
                                int grid_limit) {
   const int K = w.cols, nblk = K >> 5;
   const size_t smem = (size_t)NT * K + (size_t)(((NT * nblk + 1) & ~1)) * 4 + (size_t)NT * 8;
-  auto kern = k_gemv<NT, EPI, NCH, RPW>;
+  auto kern = k_gemv<NT, EPI, NCH, RPW, KSF>;
   static int occ = 0, nsm = 0;
   static size_t occ_smem = 0;
   if (smem > 48 * 1024) {
@@ -322,7 +335,7 @@ static cudaError_t gemv_launch(const DevQ4B &w, const DevQ4B &w2, const DevAct &
   }
   const int ngroups = (w.rows + RPW - 1) / RPW;
   constexpr int NM = epi_pair(EPI) ? 2 : 1;
-  constexpr int KS = (NT == 1 && RPW == 1 && NCH * NM >= 8) ? 2 : 1;   // as in k_gemv
+  constexpr int KS = gemv_ks<NT, NM, NCH, RPW, KSF>();   // as in k_gemv
   constexpr int GPC = GEMV_WARPS / KS;                                      // row groups per CTA round
   int grid = (ngroups + GPC - 1) / GPC;
   const int resident = nsm * occ;
@@ -341,14 +354,41 @@ static cudaError_t gemv_rpw(const DevQ4B &w, const DevQ4B &w2, const DevAct &act
   return gemv_launch<NT, EPI, NCH, 1>(w, w2, act, y, ldy, err, ymax, amax, st, grid_limit);
 }
 
+// warps per row at batch 1, per matrix kind (SPB_GEMV_KS1 single matrices of <= 4 vectors per
+// lane, default 1; SPB_GEMV_KSG gate/up pairs of <= 4, default 2; SPB_GEMV_KS16 single matrices
+// of 9-16, default 4): fewer code registers per warp, more resident warps
+static int gemv_ks_env(const char *name, int dflt) {
+  const char *e = getenv(name);
+  const int v = e ? atoi(e) : dflt;
+  return (v == 1 || v == 2 || v == 4 || v == 8) ? v : dflt;
+}
+
 template <int NT, int EPI>
 static cudaError_t gemv_nch(const DevQ4B &w, const DevQ4B &w2, const DevAct &act, float *y, int ldy,
                             uint32_t *err, uint32_t *ymax, unsigned long long *amax, cudaStream_t st,
                             int grid_limit) {
+  static int ks1 = 0, ksg = 0, ks16 = 0;
+  if (!ks1) {
+    ks1 = gemv_ks_env("SPB_GEMV_KS1", 1);
+    ksg = gemv_ks_env("SPB_GEMV_KSG", 2);
+    ks16 = gemv_ks_env("SPB_GEMV_KS16", 4);
+  }
   const int per_lane = ((w.cols >> 5) + 31) / 32;
   if (per_lane <= 1) return gemv_rpw<NT, EPI, 1>(w, w2, act, y, ldy, err, ymax, amax, st, grid_limit);
-  if (per_lane <= 4) return gemv_rpw<NT, EPI, 4>(w, w2, act, y, ldy, err, ymax, amax, st, grid_limit);
-  if (per_lane <= 16) return gemv_rpw<NT, EPI, 16>(w, w2, act, y, ldy, err, ymax, amax, st, grid_limit);
+  if (per_lane <= 4) {
+    if (NT == 1 && !epi_pair(EPI) && ks1 == 2)
+      return gemv_launch<NT, EPI, 4, 1, 2>(w, w2, act, y, ldy, err, ymax, amax, st, grid_limit);
+    if (NT == 1 && epi_pair(EPI) && ksg == 4)
+      return gemv_launch<NT, EPI, 4, 1, 4>(w, w2, act, y, ldy, err, ymax, amax, st, grid_limit);
+    return gemv_rpw<NT, EPI, 4>(w, w2, act, y, ldy, err, ymax, amax, st, grid_limit);
+  }
+  if (per_lane <= 16) {
+    if (NT == 1 && !epi_pair(EPI) && ks16 == 4)
+      return gemv_launch<NT, EPI, 16, 1, 4>(w, w2, act, y, ldy, err, ymax, amax, st, grid_limit);
+    if (NT == 1 && !epi_pair(EPI) && ks16 == 8)
+      return gemv_launch<NT, EPI, 16, 1, 8>(w, w2, act, y, ldy, err, ymax, amax, st, grid_limit);
+    return gemv_rpw<NT, EPI, 16>(w, w2, act, y, ldy, err, ymax, amax, st, grid_limit);
+  }
   return cudaErrorInvalidValue;
 }
 
