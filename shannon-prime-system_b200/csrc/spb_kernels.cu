@@ -1407,10 +1407,10 @@ cudaError_t launch_rope_kv(const RopeArgs &a, cudaStream_t st) {
   if (a.HD & 1 || a.HD / 2 > 1024) return cudaErrorInvalidValue;
   if (a.kv.rb > 0 && (a.kv.ptab || a.HD < 64 || a.kv.rb != spin_row_bytes(a.HD))) return cudaErrorInvalidValue;
   dim3 grid(a.NH + 2 * a.NKV, a.ntok);
-  // Spinor caches (or batch rows, each of which may be one): + CRC tables, a 64-byte block image
-  // per warp, the rotated K row
+  // Spinor caches (or batch rows with one among them): + CRC tables, a 64-byte block image per
+  // warp, the rotated K row
   const size_t smem = 2 * a.HD * sizeof(float) +
-                      (a.kv.rb > 0 || a.rows ? 1024 + 64 * (size_t)((a.HD / 2 + 31) / 32) + (size_t)a.HD * 4 : 0);
+                      (a.kv.rb > 0 || (a.rows && a.rows_spin) ? 1024 + 64 * (size_t)((a.HD / 2 + 31) / 32) + (size_t)a.HD * 4 : 0);
   return launch_k(k_rope_kv, grid, dim3(a.HD / 2), smem, st, 1, a);
 }
 
@@ -2303,8 +2303,9 @@ static cudaError_t attn_cl(const AttnArgs &a, cudaStream_t st) {
   const int span = a.win >= 0 ? std::min(a.P, a.win) : a.P;
   int cl = 1;
   while (cl < clmax && ((long)a.ntok * a.NKV * cl < 2L * nsm || span > cl * ATTN_SPAN)) cl *= 2;
-  // (batch rows may each keep Spinor blocks: their launches always carry the Spinor scratch)
-  const bool fused = a.qkv != nullptr, spin = a.kv.rb > 0 || a.rows != nullptr;
+  // (batch rows with a Spinor row among them carry the Spinor scratch: 2 KB that would otherwise
+  // cost the 64-session attention its second CTA per SM)
+  const bool fused = a.qkv != nullptr, spin = a.kv.rb > 0 || (a.rows != nullptr && a.rows_spin);
   while (cl < clmax && attn_smem<HD, G>((a.P + cl - 1) / cl, cl, fused, spin) > 200 * 1024) cl *= 2;
   // a rank's positions at most (the other ranks' share grows when the owner's shrinks)
   AttnArgs b = a;

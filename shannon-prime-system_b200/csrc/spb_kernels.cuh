@@ -152,6 +152,7 @@ struct RopeArgs {
   uint32_t *zero_slot;     // nullable: per-row max slots cleared for the attention output
   const BatchRow *rows;    // nullable: rows of different sessions (kv, P, pos_dev unused)
   int layer;               // the layer whose cache rows are written
+  int rows_spin;           // with rows: 1 when any row keeps Spinor blocks (sizes the shared memory)
 };
 cudaError_t launch_rope_kv(const RopeArgs &a, cudaStream_t st);
 
@@ -177,6 +178,7 @@ struct AttnArgs {
   const uint64_t *W, *T;
   uint64_t gain;
   int own_pct;             // set by launch_attn: the owning rank's share of positions (percent)
+  int rows_spin;           // with rows: 1 when any row keeps Spinor blocks (sizes the shared memory)
 };
 cudaError_t launch_attn(const AttnArgs &a, cudaStream_t st);
 

@@ -807,7 +807,7 @@ static bool rope_fused_enabled() {
 // rows (device, [nt]), row t belongs to its own session: RoPE/KV store and attention use that
 // session's cache and position; Pmax is the largest of their capacities.
 static cudaError_t enqueue_rows(spb_session *s, int nt, bool want_logits, const BatchRow *rows = nullptr,
-                                int Pmax = 0) {
+                                int Pmax = 0, bool rows_spin = false) {
   spb_model *m = s->m;
   cudaStream_t st = s->st;
   const int E = m->E, QKV = m->QD + 2 * m->KVD;
@@ -852,12 +852,14 @@ static cudaError_t enqueue_rows(spb_session *s, int nt, bool want_logits, const 
     ra.T = m->tabs; ra.gain = m->gain; ra.pos_dev = s->pos_dev;
     ra.NH = m->NH; ra.NKV = m->NKV; ra.HD = m->HD; ra.P = s->pmax; ra.ntok = nt; ra.err = s->err_dev;
     ra.zero_slot = s->ao_max;
+    ra.rows_spin = rows_spin ? 1 : 0;
     if (!fuse_rope) K(launch_rope_kv(ra, st));
     AttnArgs aa{};
     aa.rows = rows; aa.layer = L;
     aa.qi = s->qi; aa.kv = s->kv; aa.NL = m->NL; aa.ao = s->ao; aa.pos_dev = s->pos_dev;
     aa.NH = m->NH; aa.NKV = m->NKV; aa.HD = m->HD; aa.P = rows ? Pmax : s->pmax; aa.win = d.win; aa.ntok = nt;
     aa.ascale = ascale; aa.err = s->err_dev; aa.ao_max = s->ao_max;
+    aa.rows_spin = rows_spin ? 1 : 0;
     if (fuse_rope) {
       aa.qkv = s->qkv; aa.q_norm = d.q_norm; aa.k_norm = d.k_norm;
       aa.W = ra.W; aa.T = m->tabs; aa.gain = m->gain;
@@ -996,8 +998,10 @@ extern "C" int spb_batch_decode_step(spb_session *const *ss, int B, const int32_
   spb_session *lead = ss[0];
   if (!lead) return set_err(SPB_EBADARG, "spb_batch_decode_step: null session");
   int Pmax = 0;
+  bool any_spin = false;
   for (int i = 0; i < B; i++) {
     spb_session *s = ss[i];
+    if (s && s->kv.rb) any_spin = true;
     if (!s || s->m != lead->m) return set_err(SPB_EBADARG, "spb_batch_decode_step: sessions must share one model");
     if (s->pos >= s->pmax) return set_err(SPB_ECONTEXT_FULL, "spb_batch_decode_step: session %d context full", i);
     for (int j = 0; j < i; j++)
@@ -1016,7 +1020,7 @@ extern "C" int spb_batch_decode_step(spb_session *const *ss, int B, const int32_
   }
   CU(cudaMemcpyAsync(lead->tok_dev, lead->h_pinned, (size_t)B * 4, cudaMemcpyHostToDevice, lead->st));
   CU(cudaMemcpyAsync(lead->rows_dev, lead->h_rows, (size_t)B * sizeof(BatchRow), cudaMemcpyHostToDevice, lead->st));
-  CU(enqueue_rows(lead, B, true, lead->rows_dev, Pmax));
+  CU(enqueue_rows(lead, B, true, lead->rows_dev, Pmax, any_spin));
   if (logits)
     CU(cudaMemcpyAsync(logits, lead->logits, (size_t)B * lead->m->Vfull * 4, cudaMemcpyDeviceToHost, lead->st));
   CU(cudaMemcpyAsync(lead->h_argmax, lead->argmax_dev, (size_t)B * 4, cudaMemcpyDeviceToHost, lead->st));
