@@ -185,9 +185,12 @@ __device__ __forceinline__ void convert_block(const uint4 cw, int32_t mult, uint
   }
 }
 
-template <int P, int NM, int EPI, bool SN>
+// APL: the weight planes come precomputed (DevQ4B::pl) by TMA (tma0 / tma1 over [P x rows][K]
+// bytes, the same 128-byte swizzle), and the converter warps only run the epilogue
+template <int P, int NM, int EPI, bool SN, bool APL = false>
 __global__ void __launch_bounds__(TC_THREADS, 1)
-k_gemm_tc(const __grid_constant__ CUtensorMap tmb, DevQ4B w, DevQ4B w2, DevAct act, int ntok, int ks, float *y,
+k_gemm_tc(const __grid_constant__ CUtensorMap tmb, const __grid_constant__ CUtensorMap tma0,
+          const __grid_constant__ CUtensorMap tma1, DevQ4B w, DevQ4B w2, DevAct act, int ntok, int ks, float *y,
           int ldy, uint32_t *err, uint32_t *ymax, unsigned long long *amax) {
   using SH = TcShape<P, NM, SN>;
   constexpr int N = SH::N, S = SH::S;
@@ -208,13 +211,17 @@ k_gemm_tc(const __grid_constant__ CUtensorMap tmb, DevQ4B w, DevQ4B w2, DevAct a
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; s++) {
-      mbar_init(&full_a[s], TC_CONV_WARPS);
+      mbar_init(&full_a[s], APL ? 1 : TC_CONV_WARPS);
       mbar_init(&full_b[s], 1);
       mbar_init(&empty[s], 1);
     }
     mbar_init(&tfull, 1);
     mbar_init_fence();
     asm volatile("prefetch.tensormap [%0];" ::"l"(&tmb) : "memory");
+    if (APL) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(&tma0) : "memory");
+      if (NM == 2) asm volatile("prefetch.tensormap [%0];" ::"l"(&tma1) : "memory");
+    }
   }
   if (warp == 1) {   // the whole warp allocates; the base column address lands in shared memory
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&tmem_base_sh)),
@@ -243,6 +250,14 @@ k_gemm_tc(const __grid_constant__ CUtensorMap tmb, DevQ4B w, DevQ4B w2, DevAct a
         uint8_t *B = tsm + s * SH::STAGE + SH::A_BYTES;
         mbar_arrive_expect_tx(&full_b[s], SH::B_BYTES);
         tma_load_2d(B, &tmb, kbase + kt * TC_BK, t0, &full_b[s]);
+        if (APL) {   // the stage's plane tiles: plane d of matrix m at rows d * rows + row0
+          uint8_t *A = tsm + s * SH::STAGE;
+          mbar_arrive_expect_tx(&full_a[s], SH::A_BYTES);
+#pragma unroll
+          for (int q = 0; q < SH::PM; q++)
+            tma_load_2d(A + q * TC_PLANE, q / P ? &tma1 : &tma0, kbase + kt * TC_BK, (q % P) * rows + row0,
+                        &full_a[s]);
+        }
       }
       __syncwarp();
     }
@@ -274,6 +289,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap tmb, DevQ4B w, DevQ4B w2, DevAct a
   } else {
     // ---- converters: thread ct takes row ct / 2 and the two 32-column blocks (ct & 1) * 2 + {0,1}
     const int ct = threadIdx.x - 64, row = ct >> 1, hb = ct & 1;
+    if (!APL) {
     const int grow = row0 + row;
     const bool valid = grow < rows;
     const size_t rb = (size_t)(valid ? grow : 0);
@@ -345,6 +361,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap tmb, DevQ4B w, DevQ4B w2, DevAct a
         if (lane == 0) mbar_arrive(&full_a[s]);
       }
     }
+    }   // !APL
 
     // ---- epilogue (all converter warps): warp w reads tensor-memory lanes 32 (w % 4) .. + 31 (its
     // weight rows) and every other 16-column chunk (eh = 0: warps 2-5, 1: warps 6-9)
@@ -433,6 +450,26 @@ k_gemm_tc(const __grid_constant__ CUtensorMap tmb, DevQ4B w, DevQ4B w2, DevAct a
   }
 }
 
+// One thread per (row, 32-column block): the block's P digit planes (convert_block, the
+// converters' arithmetic) stored row-major, block b at bytes 32 b .. 32 b + 31 of each plane row
+template <int P>
+__global__ void __launch_bounds__(256) k_q4b_planes(DevQ4B w, uint8_t *out) {
+  const int nblk = w.cols >> 5;
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (long long)w.rows * nblk) return;
+  const int row = (int)(i / nblk), b = (int)(i - (long long)row * nblk);
+  const uint4 cw = *reinterpret_cast<const uint4 *>(w.codes + (size_t)row * (w.cols >> 1) + (size_t)b * 16);
+  const uint32_t h = w.scales[(size_t)row * nblk + b];
+  uint32_t pl[P][8];
+  convert_block<P>(cw, block_mult(h, w.shift[row]), pl);
+#pragma unroll
+  for (int d = 0; d < P; d++) {
+    uint4 *dst = reinterpret_cast<uint4 *>(out + ((size_t)d * w.rows + row) * w.cols + (size_t)b * 32);
+    dst[0] = make_uint4(pl[d][0], pl[d][1], pl[d][2], pl[d][3]);
+    dst[1] = make_uint4(pl[d][4], pl[d][5], pl[d][6], pl[d][7]);
+  }
+}
+
 // ---- host side
 using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
                                    const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
@@ -460,11 +497,22 @@ bool tc_enabled() {
   return on != 0;
 }
 
-template <int P, int NM, int EPI, bool SN>
+// a 2-D TMA map over [P x rows][K] plane bytes: 128-byte boxes of 128 rows, 128-byte swizzle
+static bool plane_map(EncodeTiledFn enc, CUtensorMap *tm, const DevQ4B &w, int P) {
+  const cuuint64_t gdim[2] = {(cuuint64_t)w.cols, (cuuint64_t)P * (cuuint64_t)w.rows};
+  const cuuint64_t gstride[1] = {(cuuint64_t)w.cols};
+  const cuuint32_t box[2] = {(cuuint32_t)TC_BK, (cuuint32_t)TC_BM};
+  const cuuint32_t estr[2] = {1, 1};
+  return enc(tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, (void *)w.pl, gdim, gstride, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+         CUDA_SUCCESS;
+}
+
+template <int P, int NM, int EPI, bool SN, bool APL = false>
 cudaError_t tc_launch_sn(const DevQ4B &w, const DevQ4B &w2, const DevAct &act, int ntok, float *y, int ldy, uint32_t *err,
                       uint32_t *ymax, unsigned long long *amax, cudaStream_t st, int ks, bool pdl) {
   using SH = TcShape<P, NM, SN>;
-  auto kern = k_gemm_tc<P, NM, EPI, SN>;
+  auto kern = k_gemm_tc<P, NM, EPI, SN, APL>;
   static bool configured = false;
   if (!configured) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SH::SMEM);
@@ -482,6 +530,8 @@ cudaError_t tc_launch_sn(const DevQ4B &w, const DevQ4B &w2, const DevAct &act, i
           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) !=
       CUDA_SUCCESS)
     return cudaErrorInvalidValue;
+  CUtensorMap ta0 = tm, ta1 = tm;   // (unused without APL)
+  if (APL && (!plane_map(enc, &ta0, w, P) || (NM == 2 && !plane_map(enc, &ta1, w2, P)))) return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((ntok + SH::N - 1) / SH::N, (w.rows + TC_BM - 1) / TC_BM, ks);
   cfg.blockDim = dim3(TC_THREADS);
@@ -496,13 +546,16 @@ cudaError_t tc_launch_sn(const DevQ4B &w, const DevQ4B &w2, const DevAct &act, i
   }
   cfg.attrs = attr;
   cfg.numAttrs = na;
-  return cudaLaunchKernelEx(&cfg, kern, tm, w, w2, act, ntok, ks, y, ldy, err, ymax, amax);
+  return cudaLaunchKernelEx(&cfg, kern, tm, ta0, ta1, w, w2, act, ntok, ks, y, ldy, err, ymax, amax);
 }
 
 template <int P, int NM, int EPI>
 cudaError_t tc_launch(const DevQ4B &w, const DevQ4B &w2, const DevAct &act, int ntok, float *y, int ldy, uint32_t *err,
                       uint32_t *ymax, unsigned long long *amax, cudaStream_t st, int ks, bool pdl) {
   if (ntok <= 64) return tc_launch_sn<P, NM, EPI, true>(w, w2, act, ntok, y, ldy, err, ymax, amax, st, ks, pdl);
+  // precomputed planes (each matrix's own plane count equal to the launch's) for larger batches
+  if (w.pl && w.planes == P && (NM == 1 || (w2.pl && w2.planes == P)))
+    return tc_launch_sn<P, NM, EPI, false, true>(w, w2, act, ntok, y, ldy, err, ymax, amax, st, ks, pdl);
   return tc_launch_sn<P, NM, EPI, false>(w, w2, act, ntok, y, ldy, err, ymax, amax, st, ks, pdl);
 }
 
@@ -532,6 +585,19 @@ int gemm_tc_covers(const DevQ4B &w, const DevQ4B *w2, int epi, int ntok) {
     if (P > 3) return 0;   // two matrices of four planes do not fit the tensor memory with a useful N
   }
   return P;
+}
+
+cudaError_t launch_q4b_planes(const DevQ4B &w, uint8_t *pl, cudaStream_t st) {
+  if (!w.shift || w.planes < 2 || w.planes > 4 || (w.cols & 31) || w.rows <= 0 || ((uintptr_t)w.codes & 15))
+    return cudaErrorInvalidValue;
+  const long long n = (long long)w.rows * (w.cols >> 5);
+  const dim3 grid((unsigned)((n + 255) / 256));
+  switch (w.planes) {
+    case 2: k_q4b_planes<2><<<grid, 256, 0, st>>>(w, pl); break;
+    case 3: k_q4b_planes<3><<<grid, 256, 0, st>>>(w, pl); break;
+    default: k_q4b_planes<4><<<grid, 256, 0, st>>>(w, pl); break;
+  }
+  return cudaGetLastError();
 }
 
 cudaError_t launch_gemm_tc(const DevQ4B &w, const DevQ4B *w2, const DevAct &act, int ntok, float *y, int ldy, int epi,

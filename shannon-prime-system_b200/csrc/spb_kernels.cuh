@@ -31,7 +31,13 @@ struct DevQ4B {
   // 2^(s_block - shift[r]) of the matrix as a two's-complement integer; 0 = not described.
   const uint8_t *shift;
   int planes;
+  // optional (unless SPB_TC_PLANES=0): the `planes` digit planes precomputed once,
+  // [planes][rows][cols] bytes in the activation column order, for the token-batch GEMM's TMA
+  const uint8_t *pl;
 };
+
+// Fill w.pl (planes x rows x cols bytes) with the digit planes of w (described: shift, planes)
+cudaError_t launch_q4b_planes(const DevQ4B &w, uint8_t *pl, cudaStream_t st);
 
 // Per-row facts of an OK_Q4B matrix's block scales, one warp per row:
 //   shift[r]  as DevQ4B::shift (0 for a row without a nonzero block)

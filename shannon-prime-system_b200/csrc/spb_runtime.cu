@@ -184,6 +184,7 @@ struct spb_model {
   int Vfull = 0, vbase = 0;
   bool out_sep = false;   // the LM head has its own storage (untied, or a vocabulary slice)
   uint8_t *shifts = nullptr;   // every matrix's DevQ4B::shift rows (one allocation)
+  uint8_t *pbuf = nullptr;     // the layer matrices' precomputed digit planes (tc_planes_enabled)
 };
 
 static int describe_matrices(spb_model *m);
@@ -408,6 +409,19 @@ extern "C" int spb_model_upload_tp(const spb_model_desc *desc, spb_tp *tp, spb_m
   return SPB_OK;
 }
 
+// SPB_TC_PLANES=0: the token-batch GEMM converts OK_Q4B codes into digit planes inside every CTA
+// instead of loading planes precomputed once per matrix (comparisons; the same bytes). The
+// planes cost planes x rows x cols bytes (about 2 bytes per weight); without room for them the
+// converters stay.
+static bool tc_planes_enabled() {
+  static int on = -1;
+  if (on < 0) {
+    const char *e = getenv("SPB_TC_PLANES");
+    on = (e && e[0] == '0') ? 0 : 1;
+  }
+  return on != 0;
+}
+
 // Describe every matrix's block scales once (launch_q4b_rowinfo): the exact-range check, the
 // small-scale flag of the token-batch GEMM and the per-row shifts and digit planes of the
 // tensor-core GEMM. A matrix outside the exact int64 bound is refused with SPB_ERANGE.
@@ -442,6 +456,31 @@ static int describe_matrices(spb_model *m) {
     ws[i]->planes = q4b_planes_for_spread(info[4 * i + 2]);
   }
   if (!m->out_sep) m->out = m->embd;
+  // every layer matrix's digit planes precomputed once (planes x rows x cols bytes, ~2 bytes per
+  // weight at two planes) for the prefill GEMM's TMA; the embedding and LM head keep the
+  // converters (no prefill logits beyond the last chunk's 64 rows)
+  cudaFree(m->pbuf);
+  m->pbuf = nullptr;
+  if (tc_planes_enabled()) {
+    const size_t nlayer = ws.size() - (m->out_sep ? 2 : 1);
+    size_t bytes = 0;
+    for (size_t i = 0; i < nlayer; i++)
+      if (ws[i]->planes >= 2 && ws[i]->cols % 128 == 0)
+        bytes += ((size_t)ws[i]->planes * ws[i]->rows * ws[i]->cols + 255) & ~(size_t)255;
+    if (bytes && cudaMalloc(&m->pbuf, bytes) == cudaSuccess) {
+      size_t o = 0;
+      for (size_t i = 0; i < nlayer && e == cudaSuccess; i++) {
+        if (ws[i]->planes < 2 || ws[i]->cols % 128) continue;
+        ws[i]->pl = m->pbuf + o;
+        e = launch_q4b_planes(*ws[i], m->pbuf + o, 0);
+        o += ((size_t)ws[i]->planes * ws[i]->rows * ws[i]->cols + 255) & ~(size_t)255;
+      }
+      if (e == cudaSuccess) e = cudaDeviceSynchronize();
+      if (e != cudaSuccess) return set_err(SPB_ECUDA, "spb_model: digit planes: %s", cudaGetErrorString(e));
+    } else {
+      (void)cudaGetLastError();   // no room for the planes: the converters stay
+    }
+  }
   return SPB_OK;
 }
 
@@ -547,6 +586,7 @@ extern "C" void spb_model_free(spb_model *m) {
   cudaSetDevice(m->device);
   cudaFree(m->wbuf);
   cudaFree(m->shifts);
+  cudaFree(m->pbuf);
   delete m;
 }
 
@@ -1200,6 +1240,7 @@ struct spb_q4b_mat {
   int device;
   DevQ4B w;
   uint8_t *shift;   // device [rows]
+  uint8_t *pl = nullptr;   // the precomputed digit planes (tc_planes_enabled)
 };
 
 extern "C" int spb_q4b_prepare(const uint8_t *codes, const uint16_t *bscale, int rows, int cols, void *stream,
@@ -1234,6 +1275,21 @@ extern "C" int spb_q4b_prepare(const uint8_t *codes, const uint16_t *bscale, int
   m->device = dev;
   m->shift = buf;
   m->w = DevQ4B{codes, bscale, rows, cols, h[1] <= 21 ? 1 : 0, buf, q4b_planes_for_spread(h[2])};
+  if (tc_planes_enabled() && m->w.planes >= 2 && cols % 128 == 0) {
+    const size_t pb = (size_t)m->w.planes * rows * cols;
+    if (cudaMalloc(&m->pl, pb) == cudaSuccess) {
+      m->w.pl = m->pl;
+      e = launch_q4b_planes(m->w, m->pl, st);
+      if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+      if (e != cudaSuccess) {
+        spb_q4b_release(m);
+        return set_err(SPB_ECUDA, "spb_q4b_prepare: digit planes: %s", cudaGetErrorString(e));
+      }
+    } else {
+      (void)cudaGetLastError();   // no room: the GEMM converts the codes itself
+      m->pl = nullptr;
+    }
+  }
   *out = m;
   return SPB_OK;
 }
@@ -1241,6 +1297,7 @@ extern "C" int spb_q4b_prepare(const uint8_t *codes, const uint16_t *bscale, int
 extern "C" void spb_q4b_release(spb_q4b_mat *m) {
   if (!m) return;
   cudaFree(m->shift);
+  cudaFree(m->pl);
   delete m;
 }
 
