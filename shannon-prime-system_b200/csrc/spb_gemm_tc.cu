@@ -45,19 +45,22 @@ constexpr int TC_THREADS = 32 * (2 + TC_CONV_WARPS);
 constexpr int TC_PLANE = TC_BM * TC_BK;   // bytes of one plane tile
 constexpr int TC_SMEM_BUDGET = 225 * 1024;
 
-// SN: the 64-token tile for batches of at most 64 rows (the multi-session decode step), where the
-// larger tiles would mostly multiply zero rows
-template <int P, int NM, bool SN = false>
+// SN 1: the 64-token tile for batches of at most 64 rows (the multi-session decode step), where
+// the larger tiles would mostly multiply zero rows; SN 2 (two planes of one matrix): a 128-token
+// tile with two stages, so that two CTAs share an SM (256 tensor-memory columns and ~97 KB of
+// shared memory each) and one CTA's epilogue overlaps the other's main loop
+template <int P, int NM, int SN = 0>
 struct TcShape {
   static constexpr int PM = P * NM;
-  static constexpr int N = SN ? 64 : PM == 2 ? 256 : PM == 3 ? 160 : PM == 4 ? 128 : 80;   // token rows per CTA
+  static constexpr int N = SN == 1 ? 64 : SN == 2 ? 128 : PM == 2 ? 256 : PM == 3 ? 160 : PM == 4 ? 128 : 80;
   static constexpr int COLS = PM * N;                                             // tensor-memory columns used
   static constexpr int TMEM_COLS = COLS <= 256 ? 256 : 512;
   static constexpr int A_BYTES = PM * TC_PLANE;
   static constexpr int B_BYTES = N * TC_BK;
   static constexpr int STAGE = A_BYTES + B_BYTES;
   static constexpr int S0 = (TC_SMEM_BUDGET - 1024) / STAGE;
-  static constexpr int S = S0 > 4 ? 4 : S0;
+  static constexpr int S = SN == 2 ? 2 : S0 > 4 ? 4 : S0;
+  static constexpr int CTAS_PER_SM = SN == 2 ? 2 : 1;
   static constexpr int SMEM = S * STAGE + 1024;   // + alignment slack (stages start 1024-aligned)
   static_assert(COLS <= 512, "tensor memory holds 512 columns");
   static_assert(S >= 2, "at least two stages");
@@ -187,8 +190,8 @@ __device__ __forceinline__ void convert_block(const uint4 cw, int32_t mult, uint
 
 // APL: the weight planes come precomputed (DevQ4B::pl) by TMA (tma0 / tma1 over [P x rows][K]
 // bytes, the same 128-byte swizzle), and the converter warps only run the epilogue
-template <int P, int NM, int EPI, bool SN, bool APL = false>
-__global__ void __launch_bounds__(TC_THREADS, 1)
+template <int P, int NM, int EPI, int SN, bool APL = false>
+__global__ void __launch_bounds__(TC_THREADS, TcShape<P, NM, SN>::CTAS_PER_SM)
 k_gemm_tc(const __grid_constant__ CUtensorMap tmb, const __grid_constant__ CUtensorMap tma0,
           const __grid_constant__ CUtensorMap tma1, DevQ4B w, DevQ4B w2, DevAct act, int ntok, int ks, float *y,
           int ldy, uint32_t *err, uint32_t *ymax, unsigned long long *amax) {
@@ -508,7 +511,7 @@ static bool plane_map(EncodeTiledFn enc, CUtensorMap *tm, const DevQ4B &w, int P
          CUDA_SUCCESS;
 }
 
-template <int P, int NM, int EPI, bool SN, bool APL = false>
+template <int P, int NM, int EPI, int SN, bool APL = false>
 cudaError_t tc_launch_sn(const DevQ4B &w, const DevQ4B &w2, const DevAct &act, int ntok, float *y, int ldy, uint32_t *err,
                       uint32_t *ymax, unsigned long long *amax, cudaStream_t st, int ks, bool pdl) {
   using SH = TcShape<P, NM, SN>;
@@ -552,11 +555,23 @@ cudaError_t tc_launch_sn(const DevQ4B &w, const DevQ4B &w2, const DevAct &act, i
 template <int P, int NM, int EPI>
 cudaError_t tc_launch(const DevQ4B &w, const DevQ4B &w2, const DevAct &act, int ntok, float *y, int ldy, uint32_t *err,
                       uint32_t *ymax, unsigned long long *amax, cudaStream_t st, int ks, bool pdl) {
-  if (ntok <= 64) return tc_launch_sn<P, NM, EPI, true>(w, w2, act, ntok, y, ldy, err, ymax, amax, st, ks, pdl);
+  if (ntok <= 64) return tc_launch_sn<P, NM, EPI, 1>(w, w2, act, ntok, y, ldy, err, ymax, amax, st, ks, pdl);
   // precomputed planes (each matrix's own plane count equal to the launch's) for larger batches
-  if (w.pl && w.planes == P && (NM == 1 || (w2.pl && w2.planes == P)))
-    return tc_launch_sn<P, NM, EPI, false, true>(w, w2, act, ntok, y, ldy, err, ymax, amax, st, ks, pdl);
-  return tc_launch_sn<P, NM, EPI, false>(w, w2, act, ntok, y, ldy, err, ymax, amax, st, ks, pdl);
+  if (w.pl && w.planes == P && (NM == 1 || (w2.pl && w2.planes == P))) {
+    // two planes of one matrix: the two-CTA 128-token tile (SPB_TC_N128=0: the 256-token tile;
+    // measured at M = 2048: 3840 x 3840 144.5 -> 132.3 us, 15360 x 3840 357.8 -> 314.4 us,
+    // 3840 x 15360 unchanged)
+    static int n128 = -1;
+    if (n128 < 0) {
+      const char *e = getenv("SPB_TC_N128");
+      n128 = (e && e[0] == '0') ? 0 : 1;
+    }
+    if (P * NM == 2 && n128)
+      return tc_launch_sn<P, NM, EPI, (P * NM == 2 ? 2 : 0), true>(w, w2, act, ntok, y, ldy, err, ymax, amax, st, ks,
+                                                                    pdl);
+    return tc_launch_sn<P, NM, EPI, 0, true>(w, w2, act, ntok, y, ldy, err, ymax, amax, st, ks, pdl);
+  }
+  return tc_launch_sn<P, NM, EPI, 0>(w, w2, act, ntok, y, ldy, err, ymax, amax, st, ks, pdl);
 }
 
 template <int EPI>
