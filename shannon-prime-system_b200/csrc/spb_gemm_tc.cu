@@ -555,9 +555,20 @@ cudaError_t tc_launch_sn(const DevQ4B &w, const DevQ4B &w2, const DevAct &act, i
 template <int P, int NM, int EPI>
 cudaError_t tc_launch(const DevQ4B &w, const DevQ4B &w2, const DevAct &act, int ntok, float *y, int ldy, uint32_t *err,
                       uint32_t *ymax, unsigned long long *amax, cudaStream_t st, int ks, bool pdl) {
-  if (ntok <= 64) return tc_launch_sn<P, NM, EPI, 1>(w, w2, act, ntok, y, ldy, err, ymax, amax, st, ks, pdl);
+  const bool apl = w.pl && w.planes == P && (NM == 1 || (w2.pl && w2.planes == P));
+  if (ntok <= 64) {
+    // the 64-token tile loads the precomputed planes too (measured on the 12B batch-64 decode
+    // step: 3723 -> 3968 tok/s); SPB_TC_PLANES_SMALL=0 keeps its converter warps
+    static int small = -1;
+    if (small < 0) {
+      const char *e = getenv("SPB_TC_PLANES_SMALL");
+      small = (e && e[0] == '0') ? 0 : 1;
+    }
+    if (apl && small) return tc_launch_sn<P, NM, EPI, 1, true>(w, w2, act, ntok, y, ldy, err, ymax, amax, st, ks, pdl);
+    return tc_launch_sn<P, NM, EPI, 1>(w, w2, act, ntok, y, ldy, err, ymax, amax, st, ks, pdl);
+  }
   // precomputed planes (each matrix's own plane count equal to the launch's) for larger batches
-  if (w.pl && w.planes == P && (NM == 1 || (w2.pl && w2.planes == P))) {
+  if (apl) {
     // two planes of one matrix: the two-CTA 128-token tile (SPB_TC_N128=0: the 256-token tile;
     // measured at M = 2048: 3840 x 3840 144.5 -> 132.3 us, 15360 x 3840 357.8 -> 314.4 us,
     // 3840 x 15360 unchanged)

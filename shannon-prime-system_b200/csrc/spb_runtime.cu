@@ -185,6 +185,11 @@ struct spb_model {
   bool out_sep = false;   // the LM head has its own storage (untied, or a vocabulary slice)
   uint8_t *shifts = nullptr;   // every matrix's DevQ4B::shift rows (one allocation)
   uint8_t *pbuf = nullptr;     // the layer matrices' precomputed digit planes (tc_planes_enabled)
+  // closed sessions' device buffers, streams and pinned staging, handed to the next open that
+  // fits (a clone-and-close loop then neither allocates nor synchronises the device)
+  struct Spare { uint8_t *buf; size_t bytes; cudaStream_t st; void *h_pinned, *h_rows, *h_argmax; };
+  std::mutex spare_mu;
+  std::vector<Spare> spares;
 };
 
 static int describe_matrices(spb_model *m);
@@ -581,9 +586,28 @@ extern "C" int spb_model_synthetic_tp(const spb_config *cfg, uint64_t seed, spb_
   return SPB_OK;
 }
 
+static void spare_destroy(const spb_model::Spare &p) {
+  if (p.st) cudaStreamDestroy(p.st);
+  cudaFreeHost(p.h_pinned);
+  cudaFreeHost(p.h_rows);
+  cudaFreeHost(p.h_argmax);
+  cudaFree(p.buf);
+}
+
+// free every kept session buffer (model teardown, or an open that found no device memory)
+static void spares_drop(spb_model *m) {
+  std::vector<spb_model::Spare> v;
+  {
+    std::lock_guard<std::mutex> lk(m->spare_mu);
+    v.swap(m->spares);
+  }
+  for (const auto &p : v) spare_destroy(p);
+}
+
 extern "C" void spb_model_free(spb_model *m) {
   if (!m) return;
   cudaSetDevice(m->device);
+  spares_drop(m);
   cudaFree(m->wbuf);
   cudaFree(m->shifts);
   cudaFree(m->pbuf);
@@ -608,6 +632,18 @@ struct spb_kvpool {
 };
 
 constexpr int NT_MAX = 256;   // token rows per schedule pass (a prefill chunk without logits)
+constexpr size_t SPARE_MAX_BYTES = (size_t)1 << 30;   // largest closed-session buffer kept for reuse
+constexpr size_t SPARE_MAX = 16;                      // closed-session buffers kept per model
+
+// SPB_SESSION_REUSE=0: every open allocates and every close frees (comparisons)
+static bool session_reuse_enabled() {
+  static int on = -1;
+  if (on < 0) {
+    const char *e = getenv("SPB_SESSION_REUSE");
+    on = (e && e[0] == '0') ? 0 : 1;
+  }
+  return on != 0;
+}
 constexpr int LG_MAX = 64;    // token rows of a pass that produces logits (and of a decode batch)
 
 struct spb_session {
@@ -632,6 +668,7 @@ struct spb_session {
   BatchRow *h_rows = nullptr;     // pinned staging for rows_dev
   int32_t *h_argmax = nullptr;    // pinned [NT_MAX] batch argmaxes
   cudaGraphExec_t step_graph = nullptr;
+  size_t buf_bytes = 0;
   // tensor parallel: int64 partial sums of the K-split matrices [NT_MAX][E], this rank's LM-head
   // logits [LG_MAX][V] and the all-gathered slices [world][LG_MAX][V]
   int64_t *y64 = nullptr;
@@ -683,8 +720,37 @@ static int session_open(spb_model *m, int pmax, spb_kvpool *pool, spb_session **
   const size_t o_hist = take((size_t)pmax * 4), o_err = take(4), o_slots = take(2 * NT_MAX * 4);
   const size_t o_keys = take(NT_MAX * 8);
   const size_t o_rows = take(NT_MAX * sizeof(BatchRow));
-  cudaError_t e = cudaMalloc(&s->buf, off);
-  if (e != cudaSuccess) { delete s; return set_err(SPB_EOOM, "spb_session_open: cudaMalloc(%zu): %s", off, cudaGetErrorString(e)); }
+  cudaError_t e = cudaSuccess;
+  if (session_reuse_enabled()) {
+    // the most recently closed buffer of exactly this size, else the smallest within 25 % above it
+    std::lock_guard<std::mutex> lk(m->spare_mu);
+    int pick = -1;
+    for (int i = (int)m->spares.size() - 1; i >= 0; i--) {
+      const size_t b = m->spares[i].bytes;
+      if (b == off) { pick = i; break; }
+      if (b > off && b - off <= off / 4 && (pick < 0 || b < m->spares[pick].bytes)) pick = i;
+    }
+    if (pick >= 0) {
+      const spb_model::Spare p = m->spares[pick];
+      s->buf = p.buf; s->buf_bytes = p.bytes; s->st = p.st;
+      s->h_pinned = (int32_t *)p.h_pinned; s->h_rows = (BatchRow *)p.h_rows; s->h_argmax = (int32_t *)p.h_argmax;
+      m->spares.erase(m->spares.begin() + pick);
+    }
+  }
+  if (!s->buf) {
+    e = cudaMalloc(&s->buf, off);
+    if (e == cudaErrorMemoryAllocation) {
+      cudaGetLastError();
+      spares_drop(m);
+      e = cudaMalloc(&s->buf, off);
+    }
+    if (e != cudaSuccess) {
+      s->buf = nullptr;
+      delete s;
+      return set_err(SPB_EOOM, "spb_session_open: cudaMalloc(%zu): %s", off, cudaGetErrorString(e));
+    }
+    s->buf_bytes = off;
+  }
   uint8_t *B = s->buf;
   if (pool) {
     s->ptab_dev = (int32_t *)(B + o_ptab);
@@ -709,10 +775,10 @@ static int session_open(spb_model *m, int pmax, spb_kvpool *pool, spb_session **
     s->logits_l = (float *)(B + o_lgl);
     s->logits_g = (float *)(B + o_lgg);
   }
-  e = cudaStreamCreateWithFlags(&s->st, cudaStreamNonBlocking);
-  if (e == cudaSuccess) e = cudaMallocHost(&s->h_pinned, (NT_MAX + 4) * 4);
-  if (e == cudaSuccess) e = cudaMallocHost(&s->h_rows, NT_MAX * sizeof(BatchRow));
-  if (e == cudaSuccess) e = cudaMallocHost(&s->h_argmax, NT_MAX * 4);
+  if (!s->st) e = cudaStreamCreateWithFlags(&s->st, cudaStreamNonBlocking);
+  if (e == cudaSuccess && !s->h_pinned) e = cudaMallocHost(&s->h_pinned, (NT_MAX + 4) * 4);
+  if (e == cudaSuccess && !s->h_rows) e = cudaMallocHost(&s->h_rows, NT_MAX * sizeof(BatchRow));
+  if (e == cudaSuccess && !s->h_argmax) e = cudaMallocHost(&s->h_argmax, NT_MAX * 4);
   if (e == cudaSuccess) e = cudaMemsetAsync(s->buf, 0, off, s->st);
   if (e == cudaSuccess) e = cudaStreamSynchronize(s->st);
   if (e != cudaSuccess) { spb_session_close(s); return set_err(SPB_ECUDA, "spb_session_open: %s", cudaGetErrorString(e)); }
@@ -821,12 +887,26 @@ extern "C" void spb_session_close(spb_session *s) {
   if (s->st) cudaStreamSynchronize(s->st);
   release_pages(s);
   if (s->step_graph) cudaGraphExecDestroy(s->step_graph);
-  if (s->st) cudaStreamDestroy(s->st);
-  cudaFreeHost(s->h_pinned);
-  cudaFreeHost(s->h_rows);
-  cudaFreeHost(s->h_argmax);
-  cudaFree(s->buf);
+  const spb_model::Spare p{s->buf, s->buf_bytes, s->st, s->h_pinned, s->h_rows, s->h_argmax};
+  spb_model *m = s->m;
   delete s;
+  // kept for the next open: buffers of at most SPARE_MAX_BYTES (scratch and paged sessions, not
+  // large private caches), only after a clean stream; the oldest of SPARE_MAX makes room
+  if (p.buf && p.st && p.h_pinned && p.h_rows && p.h_argmax && p.bytes <= SPARE_MAX_BYTES && session_reuse_enabled() &&
+      cudaStreamQuery(p.st) == cudaSuccess) {
+    spb_model::Spare old{};
+    {
+      std::lock_guard<std::mutex> lk(m->spare_mu);
+      if (m->spares.size() >= SPARE_MAX) {
+        old = m->spares.front();
+        m->spares.erase(m->spares.begin());
+      }
+      m->spares.push_back(p);
+    }
+    if (old.buf) spare_destroy(old);
+    return;
+  }
+  spare_destroy(p);
 }
 
 extern "C" void *spb_session_stream(spb_session *s) { return s ? (void *)s->st : nullptr; }

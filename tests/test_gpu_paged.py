@@ -211,3 +211,33 @@ def test_batch_mixes_paged_and_unpaged(xr, cuda_ok, env):
         toks = [int(a) for a in am]
     for h in sess + xss:
         h.close()
+
+
+def test_reopened_session_starts_clean(xr, cuda_ok, env):
+    """A closed session's device buffer, stream and pinned staging go to the next open of the same
+    shape (the clone-and-close loop then allocates nothing): the new session starts from an empty
+    state, whatever the old one held, and its results equal XREF's, paged and unpaged."""
+    cfg, T, m, pool = env
+    d = xref.build_desc(cfg, T)
+    for paged in (True, False):
+        def open_():
+            return pool.session(300) if paged else m.session(300)
+        old = open_()
+        old.prefill(spmodel.gen_tokens(70, 200, cfg.n_vocab), logits=False)
+        old.greedy(5, 16)
+        st = old.stream()
+        old.close()
+        s = open_()
+        assert s.stream() == st, "closed session's stream not reused"
+        xs = xr.session(d, 300)
+        toks = spmodel.gen_tokens(71, 37, cfg.n_vocab)
+        assert np.array_equal(u32(s.prefill(toks)), u32(xs.prefill(toks)))
+        tok = int(toks[-1])
+        for i in range(6):
+            la, ta = s.step_argmax(tok)
+            assert np.array_equal(u32(la), u32(xs.step(tok))), (paged, i)
+            tok = ta
+        for p in (0, 36, 42):
+            assert np.array_equal(s.kv(1, p, 0), xs.kv(1, p, 0)), (paged, p)
+        s.close()
+        xs.close()
