@@ -26,7 +26,7 @@
 
 static unsigned g_kv_flags = 0;   /* spb_session_open_ex flags of section-6b caches */
 static pthread_mutex_t g_mu = PTHREAD_MUTEX_INITIALIZER;
-static struct { const void *qm; spb_model *m; spb_kvpool *pool; } g_models[SPB_L1_MAX_MODELS];
+static struct { const void *qm; uint64_t fp; spb_model *m; spb_kvpool *pool; } g_models[SPB_L1_MAX_MODELS];
 static int g_device = 0;
 static int g_pool_pg = 0, g_pool_pages = 0;   /* spb_l1_set_kv_pool: 0 = unpaged caches */
 static int g_backend_tag;
@@ -105,20 +105,58 @@ static spb_model *upload(const qwen3_model *qm) {
     return m;
 }
 
+static uint64_t fnv1a(uint64_t h, const void *p, size_t n) {
+    const unsigned char *b = (const unsigned char *)p;
+    for (size_t i = 0; i < n; i++) { h ^= b[i]; h *= 1099511628211ull; }
+    return h;
+}
+
+/* The identity of a borrowed model beyond its address (a model unloaded without
+ * spb_l1_release_model and another loaded at the same address must not find the first one's
+ * device copy): FNV-1a over the config, the arena pointer, and the pointers and first bytes of
+ * the embedding's and the first layer's Q codes and block scales. */
+static uint64_t fingerprint(const qwen3_model *qm) {
+    uint64_t h = 14695981039346656037ull;
+    h = fnv1a(h, &qm->cfg, sizeof qm->cfg);
+    h = fnv1a(h, &qm->arena, sizeof qm->arena);
+    const gguf_tensor *ts[2] = {qm->token_embd, qm->cfg.n_layers > 0 ? qm->layers[0].attn_q : NULL};
+    for (int i = 0; i < 2; i++) {
+        spb_q4b t;
+        memset(&t, 0, sizeof t);
+        if (!ts[i] || !q4b_of(qm, ts[i], &t) || t.rows <= 0) continue;
+        const size_t row = (size_t)(t.cols + 1) / 2, nblk = (size_t)(t.cols + 31) / 32;
+        h = fnv1a(h, &t.codes, sizeof t.codes);
+        h = fnv1a(h, &t.bscale, sizeof t.bscale);
+        h = fnv1a(h, t.codes, row < 64 ? row : 64);
+        h = fnv1a(h, t.bscale, (nblk < 16 ? nblk : 16) * 2);
+    }
+    return h;
+}
+
 static spb_model *model_for(const void *qm_opaque, spb_kvpool **pool) {
     if (!qm_opaque) { sp_set_error("spb200: null model"); return NULL; }
     spb_model *m = NULL;
     if (pool) *pool = NULL;
+    const uint64_t fp = fingerprint((const qwen3_model *)qm_opaque);
     pthread_mutex_lock(&g_mu);
     int slot = -1;
     for (int i = 0; i < SPB_L1_MAX_MODELS; i++)
-        if (g_models[i].qm == qm_opaque) { m = g_models[i].m; slot = i; break; }
+        if (g_models[i].qm == qm_opaque) {
+            if (g_models[i].fp == fp) { m = g_models[i].m; slot = i; break; }
+            /* another model now lives at this address: drop the stale device copy */
+            spb_kvpool_free(g_models[i].pool);
+            spb_model_free(g_models[i].m);
+            g_models[i].qm = NULL;
+            g_models[i].m = NULL;
+            g_models[i].pool = NULL;
+        }
     if (!m) {
         for (int i = 0; i < SPB_L1_MAX_MODELS; i++)
             if (!g_models[i].qm) { slot = i; break; }
         if (slot < 0) sp_set_error("spb200: too many resident models");
         else if ((m = upload((const qwen3_model *)qm_opaque)) != NULL) {
             g_models[slot].qm = qm_opaque;
+            g_models[slot].fp = fp;
             g_models[slot].m = m;
             g_models[slot].pool = NULL;
             if (g_pool_pg > 0 && spb_kvpool_create(m, g_pool_pg, g_pool_pages, &g_models[slot].pool) != SPB_OK) {

@@ -27,6 +27,10 @@ def setup(request, reflib, xr, tmp_path_factory):
     model = reflib.load(mp, tp)
     l1 = spb200.load_l1()
     yield cfg, T, model, l1
+    s = reflib.session(model, 16)   # the borrowed qwen3_model the hooks were handed
+    qm = reflib.lib.sp_session_qwen3_model(s)
+    reflib.lib.sp_session_destroy(s)
+    l1.spb_l1_release_model(qm)
     reflib.lib.sp_model_unload(model)
 
 
