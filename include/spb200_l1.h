@@ -78,7 +78,10 @@ int spb_l1_set_kv_flags(unsigned flags);
 /* Device used for models uploaded after this call (default 0). */
 int spb_l1_set_device(int device);
 
-/* Drop the cached device copy of one model (call before sp_model_unload). */
+/* Drop the cached device copy of one model (call before sp_model_unload). The cache is keyed by
+ * the model's address and a fingerprint of its config, arena and first weight bytes, so a model
+ * loaded later at the address of one that was never released is uploaded afresh; releasing
+ * still frees the old copy's device memory at once. */
 void spb_l1_release_model(const void *qm_opaque);
 
 #ifdef __cplusplus
