@@ -1,6 +1,6 @@
 """Generate the golden vectors under tests/golden/ by running the reference's own
 compiled code (oracle/_ref/libspref.so, built from the reference sources by
-`make -C oracle ref`). Re-run: python tests/golden/make_golden.py
+`make -C oracle ref`). Re-run: python tests/golden/make_golden.py [spinor | fidelity]
 
 Every vector is (seeded input, reference output). The CPU test-suite checks the XREF
 restatement against them, so XREF stays pinned where the reference tree is absent.
@@ -125,8 +125,46 @@ def spinor():
     print("wrote", len(out), "arrays")
 
 
+# (case, base config, overrides, prompt tokens): the width the bench runs at, cut to a few layers and
+# a 4096-token vocabulary so the reference float forward finishes in seconds; gemma12b keeps six
+# layers so its global layer (L % 6 == 5, sp_session.c:396) is among them
+FIDELITY_CASES = [
+    ("tiny", "tiny", {}, 32),
+    ("gemma12b_w6", "gemma12b", {"n_layers": 6, "n_vocab": 4096, "max_context": 64}, 8),
+    ("qwen8b_w4", "qwen8b", {"n_layers": 4, "n_vocab": 4096, "max_context": 64}, 8),
+]
+
+
+def fidelity():
+    """The reference float forward (sp_prefill_chunk with no backend) at BASELINE configs[0] and
+    at the 12B and 8B widths: the last prompt row's logits, for XREF's fidelity test."""
+    import dataclasses
+    C.CDLL(xref.SPREF_SO, mode=C.RTLD_GLOBAL)
+    R = xref.RefLib()
+    out = {}
+    for name, base, kw, n in FIDELITY_CASES:
+        cfg = dataclasses.replace(spmodel.CONFIGS[base], **kw)
+        T = spmodel.gen_model(cfg, seed=0)
+        mp, tp = f"/tmp/fidelity_{name}.sp-model", f"/tmp/fidelity_{name}.sp-tokenizer"
+        spmodel.write_sp_model(mp, tp, cfg, T)
+        m = R.load(mp, tp)
+        sess = R.session(m, cfg.max_context)
+        toks = spmodel.gen_tokens(12, n, cfg.n_vocab)
+        rc, lg = R.prefill(sess, toks, cfg.n_vocab)
+        assert rc == 0, R.err()
+        out[f"{name}_tokens"], out[f"{name}_logits"] = toks, lg
+        R.lib.sp_session_destroy(sess)
+        R.lib.sp_model_unload(m)
+        os.remove(mp)
+        os.remove(tp)
+    np.savez_compressed(os.path.join(HERE, "fidelity_vectors.npz"), **out)
+    print("wrote", len(out), "arrays")
+
+
 if __name__ == "__main__":
     if sys.argv[1:] == ["spinor"]:
         spinor()
+    elif sys.argv[1:] == ["fidelity"]:
+        fidelity()
     else:
         main()
