@@ -78,6 +78,10 @@ def parse():
     p.add_argument("--spin-batch-steps", type=int, default=8)
     p.add_argument("--no-tp", action="store_true", help="N>1: skip the tensor-parallel objects")
     p.add_argument("--tp", action="store_true", help="(default with N>1) the tensor-parallel objects")
+    p.add_argument("--probe-gemm", default="",
+                   help="ROWS,COLS,M: time only spb_q4b_matmul of one prepared seeded matrix at M token "
+                        "rows (a small case for ncu captures of the token-batch GEMM) and exit")
+    p.add_argument("--probe-iters", type=int, default=5)
     return p.parse_args()
 
 
@@ -822,6 +826,45 @@ def run_spb(args):
         print(json.dumps(line), flush=True)
 
 
+def run_probe(args):
+    """--probe-gemm ROWS,COLS,M: one seeded rows x cols OK_Q4B matrix prepared once
+    (spb_q4b_prepare: its digit planes precomputed), spb_q4b_matmul of M seeded token rows run
+    twice untimed, then --probe-iters times between CUDA events; prints one JSON line. Not a bench
+    line: it exists so a profiler can capture a few launches of one GEMM shape."""
+    import ctypes as C
+    import torch
+    import spb200
+    rows, cols, M = (int(v) for v in args.probe_gemm.split(","))
+    spb = spb200.load()
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(args.seed)
+    codes = torch.randint(0, 256, (rows * cols // 2,), dtype=torch.uint8, device=dev, generator=g)
+    scl = torch.randint(0, 1024, (rows * (cols // 32),), dtype=torch.int16, device=dev, generator=g) | (5 << 10)
+    x = torch.randn(M, cols, device=dev, generator=g)
+    y = torch.empty(M, rows, device=dev)
+    st = torch.cuda.current_stream()
+    P = lambda t: C.c_void_p(t.data_ptr())
+    h = C.c_void_p()
+    assert spb.spb_q4b_prepare(P(codes), P(scl), rows, cols, C.c_void_p(st.cuda_stream), C.byref(h)) == 0, \
+        spb.spb_last_error()
+
+    def go():
+        assert spb.spb_q4b_matmul(h, P(x), M, P(y), C.c_void_p(st.cuda_stream)) == 0, spb.spb_last_error()
+    for _ in range(2):
+        go()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(args.probe_iters):
+        go()
+    e1.record(st)
+    e1.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / args.probe_iters
+    spb.spb_q4b_release(h)
+    print(json.dumps({"probe": "spb_q4b_matmul", "rows": rows, "cols": cols, "m": M, "iters": args.probe_iters,
+                      "us": round(us, 2), "tops": round(2 * M * rows * cols / us / 1e6, 2)}), flush=True)
+
+
 def run_reference(args):
     """The reference arm: the reference's own CPU decode (oracle/_ref/libspref.so, compiled from
     the reference sources) on all host cores. Each of the K timed steps is one decode token of
@@ -864,7 +907,9 @@ def run_reference(args):
 
 if __name__ == "__main__":
     a = parse()
-    if a.impl == "reference":
+    if a.probe_gemm:
+        run_probe(a)
+    elif a.impl == "reference":
         run_reference(a)
     else:
         run_spb(a)
