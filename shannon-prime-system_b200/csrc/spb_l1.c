@@ -38,11 +38,15 @@ static int fail(const char *what) {
     return 1;
 }
 
-static int q4b_of(const qwen3_model *qm, const gguf_tensor *t, spb_q4b *out) {
-    if (!t || !qm->arena) return 0;
+static const sp_frob_packed_tensor *packed_of(const qwen3_model *qm, const gguf_tensor *t) {
+    if (!t || !qm->arena) return NULL;
     const sp_arena_tensor *at = sp_arena_find(qm->arena, t->name);
-    if (!at) return 0;
-    const sp_frob_packed_tensor *pt = &at->pt;
+    return at ? &at->pt : NULL;
+}
+
+static int q4b_of(const qwen3_model *qm, const gguf_tensor *t, spb_q4b *out) {
+    const sp_frob_packed_tensor *pt = packed_of(qm, t);
+    if (!pt) return 0;
     if (!pt->bscale || !pt->codes || pt->bs_nblk != (pt->cols + 31) / 32) return 0;
     const size_t nib = (size_t)(pt->cols + 1) / 2;
     for (int r = 0; r < pt->rows; r++)
@@ -121,14 +125,13 @@ static uint64_t fingerprint(const qwen3_model *qm) {
     h = fnv1a(h, &qm->arena, sizeof qm->arena);
     const gguf_tensor *ts[2] = {qm->token_embd, qm->cfg.n_layers > 0 ? qm->layers[0].attn_q : NULL};
     for (int i = 0; i < 2; i++) {
-        spb_q4b t;
-        memset(&t, 0, sizeof t);
-        if (!ts[i] || !q4b_of(qm, ts[i], &t) || t.rows <= 0) continue;
-        const size_t row = (size_t)(t.cols + 1) / 2, nblk = (size_t)(t.cols + 31) / 32;
-        h = fnv1a(h, &t.codes, sizeof t.codes);
-        h = fnv1a(h, &t.bscale, sizeof t.bscale);
-        h = fnv1a(h, t.codes, row < 64 ? row : 64);
-        h = fnv1a(h, t.bscale, (nblk < 16 ? nblk : 16) * 2);
+        const sp_frob_packed_tensor *pt = packed_of(qm, ts[i]);   /* (no per-row walk: pointers and bytes) */
+        if (!pt || !pt->codes || !pt->bscale || pt->rows <= 0 || pt->cols <= 0) continue;
+        const size_t row = (size_t)(pt->cols + 1) / 2, nblk = (size_t)(pt->cols + 31) / 32;
+        h = fnv1a(h, &pt->codes, sizeof pt->codes);
+        h = fnv1a(h, &pt->bscale, sizeof pt->bscale);
+        h = fnv1a(h, pt->codes, row < 64 ? row : 64);
+        h = fnv1a(h, pt->bscale, (nblk < 16 ? nblk : 16) * 2);
     }
     return h;
 }
