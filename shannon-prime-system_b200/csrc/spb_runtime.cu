@@ -634,6 +634,7 @@ struct spb_kvpool {
 constexpr int NT_MAX = 256;   // token rows per schedule pass (a prefill chunk without logits)
 constexpr size_t SPARE_MAX_BYTES = (size_t)1 << 30;   // largest closed-session buffer kept for reuse
 constexpr size_t SPARE_MAX = 16;                      // closed-session buffers kept per model
+constexpr size_t SPARE_TOTAL_BYTES = (size_t)4 << 30; // and their bytes at most, per model
 
 // SPB_SESSION_REUSE=0: every open allocates and every close frees (comparisons)
 static bool session_reuse_enabled() {
@@ -891,19 +892,23 @@ extern "C" void spb_session_close(spb_session *s) {
   spb_model *m = s->m;
   delete s;
   // kept for the next open: buffers of at most SPARE_MAX_BYTES (scratch and paged sessions, not
-  // large private caches), only after a clean stream; the oldest of SPARE_MAX makes room
+  // large private caches), only after a clean stream; the oldest make room for SPARE_MAX buffers
+  // and SPARE_TOTAL_BYTES
   if (p.buf && p.st && p.h_pinned && p.h_rows && p.h_argmax && p.bytes <= SPARE_MAX_BYTES && session_reuse_enabled() &&
       cudaStreamQuery(p.st) == cudaSuccess) {
-    spb_model::Spare old{};
+    std::vector<spb_model::Spare> old;
     {
       std::lock_guard<std::mutex> lk(m->spare_mu);
-      if (m->spares.size() >= SPARE_MAX) {
-        old = m->spares.front();
+      m->spares.push_back(p);
+      size_t total = 0;
+      for (const auto &q : m->spares) total += q.bytes;
+      while (m->spares.size() > 1 && (m->spares.size() > SPARE_MAX || total > SPARE_TOTAL_BYTES)) {
+        total -= m->spares.front().bytes;
+        old.push_back(m->spares.front());
         m->spares.erase(m->spares.begin());
       }
-      m->spares.push_back(p);
     }
-    if (old.buf) spare_destroy(old);
+    for (const auto &q : old) spare_destroy(q);
     return;
   }
   spare_destroy(p);
