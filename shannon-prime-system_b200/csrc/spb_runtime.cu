@@ -1200,11 +1200,25 @@ extern "C" int spb_session_rewind(spb_session *s, int n) {
 // position with the same history and cache. Paged: the clone takes the same pages (O(pages) on
 // the host, no K/V copied; a page is copied later only where one of the two writes into it).
 // Unpaged: a deep copy of the cache on the device.
+static int clone_state(const spb_session *s, spb_session *c);
+
 extern "C" int spb_session_clone(const spb_session *s, spb_session **out) {
   if (!s || !out) return set_err(SPB_EBADARG, "spb_session_clone: null arg");
-  int rc = session_open(s->m, s->pmax, s->pool, out, s->flags);
+  *out = nullptr;
+  spb_session *c = nullptr;
+  int rc = session_open(s->m, s->pmax, s->pool, &c, s->flags);
   if (rc) return rc;
-  spb_session *c = *out;
+  rc = clone_state(s, c);
+  if (rc) {   // no half-made clone is handed out (its pages, if it took any, go back)
+    spb_session_close(c);
+    return rc;
+  }
+  *out = c;
+  return SPB_OK;
+}
+
+// the cache (or the page references), history and position of s into the new session c
+static int clone_state(const spb_session *s, spb_session *c) {
   CU(cudaStreamSynchronize(s->st));
   if (s->pool) {
     {
@@ -1222,7 +1236,7 @@ extern "C" int spb_session_clone(const spb_session *s, spb_session **out) {
   }
   CU(cudaMemcpyAsync(c->hist_dev, s->hist_dev, (size_t)s->pmax * 4, cudaMemcpyDeviceToDevice, c->st));
   c->pos = s->pos;
-  rc = sync_pos(c);
+  const int rc = sync_pos(c);
   if (rc) return rc;
   CU(cudaStreamSynchronize(c->st));
   return SPB_OK;
