@@ -67,3 +67,20 @@ def test_reference_arm_line():
     for k in ("reference", "xref"):
         c1 = line["config1_unscaled"][k]
         assert c1["decode_tokens_per_s"] > 0 and c1["cores"] == 1 and c1["scaled"] is False
+
+
+def _gpu_usable():
+    try:
+        import torch
+        return torch.cuda.is_available()
+    except Exception:
+        return False
+
+
+@pytest.mark.skipif(_gpu_usable(), reason="checks the behaviour without a GPU")
+def test_gpu_arm_fails_loudly_without_a_gpu():
+    """No CPU fallback: without a GPU the device arm exits nonzero and prints no bench line."""
+    r = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--steps", "1", "--warmup", "1"],
+                       capture_output=True, text=True, timeout=300)
+    assert r.returncode != 0
+    assert r.stdout.strip() == ""
