@@ -86,7 +86,7 @@ int     spb_model_upload(const spb_model_desc *desc, int device, spb_model **out
 /* Same geometry filled on the device by the counter-based generator of the test
  * fixtures (seeded; identical bytes to the host generator). */
 int     spb_model_synthetic(const spb_config *cfg, uint64_t seed, int device, spb_model **out);
-void    spb_model_free(spb_model *m);
+void    spb_model_free(spb_model *m);   /* also frees the closed sessions' kept buffers */
 int64_t spb_model_weight_bytes(const spb_model *m);   /* OK_Q4B bytes streamed per token */
 
 /* ---- resident KV session (the section-6b verbs, sp_l1.h:386-410) ------------ */
@@ -136,6 +136,9 @@ void spb_kvpool_free(spb_kvpool *p);
 int  spb_kvpool_free_pages(spb_kvpool *p);                 /* pages not held by any session */
 /* spb_session_open with the K/V rows in pool pages (same verbs and bytes as an unpaged session) */
 int  spb_session_open_paged(spb_kvpool *p, int pmax, spb_session **out);
+/* Ends a session. Its device buffer (at most 1 GiB), stream and pinned staging stay with the model
+ * for the next open of the same size (at most 16 buffers and 4 GiB per model, oldest dropped
+ * first); spb_model_free releases them. Environment SPB_SESSION_REUSE=0 frees them at once. */
 void spb_session_close(spb_session *s);
 /* readback of one cached K (which=0) or V (which=1) row: [n_head_kv*head_dim] int32
  * (SPB_EUNSUPPORTED for a Spinor session) */
